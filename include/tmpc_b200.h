@@ -1,0 +1,188 @@
+/*
+ * tmpc_b200.h - C ABI of the B200-native batched SQP+ADMM inner solve.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, sizes and a
+ * CUDA stream (passed as `void*`, i.e. a `cudaStream_t`), enqueues its work on
+ * that stream and returns an int status:
+ *      0              success
+ *     <0              argument error (nothing was launched)
+ *     >0              CUDA error code from the launch
+ * No exception crosses the ABI, nothing is allocated behind the caller's back
+ * (scratch space is a caller-owned workspace whose size a *_workspace_bytes
+ * query reports), and no entry point keeps global state, so calls on
+ * different streams are independent.
+ *
+ * Batched arrays are problem-major and contiguous, exactly the layout the
+ * reference's XLA FFI handlers receive after `vmap_method="broadcast_all"`
+ * (turbompc/solvers/admm/admm_ffi_backend.py:358-362):
+ *     D       [Nb, T, n, n]      E        [Nb, N, n, n]     q  [Nb, T, n]
+ *     A0      [Nb, n0, n]        A_minus  [Nb, N, nx, n]    A_plus [Nb, N, nx, n]
+ *     c0      [Nb, n0]           c        [Nb, N, nx]
+ *     G       [Nb, T, m, n]      l, u     [Nb, T, m]
+ *     S, Phiinv (reference layout) [Nb, T, n, 3n]
+ * with T = N + 1 and n = nx + nu.
+ */
+#ifndef TMPC_B200_H_
+#define TMPC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMPC_OK 0
+#define TMPC_ERR_NULL_ARG (-1)
+#define TMPC_ERR_BAD_DIMS (-2)
+#define TMPC_ERR_UNSUPPORTED (-3)
+#define TMPC_ERR_WORKSPACE (-4)
+#define TMPC_ERR_SMEM (-5)
+
+/* Per-problem status bits written by solves (status_out[b]). */
+#define TMPC_STATUS_SINGULAR_BLOCK 1 /* a Theta_t / Cholesky / LU pivot was zero or not finite */
+#define TMPC_STATUS_NONFINITE 2      /* a non-finite value reached the output */
+
+typedef void* tmpc_stream_t; /* a cudaStream_t */
+
+typedef struct TmpcDims {
+  int32_t Nb; /* batch size (independent problems) */
+  int32_t T;  /* stages, N + 1 */
+  int32_t n;  /* nx + nu */
+  int32_t nx; /* states */
+  int32_t n0; /* rows of A0 (nx, or nx + nu with a fixed initial control) */
+  int32_t m;  /* inequality rows per stage (may be 0) */
+} TmpcDims;
+
+/* Stage-blocked QP (turbompc/solvers/qp_data.py:13-97). Device pointers of the
+ * function's precision.  G, l, u may be NULL when m == 0. */
+typedef struct TmpcQP {
+  const void* D;
+  const void* E;
+  const void* q;
+  const void* A0;
+  const void* A_minus;
+  const void* A_plus;
+  const void* c0;
+  const void* c;
+  const void* G;
+  const void* l;
+  const void* u;
+} TmpcQP;
+
+/* ADMMState (turbompc/solvers/admm/admm.py:27-34), batched. */
+typedef struct TmpcAdmmState {
+  void* x;       /* [Nb, T, n] */
+  void* y_g;     /* [Nb, T, m] */
+  void* y_f0;    /* [Nb, n0]   */
+  void* y_fdyn;  /* [Nb, N, nx] */
+  void* z_g;     /* [Nb, T, m] */
+  void* xi_g;    /* [Nb, T, m] */
+  void* rho_bar; /* [Nb]       */
+} TmpcAdmmState;
+
+#define TMPC_LINSYS_PCG 0    /* preconditioned CG on the Schur system (admm_fused_pcg) */
+#define TMPC_LINSYS_DIRECT 1 /* block-tridiagonal Cholesky (replaces admm_fused_cudss) */
+
+/* Mirrors ADMMConfig (turbompc/solvers/admm/csrc/admm_fused.cuh:6-22). */
+typedef struct TmpcAdmmConfig {
+  int32_t max_iter;
+  int32_t pcg_max_iter;
+  int32_t check_every;     /* <= 0 disables residual checks */
+  int32_t adapt_rho_every; /* <= 0 disables rho adaptation */
+  double eps_abs;
+  double eps_rel;
+  double sigma;
+  double rho_f_factor;
+  double alpha;
+  double pcg_eps;
+  double adaptive_rho_tolerance;
+  double rho_min;
+  double rho_max;
+  int32_t use_slack;
+  int32_t linsys; /* TMPC_LINSYS_* */
+} TmpcAdmmConfig;
+
+/* Library version (major*10000 + minor*100 + patch) and error strings. */
+int32_t tmpc_version(void);
+const char* tmpc_error_string(int32_t code);
+
+/* ---------------------------------------------------------------------------
+ * Schur complement + preconditioner assembly.
+ * Replaces compute_S_Phiinv (turbompc/solvers/admm/admm.py:71-154): writes the
+ * reference-layout S and Phiinv [Nb, T, n, 3n] for rho_f = rho_bar[b] *
+ * rho_f_factor and rho_ineq = rho_bar[b].
+ * ------------------------------------------------------------------------- */
+int32_t tmpc_schur_assemble_f32(const TmpcDims* dims, const TmpcQP* qp, const float* rho_bar,
+                                double sigma, double rho_f_factor, float* S, float* Phiinv,
+                                int32_t* status_out, tmpc_stream_t stream);
+int32_t tmpc_schur_assemble_f64(const TmpcDims* dims, const TmpcQP* qp, const double* rho_bar,
+                                double sigma, double rho_f_factor, double* S, double* Phiinv,
+                                int32_t* status_out, tmpc_stream_t stream);
+
+/* Packed operator format: per problem the unique blocks of S and Phiinv
+ * (upper triangle of each diagonal block, the full sub-diagonal blocks),
+ * zero-padded to the kernel block size.  Bytes for the whole batch: */
+size_t tmpc_packed_operator_bytes(const TmpcDims* dims, int32_t dtype_bytes);
+int32_t tmpc_schur_assemble_packed_f32(const TmpcDims* dims, const TmpcQP* qp, const float* rho_bar,
+                                       double sigma, double rho_f_factor, void* ops,
+                                       int32_t* status_out, tmpc_stream_t stream);
+int32_t tmpc_schur_assemble_packed_f64(const TmpcDims* dims, const TmpcQP* qp, const double* rho_bar,
+                                       double sigma, double rho_f_factor, void* ops,
+                                       int32_t* status_out, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Batched block-tridiagonal PCG.
+ * Replaces the `pcg_blktridi_cuda[_f64]` FFI target
+ * (turbompc/solvers/linear_systems_solvers/csrc/pcg_ffi.cc:115-147;
+ * LaunchPcgBlkTridiF32/F64 pcg_blktridi.cuh:7-32): solves S x = rhs from x0
+ * with the preconditioner Phiinv, stopping when |eta| < 1e-12 + eps*|eta_0|
+ * or after max_iters iterations; iters_out[b] is the iteration count.
+ * Any T*n is accepted (no size cliff, no host synchronisation).
+ * ------------------------------------------------------------------------- */
+int32_t tmpc_pcg_solve_f32(const TmpcDims* dims, const float* S, const float* Phiinv,
+                           const float* rhs, const float* x0, float* x_out, uint32_t* iters_out,
+                           double eps, int32_t max_iters, tmpc_stream_t stream);
+int32_t tmpc_pcg_solve_f64(const TmpcDims* dims, const double* S, const double* Phiinv,
+                           const double* rhs, const double* x0, double* x_out, uint32_t* iters_out,
+                           double eps, int32_t max_iters, tmpc_stream_t stream);
+/* Same solve on operators in the packed format written by
+ * tmpc_schur_assemble_packed_*. */
+int32_t tmpc_pcg_solve_packed_f32(const TmpcDims* dims, const void* ops, const float* rhs,
+                                  const float* x0, float* x_out, uint32_t* iters_out, double eps,
+                                  int32_t max_iters, tmpc_stream_t stream);
+int32_t tmpc_pcg_solve_packed_f64(const TmpcDims* dims, const void* ops, const double* rhs,
+                                  const double* x0, double* x_out, uint32_t* iters_out, double eps,
+                                  int32_t max_iters, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused ADMM solve (Schur assembly + ADMM iteration + linear solve in one
+ * kernel, one CTA per problem).
+ * Replaces the `admm_fused_cuda[_f64]` FFI target
+ * (turbompc/solvers/admm/csrc/admm_ffi.cc:150-274; LaunchADMMFusedF32/F64,
+ * admm_fused.cuh:25-124) and, with cfg->linsys == TMPC_LINSYS_DIRECT, the
+ * cuDSS loop `admm_cudss_cuda[_f64]` (admm/csrc/admm_cudss_ffi.cc:142-256).
+ * S / Phiinv are built on the device from the QP (no host-side
+ * compute_S_Phiinv), so the reference's S, Phiinv, S_work and Phiinv_work
+ * buffers have no counterpart.  state_out may alias state_in.
+ * slack_weight [Nb] may be NULL (all zero).  x_out [Nb, T, n] may be NULL.
+ * The workspace is needed only when the per-problem operators do not fit in
+ * shared memory; query its size with tmpc_admm_workspace_bytes.
+ * ------------------------------------------------------------------------- */
+size_t tmpc_admm_workspace_bytes(const TmpcDims* dims, int32_t dtype_bytes, const TmpcAdmmConfig* cfg);
+int32_t tmpc_admm_solve_f32(const TmpcDims* dims, const TmpcQP* qp, const TmpcAdmmState* state_in,
+                            const TmpcAdmmState* state_out, const float* slack_weight,
+                            const TmpcAdmmConfig* cfg, float* x_out, uint32_t* iters_out,
+                            int32_t* status_out, void* workspace, size_t workspace_bytes,
+                            tmpc_stream_t stream);
+int32_t tmpc_admm_solve_f64(const TmpcDims* dims, const TmpcQP* qp, const TmpcAdmmState* state_in,
+                            const TmpcAdmmState* state_out, const double* slack_weight,
+                            const TmpcAdmmConfig* cfg, double* x_out, uint32_t* iters_out,
+                            int32_t* status_out, void* workspace, size_t workspace_bytes,
+                            tmpc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TMPC_B200_H_ */

@@ -1,0 +1,41 @@
+// Library-level C ABI entry points (version, error strings) and host helpers.
+#include <cuda_runtime.h>
+
+#include "tmpc_common.cuh"
+
+namespace tmpc {
+
+int check_dims(const TmpcDims* d) {
+  if (!d) return TMPC_ERR_NULL_ARG;
+  if (d->Nb < 0 || d->T < 2 || d->n < 1 || d->nx < 1 || d->nx > d->n || d->n0 < 0 || d->m < 0)
+    return TMPC_ERR_BAD_DIMS;
+  return TMPC_OK;
+}
+
+int max_dyn_smem() {
+  int dev = 0, v = 48 * 1024;
+  if (cudaGetDevice(&dev) != cudaSuccess) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 48 * 1024;
+  return v;
+}
+
+}  // namespace tmpc
+
+extern "C" {
+
+int32_t tmpc_version(void) { return 100; }
+
+const char* tmpc_error_string(int32_t code) {
+  switch (code) {
+    case TMPC_OK: return "ok";
+    case TMPC_ERR_NULL_ARG: return "null pointer argument";
+    case TMPC_ERR_BAD_DIMS: return "invalid dimensions";
+    case TMPC_ERR_UNSUPPORTED: return "unsupported configuration (block size n > 32 or unknown option)";
+    case TMPC_ERR_WORKSPACE: return "workspace missing or too small";
+    case TMPC_ERR_SMEM: return "problem does not fit the shared-memory budget of one CTA";
+  }
+  if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+  return "unknown error";
+}
+
+}  // extern "C"
