@@ -1,438 +1,8 @@
-// Fused ADMM solve: Schur/preconditioner assembly + the whole ADMM loop with
-// the PCG linear solve, one CTA per problem, operators resident in shared
-// memory when they fit (else in a caller workspace in HBM).
-//
-// Per ADMM iteration (order of turbompc/solvers/admm/csrc/admm_fused.cu:701-925):
-//   gamma = sigma x - q + C^T(rho_f c - y_f) + G^T(rho z_g - y_g)   (admm.py:157-174)
-//   x_old = x ; x = PCG(S, Phiinv, gamma, x)
-//   Cx0, Cx, Gx on the pre-relaxation x                             (admm.py:884-887)
-//   x = alpha x + (1 - alpha) x_old
-//   z~ = alpha Gx + (1 - alpha) z_old + y_g / rho ; z = clamp(z~, l, u)  (+ slack form)
-//   y_f0 += rho_f alpha (Cx0 - c0) ; y_fdyn += rho_f alpha (Cx - c)
-//   y_g  += rho (alpha Gx + (1 - alpha) z_old - z)
-//   every check_every: residuals, convergence, OSQP rho adaptation with an
-//   on-chip rebuild of S and Phiinv.
-#include "assemble.cuh"
-#include "pcg_core.cuh"
-#include "tmpc_common.cuh"
+// Fused ADMM: size queries, argument checks and dispatch to the per-block-size
+// kernels (instantiated in inst_nb*.cu).
+#include "launchers.cuh"
 
 namespace tmpc {
-
-template <typename R>
-struct AdmmParams {
-  TmpcQP qp;
-  TmpcAdmmState in, out;
-  const R* slack_weight;
-  R* x_out;
-  uint32_t* iters_out;
-  int32_t* status_out;
-  R* ws;  // operators in HBM when they do not fit on chip
-  int T, n, nx, n0, m, Nb;
-  int max_iter, pcg_max_iter, check_every, adapt_every, use_slack;
-  R eps_abs, eps_rel, sigma, rho_f_factor, alpha, pcg_eps, adapt_tol, rho_min, rho_max;
-};
-
-// Element offsets inside the dynamic shared-memory arena.
-template <int NB, typename R>
-struct AdmmSmem {
-  size_t opS, opP, vec0, yf0, yfd, zg, yg, xig, cx0, cx, gx, ct, gt, red, nelem;
-  __host__ __device__ AdmmSmem(int T, int nx, int n0, int m, bool ops_smem) {
-    using Gm = Geo<NB, R>;
-    const int N = T - 1;
-    auto a4 = [](size_t v) { return (v + 3) & ~size_t(3); };  // 16-byte alignment for both precisions
-    size_t o = 0;
-    const size_t opn = Gm::op_elems(T);
-    opS = o;
-    if (ops_smem) o += opn;
-    opP = o;
-    if (ops_smem) o += opn;
-    vec0 = o;
-    o += 10 * (size_t)T * Gm::VSTR;  // x r z p d lo up0 up1 gam xold
-    yf0 = a4(o); o = yf0 + n0;
-    yfd = a4(o); o = yfd + (size_t)N * nx;
-    zg = a4(o); o = zg + (size_t)T * m;
-    yg = a4(o); o = yg + (size_t)T * m;
-    xig = a4(o); o = xig + (size_t)T * m;
-    cx0 = a4(o); o = cx0 + n0;
-    cx = a4(o); o = cx + (size_t)N * nx;
-    gx = a4(o); o = gx + (size_t)T * m;
-    ct = a4(o); o = ct + n0 + (size_t)N * nx;
-    gt = a4(o); o = gt + (size_t)T * m;
-    red = a4(o); o = red + 64 + 16;
-    nelem = a4(o);
-  }
-};
-
-// gamma_t[j] (padded to NB) from the on-chip duals; ct = rho_f c - y_f, gt = rho z - y_g.
-template <int NB, typename R>
-__device__ void compute_gamma(R* gam, const R* x, const QPView<R>& qp, const R* ct, const R* gt, R sigma, int T,
-                              int n, int nx, int n0, int m) {
-  using Gm = Geo<NB, R>;
-  const int N = T - 1;
-  TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) {
-    const int t = e / NB, j = e - t * NB;
-    R val = R(0);
-    if (j < n) {
-      val = sigma * x[o] - qp.q[t * n + j];
-      R eq = R(0);
-      if (t == 0) {
-        for (int k = 0; k < n0; ++k) eq += qp.A0[k * n + j] * ct[k];
-        if (N > 0)
-          for (int k = 0; k < nx; ++k) eq += qp.Am[k * n + j] * ct[n0 + k];
-      } else {
-        const R* ap = qp.Ap + (size_t)(t - 1) * nx * n;
-        for (int k = 0; k < nx; ++k) eq += ap[k * n + j] * ct[n0 + (t - 1) * nx + k];
-        if (t < N) {
-          const R* am = qp.Am + (size_t)t * nx * n;
-          for (int k = 0; k < nx; ++k) eq += am[k * n + j] * ct[n0 + t * nx + k];
-        }
-      }
-      val += eq;
-      R iq = R(0);
-      for (int k = 0; k < m; ++k) iq += qp.G[((size_t)t * m + k) * n + j] * gt[t * m + k];
-      val += iq;
-    }
-    gam[o] = val;
-  }
-}
-
-// Cx0 = A0 x_0, Cx_t = Am_t x_t + Ap_t x_{t+1}, Gx_t = G_t x_t.
-template <int NB, typename R>
-__device__ void apply_constraints(R* cx0, R* cx, R* gx, const R* x, const QPView<R>& qp, int T, int n, int nx,
-                                  int n0, int m) {
-  using Gm = Geo<NB, R>;
-  const int N = T - 1;
-  const int tot = n0 + N * nx + T * m;
-  for (int e = threadIdx.x; e < tot; e += blockDim.x) {
-    if (e < n0) {
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += qp.A0[e * n + j] * x[j];
-      cx0[e] = s;
-    } else if (e < n0 + N * nx) {
-      const int k = e - n0, t = k / nx, i = k - t * nx;
-      const R* am = qp.Am + ((size_t)t * nx + i) * n;
-      const R* ap = qp.Ap + ((size_t)t * nx + i) * n;
-      const R* xt = x + t * Gm::VSTR;
-      const R* xt1 = x + (t + 1) * Gm::VSTR;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += am[j] * xt[j] + ap[j] * xt1[j];
-      cx[k] = s;
-    } else {
-      const int k = e - n0 - N * nx, t = k / m, i = k - t * m;
-      const R* g = qp.G + ((size_t)t * m + i) * n;
-      const R* xt = x + t * Gm::VSTR;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += g[j] * xt[j];
-      gx[k] = s;
-    }
-  }
-}
-
-// Residuals of admm.py:266-331 (primal, dual, normalised), written to sc[0..5].
-template <int NB, typename R>
-__device__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const R* yg, const R* xig, const R* yf0,
-                                  const R* yfd, const QPView<R>& qp, R slack_w, bool use_slack, int T, int n, int nx,
-                                  int n0, int m) {
-  using Gm = Geo<NB, R>;
-  const int N = T - 1;
-  R pr = R(0), ncx = R(0), nc = R(0), ngx = R(0), nz = R(0);
-  const int tot = n0 + N * nx + T * m;
-  for (int e = threadIdx.x; e < tot; e += blockDim.x) {
-    if (e < n0) {
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += qp.A0[e * n + j] * x[j];
-      pr = fmax(pr, fabs(s - qp.c0[e]));
-      ncx = fmax(ncx, fabs(s));
-      nc = fmax(nc, fabs(qp.c0[e]));
-    } else if (e < n0 + N * nx) {
-      const int k = e - n0, t = k / nx, i = k - t * nx;
-      const R* am = qp.Am + ((size_t)t * nx + i) * n;
-      const R* ap = qp.Ap + ((size_t)t * nx + i) * n;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += am[j] * x[t * Gm::VSTR + j] + ap[j] * x[(t + 1) * Gm::VSTR + j];
-      pr = fmax(pr, fabs(s - qp.c[k]));
-      ncx = fmax(ncx, fabs(s));
-      nc = fmax(nc, fabs(qp.c[k]));
-    } else {
-      const int k = e - n0 - N * nx, t = k / m, i = k - t * m;
-      const R* g = qp.G + ((size_t)t * m + i) * n;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += g[j] * x[t * Gm::VSTR + j];
-      pr = fmax(pr, fabs(s - zg[k]));
-      ngx = fmax(ngx, fabs(s));
-      nz = fmax(nz, fabs(zg[k]));
-    }
-  }
-  R du = R(0), npx = R(0), naty = R(0), nq = R(0);
-  for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
-    const int t = e / n, j = e - t * n;
-    R px = R(0);
-    const R* Dt = qp.D + (size_t)t * n * n;
-    for (int k = 0; k < n; ++k) px += Dt[j * n + k] * x[t * Gm::VSTR + k];
-    if (t > 0) {
-      const R* Et = qp.E + (size_t)(t - 1) * n * n;
-      for (int k = 0; k < n; ++k) px += Et[j * n + k] * x[(t - 1) * Gm::VSTR + k];
-    }
-    if (t < N) {
-      const R* Et = qp.E + (size_t)t * n * n;
-      for (int k = 0; k < n; ++k) px += Et[k * n + j] * x[(t + 1) * Gm::VSTR + k];
-    }
-    R cty = R(0);
-    if (t == 0) {
-      for (int k = 0; k < n0; ++k) cty += qp.A0[k * n + j] * yf0[k];
-      if (N > 0)
-        for (int k = 0; k < nx; ++k) cty += qp.Am[k * n + j] * yfd[k];
-    } else {
-      const R* ap = qp.Ap + (size_t)(t - 1) * nx * n;
-      for (int k = 0; k < nx; ++k) cty += ap[k * n + j] * yfd[(t - 1) * nx + k];
-      if (t < N) {
-        const R* am = qp.Am + (size_t)t * nx * n;
-        for (int k = 0; k < nx; ++k) cty += am[k * n + j] * yfd[t * nx + k];
-      }
-    }
-    for (int k = 0; k < m; ++k) cty += qp.G[((size_t)t * m + k) * n + j] * yg[t * m + k];
-    const R qq = qp.q[t * n + j];
-    du = fmax(du, fabs(px + qq + cty));
-    npx = fmax(npx, fabs(px));
-    naty = fmax(naty, fabs(cty));
-    nq = fmax(nq, fabs(qq));
-  }
-  R nxi = R(0), nyg = R(0);
-  if (use_slack && m > 0) {
-    for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
-      du = fmax(du, fabs(slack_w * xig[e] + yg[e]));
-      nxi = fmax(nxi, fabs(xig[e]));
-      nyg = fmax(nyg, fabs(yg[e]));
-    }
-  }
-  R vals[11] = {pr, ncx, nc, ngx, nz, du, npx, naty, nq, nxi, nyg};
-  R outv[11];
-#pragma unroll
-  for (int k = 0; k < 11; ++k) {
-    outv[k] = block_max(vals[k], red + (k & 1) * 32);
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    const R prim = outv[0];
-    const R pterm = fmax(fmax(outv[1], outv[3]), fmax(outv[2], outv[4]));
-    const R dual = outv[5];
-    R dterm = fmax(fmax(outv[6], outv[7]), outv[8]);
-    if (use_slack && m > 0) dterm = fmax(dterm, fmax(slack_w * outv[9], outv[10]));
-    sc[0] = prim;
-    sc[1] = dual;
-    sc[2] = prim / (R(1e-10) + pterm);
-    sc[3] = dual / (R(1e-10) + dterm);
-    sc[4] = pterm;
-    sc[5] = dterm;
-  }
-  __syncthreads();
-}
-
-template <int NB, typename R, bool OPS_SMEM>
-__global__ void __launch_bounds__(kMaxThreads) admm_fused_kernel(const AdmmParams<R> P) {
-  using Gm = Geo<NB, R>;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  R* sm = reinterpret_cast<R*>(smem_raw);
-  const int b = blockIdx.x;
-  if (b >= P.Nb) return;
-  const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
-  const AdmmSmem<NB, R> L(T, nx, n0, m, OPS_SMEM);
-  const size_t opn = Gm::op_elems(T);
-  R* opS = OPS_SMEM ? sm + L.opS : P.ws + (size_t)b * 2 * opn;
-  R* opP = OPS_SMEM ? sm + L.opP : P.ws + (size_t)b * 2 * opn + opn;
-  const size_t VS = (size_t)T * Gm::VSTR;
-  R* vbase = sm + L.vec0;
-  BlockVecs<NB, R> w{vbase,          vbase + VS,     vbase + 2 * VS, vbase + 3 * VS,
-                     vbase + 4 * VS, vbase + 5 * VS, vbase + 6 * VS, vbase + 7 * VS};
-  R* gam = vbase + 8 * VS;
-  R* xold = vbase + 9 * VS;
-  R* yf0 = sm + L.yf0;
-  R* yfd = sm + L.yfd;
-  R* zg = sm + L.zg;
-  R* yg = sm + L.yg;
-  R* xig = sm + L.xig;
-  R* cx0 = sm + L.cx0;
-  R* cx = sm + L.cx;
-  R* gx = sm + L.gx;
-  R* ct = sm + L.ct;
-  R* gt = sm + L.gt;
-  R* red = sm + L.red;
-  R* sc = red + 64;
-  __shared__ int flag;
-  if (threadIdx.x == 0) flag = 0;
-
-  const QPView<R> qp = qp_view<R>(P.qp, b, T, n, nx, n0, m);
-
-  // ---- load the warm-start state; zero all block vectors (keeps padding 0)
-  for (size_t e = threadIdx.x; e < 10 * VS; e += blockDim.x) vbase[e] = R(0);
-  __syncthreads();
-  {
-    const R* x_in = static_cast<const R*>(P.in.x) + (size_t)b * T * n;
-    for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
-      const int t = e / n, j = e - t * n;
-      w.x[t * Gm::VSTR + j] = x_in[e];
-    }
-    if (n0 > 0) {
-      const R* a = static_cast<const R*>(P.in.y_f0) + (size_t)b * n0;
-      for (int e = threadIdx.x; e < n0; e += blockDim.x) yf0[e] = a[e];
-    }
-    const R* a = static_cast<const R*>(P.in.y_fdyn) + (size_t)b * N * nx;
-    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) yfd[e] = a[e];
-    if (m > 0) {
-      const R* z = static_cast<const R*>(P.in.z_g) + (size_t)b * T * m;
-      const R* y = static_cast<const R*>(P.in.y_g) + (size_t)b * T * m;
-      const R* xi = static_cast<const R*>(P.in.xi_g) + (size_t)b * T * m;
-      for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
-        zg[e] = z[e];
-        yg[e] = y[e];
-        xig[e] = xi[e];
-      }
-    }
-  }
-  R rho = static_cast<const R*>(P.in.rho_bar)[b];
-  const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
-  const R al = P.alpha;
-  const PackedAcc<NB, R> acc{opS, opP, T};
-
-  assemble_ops<NB>(acc, qp, rho * P.rho_f_factor, rho, P.sigma, T, n, nx, n0, m, &flag);
-
-  uint32_t iters = (uint32_t)P.max_iter;
-  for (int it = 0; it < P.max_iter; ++it) {
-    const R rho_f = rho * P.rho_f_factor;
-    for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
-      if (e < n0) ct[e] = rho_f * qp.c0[e] - yf0[e];
-      else if (e < n0 + N * nx) ct[e] = rho_f * qp.c[e - n0] - yfd[e - n0];
-      else gt[e - n0 - N * nx] = rho * zg[e - n0 - N * nx] - yg[e - n0 - N * nx];
-    }
-    __syncthreads();
-    compute_gamma<NB>(gam, w.x, qp, ct, gt, P.sigma, T, n, nx, n0, m);
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { xold[o] = w.x[o]; }
-    __syncthreads();
-    pcg_solve<NB, OPS_SMEM>(opS, opP, T, gam, w, red, P.pcg_max_iter, P.pcg_eps);
-    apply_constraints<NB>(cx0, cx, gx, w.x, qp, T, n, nx, n0, m);
-    __syncthreads();
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { w.x[o] = al * w.x[o] + (R(1) - al) * xold[o]; }
-    for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
-      if (e < n0) {
-        yf0[e] += rho_f * al * (cx0[e] - qp.c0[e]);
-      } else if (e < n0 + N * nx) {
-        const int k = e - n0;
-        yfd[k] += rho_f * al * (cx[k] - qp.c[k]);
-      } else {
-        const int k = e - n0 - N * nx;
-        const R zold = zg[k];
-        const R zt = al * gx[k] + (R(1) - al) * zold + yg[k] / rho;
-        R cl = zt;
-        const R lb = qp.l[k], ub = qp.u[k];
-        if (cl < lb) cl = lb;
-        if (cl > ub) cl = ub;
-        R znew;
-        if (P.use_slack) {
-          const R f = sw / (sw + rho);
-          znew = (R(1) - f) * zt + f * cl;
-          xig[k] = (rho / (sw + rho)) * (cl - zt);
-        } else {
-          znew = cl;
-        }
-        zg[k] = znew;
-        yg[k] += rho * (al * gx[k] + (R(1) - al) * zold - znew);
-      }
-    }
-    __syncthreads();
-    if (P.check_every > 0 && (it % P.check_every) == 0) {
-      compute_residuals<NB>(sc, red, w.x, zg, yg, xig, yf0, yfd, qp, sw, P.use_slack != 0, T, n, nx, n0, m);
-      const bool conv = (sc[0] < P.eps_abs + P.eps_rel * sc[4]) && (sc[1] < P.eps_abs + P.eps_rel * sc[5]);
-      if (conv) {
-        iters = (uint32_t)(it + 1);
-        break;
-      }
-      if (P.adapt_every > 0 && it >= 2 && (it % P.adapt_every) == 0) {
-        R cand = rho * sqrt(sc[2] / (sc[3] + R(1e-30)));
-        if (cand < P.rho_min) cand = P.rho_min;
-        if (cand > P.rho_max) cand = P.rho_max;
-        R ratio = cand / rho;
-        if (ratio < R(1)) ratio = R(1) / ratio;
-        if (ratio >= P.adapt_tol) {
-          rho = cand;
-          assemble_ops<NB>(acc, qp, rho * P.rho_f_factor, rho, P.sigma, T, n, nx, n0, m, &flag);
-        }
-      }
-      __syncthreads();
-    }
-  }
-
-  // ---- store
-  bool nonfinite = false;
-  {
-    R* xo = static_cast<R*>(P.out.x) + (size_t)b * T * n;
-    R* xo2 = P.x_out ? P.x_out + (size_t)b * T * n : nullptr;
-    for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
-      const int t = e / n, j = e - t * n;
-      const R v = w.x[t * Gm::VSTR + j];
-      if (!isfinite(v)) nonfinite = true;
-      xo[e] = v;
-      if (xo2) xo2[e] = v;
-    }
-    if (n0 > 0) {
-      R* a = static_cast<R*>(P.out.y_f0) + (size_t)b * n0;
-      for (int e = threadIdx.x; e < n0; e += blockDim.x) a[e] = yf0[e];
-    }
-    R* a = static_cast<R*>(P.out.y_fdyn) + (size_t)b * N * nx;
-    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) a[e] = yfd[e];
-    if (m > 0) {
-      R* z = static_cast<R*>(P.out.z_g) + (size_t)b * T * m;
-      R* y = static_cast<R*>(P.out.y_g) + (size_t)b * T * m;
-      R* xi = static_cast<R*>(P.out.xi_g) + (size_t)b * T * m;
-      for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
-        z[e] = zg[e];
-        y[e] = yg[e];
-        xi[e] = xig[e];
-      }
-    }
-  }
-  if (nonfinite) atomicOr(&flag, TMPC_STATUS_NONFINITE);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    static_cast<R*>(P.out.rho_bar)[b] = rho;
-    if (P.iters_out) P.iters_out[b] = iters;
-    if (P.status_out) P.status_out[b] = flag;
-  }
-}
-
-inline int cta_threads(int T) {
-  int th = ((T + 2 * (T - 1)) + 31) / 32 * 32;
-  if (th < 64) th = 64;
-  if (th > kMaxThreads) th = kMaxThreads;
-  return th;
-}
-
-template <int NB, typename R>
-size_t admm_smem_bytes(int T, int nx, int n0, int m, bool ops_smem) {
-  return AdmmSmem<NB, R>(T, nx, n0, m, ops_smem).nelem * sizeof(R);
-}
-
-template <int NB, typename R>
-int launch_admm_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st) {
-  const int th = cta_threads(P.T);
-  const int smax = max_dyn_smem();
-  const size_t s_res = admm_smem_bytes<NB, R>(P.T, P.nx, P.n0, P.m, true);
-  if ((long)s_res <= smax) {
-    auto k = admm_fused_kernel<NB, R, true>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s_res);
-    if (e != cudaSuccess) return (int)e;
-    k<<<P.Nb, th, s_res, st>>>(P);
-    return (int)cudaPeekAtLastError();
-  }
-  const size_t need = (size_t)P.Nb * 2 * Geo<NB, R>::op_elems(P.T) * sizeof(R);
-  if (P.ws == nullptr || ws_bytes < need) return TMPC_ERR_WORKSPACE;
-  const size_t s_str = admm_smem_bytes<NB, R>(P.T, P.nx, P.n0, P.m, false);
-  if ((long)s_str > smax) return TMPC_ERR_SMEM;
-  auto k = admm_fused_kernel<NB, R, false>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s_str);
-  if (e != cudaSuccess) return (int)e;
-  k<<<P.Nb, th, s_str, st>>>(P);
-  return (int)cudaPeekAtLastError();
-}
 
 template <typename R>
 size_t admm_ws_bytes(const TmpcDims& d) {

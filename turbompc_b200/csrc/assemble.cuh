@@ -260,7 +260,7 @@ __device__ void assemble_precond_offdiag(const Acc& acc, int T) {
 
 // Full assembly; all threads of the CTA must call it.  Ends with a barrier.
 template <int NB, typename R, class Acc>
-__device__ void assemble_ops(const Acc& acc, const QPView<R>& qp, R rho_f, R rho_i, R sigma, int T, int n, int nx,
+__device__ __noinline__ void assemble_ops(const Acc& acc, const QPView<R>& qp, R rho_f, R rho_i, R sigma, int T, int n, int nx,
                              int n0, int m, int* flag) {
   acc.init();
   assemble_theta_phi<NB>(acc, qp, rho_f, rho_i, sigma, T, n, nx, n0, m);

@@ -1,45 +1,8 @@
 // Standalone Schur assembly (compute_S_Phiinv) and batched block-tridiagonal
 // PCG (pcg_blktridi_cuda) entry points.
-#include "assemble.cuh"
-#include "pcg_core.cuh"
-#include "tma.cuh"
-#include "tmpc_common.cuh"
+#include "launchers.cuh"
 
 namespace tmpc {
-
-template <int NB, typename R>
-__global__ void __launch_bounds__(256) assemble_packed_kernel(TmpcQP qpa, const R* rho, R sigma, R rho_f_factor,
-                                                              R* ops, int32_t* status, int Nb, int T, int n, int nx,
-                                                              int n0, int m) {
-  const int b = blockIdx.x;
-  if (b >= Nb) return;
-  __shared__ int flag;
-  if (threadIdx.x == 0) flag = 0;
-  __syncthreads();
-  const size_t opn = Geo<NB, R>::op_elems(T);
-  const PackedAcc<NB, R> acc{ops + (size_t)b * 2 * opn, ops + (size_t)b * 2 * opn + opn, T};
-  const QPView<R> qp = qp_view<R>(qpa, b, T, n, nx, n0, m);
-  const R r = rho[b];
-  assemble_ops<NB>(acc, qp, r * rho_f_factor, r, sigma, T, n, nx, n0, m, &flag);
-  if (threadIdx.x == 0 && status) status[b] = flag;
-}
-
-template <int NB, typename R>
-__global__ void __launch_bounds__(256) assemble_ref_kernel(TmpcQP qpa, const R* rho, R sigma, R rho_f_factor, R* S,
-                                                           R* P, int32_t* status, int Nb, int T, int n, int nx,
-                                                           int n0, int m) {
-  const int b = blockIdx.x;
-  if (b >= Nb) return;
-  __shared__ int flag;
-  if (threadIdx.x == 0) flag = 0;
-  __syncthreads();
-  const size_t per = (size_t)T * n * 3 * n;
-  const RefAcc<R> acc{S + (size_t)b * per, P + (size_t)b * per, T, n};
-  const QPView<R> qp = qp_view<R>(qpa, b, T, n, nx, n0, m);
-  const R r = rho[b];
-  assemble_ops<NB>(acc, qp, r * rho_f_factor, r, sigma, T, n, nx, n0, m, &flag);
-  if (threadIdx.x == 0 && status) status[b] = flag;
-}
 
 // ---------------------------------------------------------------------------
 // PCG on the reference layout: one CTA per problem, vectors in shared memory,
@@ -126,78 +89,6 @@ __global__ void __launch_bounds__(512) pcg_ref_kernel(const R* __restrict__ S, c
   if (threadIdx.x == 0) iters_out[b] = (uint32_t)it;
 }
 
-// ---------------------------------------------------------------------------
-// PCG on packed operators.  OPS_SMEM: the problem's operators are staged into
-// shared memory by TMA bulk copies, then all iterations run on chip;
-// otherwise they are streamed from HBM/L2 every iteration.
-// ---------------------------------------------------------------------------
-template <int NB, typename R, bool OPS_SMEM>
-__global__ void __launch_bounds__(kMaxThreads) pcg_packed_kernel(const R* __restrict__ ops,
-                                                                 const R* __restrict__ rhs,
-                                                                 const R* __restrict__ x0, R* x_out,
-                                                                 uint32_t* iters_out, R eps, int max_iter, int Nb,
-                                                                 int T, int n) {
-  using Gm = Geo<NB, R>;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  R* sm = reinterpret_cast<R*>(smem_raw);
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ int tma_ok;
-  const int b = blockIdx.x;
-  if (b >= Nb) return;
-  const size_t opn = Gm::op_elems(T);
-  const R* gS = ops + (size_t)b * 2 * opn;
-  const R* opS = gS;
-  const R* opP = gS + opn;
-  R* vb = sm;
-  if constexpr (OPS_SMEM) {
-    R* s_ops = sm;
-    vb = sm + 2 * opn;
-    if (threadIdx.x == 0) {
-      tma_ok = 1;
-      mbar_init(&bar, 1);
-      const uint32_t bytes = (uint32_t)(2 * opn * sizeof(R));
-      mbar_expect_tx(&bar, bytes);
-      for (uint32_t off = 0; off < bytes; off += 65536u) {
-        const uint32_t len = bytes - off < 65536u ? bytes - off : 65536u;
-        bulk_g2s(reinterpret_cast<unsigned char*>(s_ops) + off, reinterpret_cast<const unsigned char*>(gS) + off,
-                 len, &bar);
-      }
-    }
-    opS = s_ops;
-    opP = s_ops + opn;
-  }
-  const size_t VS = (size_t)T * Gm::VSTR;
-  BlockVecs<NB, R> w{vb, vb + VS, vb + 2 * VS, vb + 3 * VS, vb + 4 * VS, vb + 5 * VS, vb + 6 * VS, vb + 7 * VS};
-  R* g = vb + 8 * VS;
-  R* red = vb + 9 * VS;
-  for (size_t e = threadIdx.x; e < 9 * VS; e += blockDim.x) vb[e] = R(0);
-  __syncthreads();
-  const int tot = T * n;
-  for (int e = threadIdx.x; e < tot; e += blockDim.x) {
-    const int t = e / n, j = e - t * n;
-    w.x[t * Gm::VSTR + j] = x0[(size_t)b * tot + e];
-    g[t * Gm::VSTR + j] = rhs[(size_t)b * tot + e];
-  }
-  if constexpr (OPS_SMEM) {
-    if (threadIdx.x == 0) {
-      if (!mbar_wait_bounded(&bar, 0, 1u << 26)) tma_ok = 0;
-    }
-  }
-  __syncthreads();
-  if constexpr (OPS_SMEM) {
-    if (!tma_ok) {
-      if (threadIdx.x == 0) iters_out[b] = 0xffffffffu;  // transfer timed out
-      return;
-    }
-  }
-  const int it = pcg_solve<NB, OPS_SMEM>(opS, opP, T, g, w, red, max_iter, eps);
-  for (int e = threadIdx.x; e < tot; e += blockDim.x) {
-    const int t = e / n, j = e - t * n;
-    x_out[(size_t)b * tot + e] = w.x[t * Gm::VSTR + j];
-  }
-  if (threadIdx.x == 0) iters_out[b] = (uint32_t)it;
-}
-
 template <typename R>
 int schur_assemble(const TmpcDims* d, const TmpcQP* qp, const R* rho, double sigma, double rff, R* S, R* P,
                    int32_t* status, cudaStream_t st) {
@@ -209,9 +100,7 @@ int schur_assemble(const TmpcDims* d, const TmpcQP* qp, const R* rho, double sig
   if (d->Nb == 0) return TMPC_OK;
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    assemble_ref_kernel<NB, R><<<d->Nb, 256, 0, st>>>(*qp, rho, (R)sigma, (R)rff, S, P, status, d->Nb, d->T, d->n,
-                                                      d->nx, d->n0, d->m);
-    return (int)cudaPeekAtLastError();
+    return launch_assemble_ref<NB, R>(d, qp, rho, (R)sigma, (R)rff, S, P, status, st);
   });
 }
 
@@ -226,9 +115,7 @@ int schur_assemble_packed(const TmpcDims* d, const TmpcQP* qp, const R* rho, dou
   if (d->Nb == 0) return TMPC_OK;
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    assemble_packed_kernel<NB, R><<<d->Nb, 256, 0, st>>>(*qp, rho, (R)sigma, (R)rff, static_cast<R*>(ops), status,
-                                                         d->Nb, d->T, d->n, d->nx, d->n0, d->m);
-    return (int)cudaPeekAtLastError();
+    return launch_assemble_packed<NB, R>(d, qp, rho, (R)sigma, (R)rff, static_cast<R*>(ops), status, st);
   });
 }
 
@@ -258,30 +145,9 @@ int pcg_packed(const TmpcDims* d, const void* ops, const R* rhs, const R* x0, R*
   if (d->Nb < 0 || d->T < 2 || d->n < 1) return TMPC_ERR_BAD_DIMS;
   if (!ops || !rhs || !x0 || !xo || !it) return TMPC_ERR_NULL_ARG;
   if (d->Nb == 0) return TMPC_OK;
-  int th = ((d->T + 2 * (d->T - 1)) + 31) / 32 * 32;
-  if (th > kMaxThreads) th = kMaxThreads;
-  if (th < 64) th = 64;
-  const int smax = max_dyn_smem();
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    using Gm = Geo<NB, R>;
-    const size_t vec_bytes = (9 * (size_t)d->T * Gm::VSTR + 64) * sizeof(R);
-    const size_t op_bytes = 2 * Gm::op_elems(d->T) * sizeof(R);
-    const R* o = static_cast<const R*>(ops);
-    if ((long)(vec_bytes + op_bytes) <= smax) {
-      auto k = pcg_packed_kernel<NB, R, true>;
-      cudaError_t e =
-          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(vec_bytes + op_bytes));
-      if (e != cudaSuccess) return (int)e;
-      k<<<d->Nb, th, vec_bytes + op_bytes, st>>>(o, rhs, x0, xo, it, (R)eps, max_iter, d->Nb, d->T, d->n);
-    } else {
-      if ((long)vec_bytes > smax) return (int)TMPC_ERR_SMEM;
-      auto k = pcg_packed_kernel<NB, R, false>;
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vec_bytes);
-      if (e != cudaSuccess) return (int)e;
-      k<<<d->Nb, th, vec_bytes, st>>>(o, rhs, x0, xo, it, (R)eps, max_iter, d->Nb, d->T, d->n);
-    }
-    return (int)cudaPeekAtLastError();
+    return launch_pcg_packed<NB, R>(d, static_cast<const R*>(ops), rhs, x0, xo, it, (R)eps, max_iter, st);
   });
 }
 
