@@ -1,0 +1,38 @@
+"""The C ABI library loads and exports every function the header declares;
+argument errors are reported (these calls touch no GPU)."""
+import ctypes as C
+import os
+import re
+
+from turbompc_b200 import _ffi
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "tmpc_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int32_t|size_t|const char\*)\s+(tmpc_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _ffi.load()
+    names = declared_functions()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(_ffi.exported_symbols())
+
+
+def test_error_codes_without_gpu():
+    lib = _ffi.load()
+    assert lib.tmpc_version() >= 100
+    assert b"null" in lib.tmpc_error_string(-1)
+    cfg = _ffi.TmpcAdmmConfig()
+    assert lib.tmpc_admm_solve_f32(None, None, None, None, None, C.byref(cfg), None, None, None, None, 0, None) == -1
+    bad = _ffi.TmpcDims(1, 1, 4, 2, 2, 0)  # T < 2
+    assert lib.tmpc_admm_solve_f64(C.byref(bad), None, None, None, None, C.byref(cfg), None, None, None, None, 0,
+                                   None) == -2
+    assert lib.tmpc_packed_operator_bytes(C.byref(_ffi.TmpcDims(1, 3, 40, 20, 20, 0)), 4) == 0  # n > 32
+    d = _ffi.TmpcDims(2, 5, 16, 12, 12, 4)
+    assert lib.tmpc_packed_operator_bytes(C.byref(d), 4) > 0

@@ -1,0 +1,217 @@
+"""Torch-facing wrappers of the CUDA C ABI (one call = one kernel launch on the
+current CUDA stream).  All tensors must live on the same CUDA device, share
+one dtype (float32 or float64) and be contiguous; wrappers raise otherwise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import NamedTuple, Optional
+
+import torch
+
+from . import _ffi
+from .qp_data import QPData
+
+
+class ADMMState(NamedTuple):
+    """turbompc/solvers/admm/admm.py:27-34, batched."""
+
+    x_blocks: torch.Tensor  # (Nb, T, n)
+    y_g: torch.Tensor  # (Nb, T, m)
+    y_f_0: torch.Tensor  # (Nb, n0)
+    y_f_dyn: torch.Tensor  # (Nb, N, nx)
+    z_g: torch.Tensor  # (Nb, T, m)
+    xi_g: torch.Tensor  # (Nb, T, m)
+    rho_bar: torch.Tensor  # (Nb,)
+
+
+@dataclass
+class AdmmConfig:
+    """ADMMConfig of turbompc/solvers/admm/csrc/admm_fused.cuh:6-22."""
+
+    max_iter: int = 100
+    pcg_max_iter: int = 10000
+    check_every: int = 25
+    adapt_rho_every: int = 25
+    eps_abs: float = 1e-9
+    eps_rel: float = 1e-9
+    sigma: float = 1e-6
+    rho_f_factor: float = 1000.0
+    alpha: float = 1.6
+    pcg_eps: float = 1e-20
+    adaptive_rho_tolerance: float = 5.0
+    rho_min: float = 1e-6
+    rho_max: float = 1e6
+    use_slack: bool = False
+    linsys: int = _ffi.LINSYS_PCG
+
+    def to_c(self) -> _ffi.TmpcAdmmConfig:
+        return _ffi.TmpcAdmmConfig(int(self.max_iter), int(self.pcg_max_iter), int(self.check_every),
+                                   int(self.adapt_rho_every), float(self.eps_abs), float(self.eps_rel),
+                                   float(self.sigma), float(self.rho_f_factor), float(self.alpha),
+                                   float(self.pcg_eps), float(self.adaptive_rho_tolerance), float(self.rho_min),
+                                   float(self.rho_max), int(bool(self.use_slack)), int(self.linsys))
+
+
+def _suffix(dtype: torch.dtype) -> str:
+    if dtype == torch.float32:
+        return "f32"
+    if dtype == torch.float64:
+        return "f64"
+    raise TypeError(f"turbompc_b200 kernels support float32/float64, got {dtype}")
+
+
+def _ptr(t: Optional[torch.Tensor], dtype=None, device=None) -> Optional[int]:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("turbompc_b200 kernels need CUDA tensors (no CPU fallback)")
+    if device is not None and t.device != device:
+        raise ValueError(f"tensor on {t.device}, expected {device}")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"tensor dtype {t.dtype}, expected {dtype}")
+    if not t.is_contiguous():
+        raise ValueError("turbompc_b200 kernels need contiguous tensors")
+    return t.data_ptr() if t.numel() > 0 else None
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dims_of(qp: QPData) -> _ffi.TmpcDims:
+    return _ffi.TmpcDims(qp.Nb, qp.T, qp.n, qp.nx, qp.n0, qp.m)
+
+
+def _qp_c(qp: QPData) -> _ffi.TmpcQP:
+    dt, dev = qp.dtype, qp.device
+    t = qp.tensors()
+    B, T, n, nx, n0, m = qp.Nb, qp.T, qp.n, qp.nx, qp.n0, qp.m
+    N = T - 1
+    shapes = dict(D=(B, T, n, n), E=(B, N, n, n), q=(B, T, n), A0=(B, n0, n), A_minus=(B, N, nx, n),
+                  A_plus=(B, N, nx, n), c0=(B, n0), c=(B, N, nx), G=(B, T, m, n), l=(B, T, m), u=(B, T, m))
+    for k, s in shapes.items():
+        if tuple(t[k].shape) != s:
+            raise ValueError(f"QP field {k} has shape {tuple(t[k].shape)}, expected {s}")
+    return _ffi.TmpcQP(*(_ptr(t[k], dt, dev) for k in ("D", "E", "q", "A0", "A_minus", "A_plus", "c0", "c", "G",
+                                                       "l", "u")))
+
+
+def _rho_vec(rho, qp: QPData) -> torch.Tensor:
+    r = torch.as_tensor(rho, dtype=qp.dtype, device=qp.device)
+    return r.expand(qp.Nb).contiguous() if r.dim() == 0 else r.contiguous()
+
+
+def schur_assemble(qp: QPData, rho_bar, sigma: float, rho_f_factor: float):
+    """compute_S_Phiinv (admm.py:71-154) for rho_f = rho_bar*rho_f_factor, rho_ineq = rho_bar.
+    Returns (S, Phiinv, status), S/Phiinv (Nb, T, n, 3n) in the reference layout."""
+    lib = _ffi.load()
+    B, T, n = qp.Nb, qp.T, qp.n
+    S = torch.empty(B, T, n, 3 * n, dtype=qp.dtype, device=qp.device)
+    P = torch.empty_like(S)
+    st = torch.zeros(B, dtype=torch.int32, device=qp.device)
+    rho = _rho_vec(rho_bar, qp)
+    name = f"tmpc_schur_assemble_{_suffix(qp.dtype)}"
+    d, q = dims_of(qp), _qp_c(qp)
+    _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), _ptr(rho), float(sigma), float(rho_f_factor),
+                                        _ptr(S), _ptr(P), _ptr(st), _stream(qp.device)))
+    return S, P, st
+
+
+def schur_assemble_packed(qp: QPData, rho_bar, sigma: float, rho_f_factor: float):
+    """Same operators in the packed format; returns (ops uint8 tensor, status)."""
+    lib = _ffi.load()
+    d, q = dims_of(qp), _qp_c(qp)
+    nbytes = lib.tmpc_packed_operator_bytes(C.byref(d), qp.dtype.itemsize)
+    if nbytes == 0 and qp.Nb > 0:
+        raise ValueError(f"unsupported dimensions for the packed format (n={qp.n})")
+    ops = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=qp.device)
+    st = torch.zeros(qp.Nb, dtype=torch.int32, device=qp.device)
+    rho = _rho_vec(rho_bar, qp)
+    name = f"tmpc_schur_assemble_packed_{_suffix(qp.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), _ptr(rho), float(sigma), float(rho_f_factor),
+                                        ops.data_ptr(), _ptr(st), _stream(qp.device)))
+    return ops, st
+
+
+def pcg_solve(S: torch.Tensor, Phiinv: torch.Tensor, rhs: torch.Tensor, x0: torch.Tensor, eps: float,
+              max_iters: int):
+    """pcg_blktridi_cuda (pcg_ffi.cc:115-147) on reference-layout operators.
+    S, Phiinv (Nb, T, n, 3n); rhs, x0 (Nb, T, n).  Returns (x, iters uint32->int64)."""
+    lib = _ffi.load()
+    if S.dim() != 4 or S.shape[-1] != 3 * S.shape[-2]:
+        raise ValueError("S must be (Nb, T, n, 3n)")
+    B, T, n = S.shape[:3]
+    for name_, t in (("Phiinv", Phiinv), ("rhs", rhs), ("x0", x0)):
+        want = S.shape if name_ == "Phiinv" else (B, T, n)
+        if tuple(t.shape) != tuple(want):
+            raise ValueError(f"{name_} has shape {tuple(t.shape)}, expected {tuple(want)}")
+    x = torch.empty_like(rhs)
+    it = torch.empty(B, dtype=torch.int32, device=S.device)
+    d = _ffi.TmpcDims(B, T, n, n, 0, 0)
+    name = f"tmpc_pcg_solve_{_suffix(S.dtype)}"
+    dt = S.dtype
+    _ffi.check(name, getattr(lib, name)(C.byref(d), _ptr(S, dt), _ptr(Phiinv, dt), _ptr(rhs, dt), _ptr(x0, dt),
+                                        _ptr(x), _ptr(it), float(eps), int(max_iters), _stream(S.device)))
+    return x, it.to(torch.int64) & 0xFFFFFFFF
+
+
+def pcg_solve_packed(ops: torch.Tensor, dims: _ffi.TmpcDims, rhs: torch.Tensor, x0: torch.Tensor, eps: float,
+                     max_iters: int):
+    """PCG on packed operators (from schur_assemble_packed)."""
+    lib = _ffi.load()
+    x = torch.empty_like(rhs)
+    it = torch.empty(rhs.shape[0], dtype=torch.int32, device=rhs.device)
+    name = f"tmpc_pcg_solve_packed_{_suffix(rhs.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(dims), ops.data_ptr(), _ptr(rhs), _ptr(x0, rhs.dtype), _ptr(x),
+                                        _ptr(it), float(eps), int(max_iters), _stream(rhs.device)))
+    return x, it.to(torch.int64) & 0xFFFFFFFF
+
+
+def admm_workspace_bytes(qp: QPData, cfg: AdmmConfig) -> int:
+    lib = _ffi.load()
+    d = dims_of(qp)
+    c = cfg.to_c()
+    return int(lib.tmpc_admm_workspace_bytes(C.byref(d), qp.dtype.itemsize, C.byref(c)))
+
+
+def _state_c(s: ADMMState, dt, dev) -> _ffi.TmpcAdmmState:
+    return _ffi.TmpcAdmmState(_ptr(s.x_blocks, dt, dev), _ptr(s.y_g, dt, dev), _ptr(s.y_f_0, dt, dev),
+                              _ptr(s.y_f_dyn, dt, dev), _ptr(s.z_g, dt, dev), _ptr(s.xi_g, dt, dev),
+                              _ptr(s.rho_bar, dt, dev))
+
+
+def empty_state_like(s: ADMMState) -> ADMMState:
+    return ADMMState(*(torch.empty_like(t) for t in s))
+
+
+def admm_solve(qp: QPData, state0: ADMMState, cfg: AdmmConfig, slack_weight=None, out: Optional[ADMMState] = None,
+               workspace: Optional[torch.Tensor] = None):
+    """Fused ADMM solve (admm_fused_cuda).  Returns (state, iters, status)."""
+    lib = _ffi.load()
+    dt, dev = qp.dtype, qp.device
+    if out is None:
+        out = empty_state_like(state0)
+    it = torch.empty(qp.Nb, dtype=torch.int32, device=dev)
+    st = torch.empty(qp.Nb, dtype=torch.int32, device=dev)
+    sw = None if slack_weight is None else _rho_vec(slack_weight, qp)
+    ws_need = admm_workspace_bytes(qp, cfg)
+    if ws_need > 0 and (workspace is None or workspace.numel() < ws_need):
+        workspace = torch.empty(ws_need, dtype=torch.uint8, device=dev)
+    ws_ptr = workspace.data_ptr() if (workspace is not None and ws_need > 0) else None
+    d, q, c = dims_of(qp), _qp_c(qp), cfg.to_c()
+    si, so = _state_c(state0, dt, dev), _state_c(out, dt, dev)
+    name = f"tmpc_admm_solve_{_suffix(dt)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), C.byref(si), C.byref(so), _ptr(sw), C.byref(c),
+                                        None, _ptr(it), _ptr(st), ws_ptr, ws_need, _stream(dev)))
+    return out, it.to(torch.int64) & 0xFFFFFFFF, st
+
+
+def admm_initial_state(qp: QPData, rho_bar, x0: Optional[torch.Tensor] = None) -> ADMMState:
+    """admm.py:1051-1088: x = 0 (or x0), z_g = clamp(G x, l, u), duals zero."""
+    B, T, n, m = qp.Nb, qp.T, qp.n, qp.m
+    x = torch.zeros(B, T, n, dtype=qp.dtype, device=qp.device) if x0 is None else x0.clone().contiguous()
+    z = torch.minimum(torch.maximum(torch.einsum("btmn,btn->btm", qp.ineq.G, x), qp.ineq.l), qp.ineq.u)
+    return ADMMState(x, torch.zeros_like(z), torch.zeros_like(qp.eq.c0), torch.zeros_like(qp.eq.c),
+                     z.contiguous(), torch.zeros_like(z), _rho_vec(rho_bar, qp).clone())
