@@ -124,8 +124,10 @@ def test_admm_slack_and_residual_checks(prec):
     """Soft constraints (slack update, admm_math.cuh:168-200), residual checks
     and adaptive rho; early termination per problem."""
     b = dense_blocks(6, 4, 2, 10, 3, seed=3)
-    kw = dict(max_iter=60, pcg_max_iter=40, check_every=5, adapt_rho_every=10, eps_abs=1e-6, eps_rel=1e-6,
-              pcg_eps=1e-20, rho_f_factor=100.0, alpha=1.6, sigma=1e-6)
+    # Few PCG iterations (no PCG early stop) keep the residuals far from
+    # convergence, where the rho candidate sqrt(p/d) is well conditioned.
+    kw = dict(max_iter=60, pcg_max_iter=6, check_every=5, adapt_rho_every=10, eps_abs=1e-3, eps_rel=1e-3,
+              pcg_eps=0.0, rho_f_factor=100.0, alpha=1.6, sigma=1e-6)
     out, iters, status, so, io, tol = _run_admm(b, prec, kw, slack=10.0)
     assert (_np(iters) == io).all()
     assert rel_err(_np(out.rho_bar), so.rho) < 1e-9
