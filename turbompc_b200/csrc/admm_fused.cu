@@ -22,6 +22,7 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
                void* ws, size_t ws_bytes, cudaStream_t st) {
   int rc = check_dims(d);
   if (rc) return rc;
+  if (d->Nb == 0) return TMPC_OK;
   if (!qp || !in || !out || !cfg) return TMPC_ERR_NULL_ARG;
   if (!qp->D || !qp->E || !qp->q || !qp->A_minus || !qp->A_plus || !qp->c) return TMPC_ERR_NULL_ARG;
   if (d->n0 > 0 && (!qp->A0 || !qp->c0)) return TMPC_ERR_NULL_ARG;

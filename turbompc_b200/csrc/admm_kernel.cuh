@@ -36,7 +36,7 @@ struct AdmmSmem {
     opP = o;
     if (ops_smem) o += opn;
     vec0 = o;
-    o += 10 * (size_t)T * Gm::VSTR;  // x r z p d lo up0 up1 gam xold
+    o += 12 * (size_t)T * Gm::VSTR;  // x r z p d lo up0..up3 gam xold
     yf0 = a4(o); o = yf0 + n0;
     yfd = a4(o); o = yfd + (size_t)N * nx;
     zg = a4(o); o = zg + (size_t)T * m;
@@ -231,10 +231,11 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   R* opP = OPS_SMEM ? sm + L.opP : P.ws + (size_t)b * 2 * opn + opn;
   const size_t VS = (size_t)T * Gm::VSTR;
   R* vbase = sm + L.vec0;
-  BlockVecs<NB, R> w{vbase,          vbase + VS,     vbase + 2 * VS, vbase + 3 * VS,
-                     vbase + 4 * VS, vbase + 5 * VS, vbase + 6 * VS, vbase + 7 * VS};
-  R* gam = vbase + 8 * VS;
-  R* xold = vbase + 9 * VS;
+  BlockVecs<NB, R> w{vbase,          vbase + VS,     vbase + 2 * VS,
+                     vbase + 3 * VS, vbase + 4 * VS, vbase + 5 * VS,
+                     {vbase + 6 * VS, vbase + 7 * VS, vbase + 8 * VS, vbase + 9 * VS}};
+  R* gam = vbase + 10 * VS;
+  R* xold = vbase + 11 * VS;
   R* yf0 = sm + L.yf0;
   R* yfd = sm + L.yfd;
   R* zg = sm + L.zg;
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   const QPView<R> qp = qp_view<R>(P.qp, b, T, n, nx, n0, m);
 
   // ---- load the warm-start state; zero all block vectors (keeps padding 0)
-  for (size_t e = threadIdx.x; e < 10 * VS; e += blockDim.x) vbase[e] = R(0);
+  for (size_t e = threadIdx.x; e < 12 * VS; e += blockDim.x) vbase[e] = R(0);
   __syncthreads();
   {
     const R* x_in = static_cast<const R*>(P.in.x) + (size_t)b * T * n;

@@ -3,13 +3,14 @@
 // Matvec y = M v for a symmetric block-tridiagonal M in packed form
 // (diagonal blocks Dg_t, sub-diagonal blocks L_t = M(t+1, t)):
 //     y_t = L_{t-1} v_{t-1} + Dg_t v_t + L_t^T v_{t+1}
-// is split into T + 2N independent tasks, one thread each:
-//   diag task t          d[t]      = Dg_t v_t       (each packed entry used twice)
-//   half task (t, h)     lo[t+1]  |= L_t[rows_h] v_t
-//                        up_h[t]   = L_t[rows_h]^T v_{t+1}[rows_h]
-// A task reads its whole block once with 128-bit loads and keeps the
+// is split into T + 4N independent tasks, one thread each:
+//   diag task t           d[t]      = Dg_t v_t       (each packed entry used twice)
+//   quarter task (t, q)   lo[t+1]  |= L_t[rows_q] v_t
+//                         up_q[t]   = L_t[rows_q]^T v_{t+1}[rows_q]
+// A task reads its part of the block once with 128-bit loads and keeps the
 // partial results in registers, so every stored entry is read once per
-// matvec and feeds two FMAs.  y = d + lo + up0 + up1 after a barrier.
+// matvec and feeds two FMAs.  y = d + lo + up0 + up1 + up2 + up3 after a
+// barrier (fixed summation order: deterministic).
 //
 // The PCG recurrences and the stopping rule follow
 // turbompc/solvers/admm/csrc/admm_fused.cu:54-161 (the fused kernel's PCG):
@@ -31,8 +32,7 @@ struct BlockVecs {
   R* p;
   R* d;
   R* lo;
-  R* up0;
-  R* up1;
+  R* up[4];
 };
 
 template <int NB, bool OPS_SMEM, typename R>
@@ -61,14 +61,14 @@ __device__ __forceinline__ void diag_task(const R* __restrict__ blk, const R* __
   for (int c = 0; c < NB / VEC; ++c) st128(out + c * VEC, &acc[c * VEC]);
 }
 
-// Half h of sub-diagonal block L_t: rows [h*NB/2, (h+1)*NB/2).
+// Quarter h of sub-diagonal block L_t: rows [h*NB/4, (h+1)*NB/4).
 template <int NB, bool OPS_SMEM, typename R>
-__device__ __forceinline__ void half_task(const R* __restrict__ blk, const R* __restrict__ vt,
+__device__ __forceinline__ void quarter_task(const R* __restrict__ blk, const R* __restrict__ vt,
                                           const R* __restrict__ vt1, R* __restrict__ lo_out,
                                           R* __restrict__ up_out, int h) {
   using Gm = Geo<NB, R>;
   constexpr int VEC = Gm::VEC;
-  constexpr int HR = NB / 2;
+  constexpr int HR = NB / 4;
   R a[NB], b[HR], up[NB];
 #pragma unroll
   for (int c = 0; c < NB / VEC; ++c) ld128(&a[c * VEC], vt + c * VEC);
@@ -110,30 +110,54 @@ __device__ __forceinline__ void half_task(const R* __restrict__ blk, const R* __
   for (int c = 0; c < NB / VEC; ++c) st128(up_out + c * VEC, &up[c * VEC]);
 }
 
-// Partial results of y = M v; caller syncs before reading d/lo/up0/up1.
-// lo[0], up0[N], up1[N] are never written and must hold zeros.
+// Partial results of y = M v; caller syncs before reading d/lo/up[].
+// lo[0] and up[q][N] are never written and must hold zeros.
 template <int NB, bool OPS_SMEM, typename R>
-__device__ __forceinline__ void matvec_partials(const R* op, int T, const R* v, R* d, R* lo, R* up0, R* up1) {
+__device__ __forceinline__ void matvec_partials(const R* op, int T, const R* v, const BlockVecs<NB, R>& w) {
   using Gm = Geo<NB, R>;
   const int N = T - 1;
   const R* Dg = op;
   const R* L = op + (size_t)T * Gm::DSTR;
-  const int ntask = T + 2 * N;
+  const int ntask = T + 4 * N;
   for (int task = threadIdx.x; task < ntask; task += blockDim.x) {
     if (task < T) {
-      diag_task<NB, OPS_SMEM>(Dg + (size_t)task * Gm::DSTR, v + task * Gm::VSTR, d + task * Gm::VSTR);
+      diag_task<NB, OPS_SMEM>(Dg + (size_t)task * Gm::DSTR, v + task * Gm::VSTR, w.d + task * Gm::VSTR);
     } else {
       const int k = task - T;
-      const int h = k >= N ? 1 : 0;
-      const int t = k - h * N;
-      half_task<NB, OPS_SMEM>(L + (size_t)t * Gm::OSTR, v + t * Gm::VSTR, v + (t + 1) * Gm::VSTR,
-                              lo + (t + 1) * Gm::VSTR, (h ? up1 : up0) + t * Gm::VSTR, h);
+      const int q = k / N;  // consecutive threads take consecutive blocks of the same quarter
+      const int t = k - q * N;
+      quarter_task<NB, OPS_SMEM>(L + (size_t)t * Gm::OSTR, v + t * Gm::VSTR, v + (t + 1) * Gm::VSTR,
+                                 w.lo + (t + 1) * Gm::VSTR, w.up[q] + t * Gm::VSTR, q);
     }
   }
 }
 
-// Elementwise loop over the T*NB padded entries of a block vector: e is the
-// dense index, off the on-chip offset t*VSTR + j.
+// y = d + lo + up0 + up1 + up2 + up3 for the VEC entries at offset o.
+template <int NB, typename R>
+__device__ __forceinline__ void gather_y(R* y, const BlockVecs<NB, R>& w, int o) {
+  constexpr int VEC = Geo<NB, R>::VEC;
+  R a[VEC], b[VEC];
+  ld128(y, w.d + o);
+  ld128(a, w.lo + o);
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) y[k] += a[k];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    ld128(b, w.up[q] + o);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) y[k] += b[k];
+  }
+}
+
+// Vectorised elementwise loop over the T*NB padded entries of a block
+// vector: each iteration handles VEC consecutive entries at on-chip offset
+// `off` (16-byte aligned).
+#define TMPC_FOR_CHUNKS(off, T, NB, VSTR, VEC)                                                            \
+  for (int c_ = threadIdx.x, off = 0;                                                                    \
+       c_ < (T) * ((NB) / (VEC)) && ((off = (c_ / ((NB) / (VEC))) * (VSTR) + (c_ % ((NB) / (VEC))) * (VEC)), true); \
+       c_ += blockDim.x)
+
+// Scalar elementwise loop (e: dense index t*NB + j, off: on-chip offset).
 #define TMPC_FOR_ENTRIES(e, off, T, NB, VSTR)                                                       \
   for (int e = threadIdx.x, off = 0; e < (T) * (NB) && ((off = (e / (NB)) * (VSTR) + e % (NB)), true); \
        e += blockDim.x)
@@ -145,18 +169,29 @@ template <int NB, bool OPS_SMEM, typename R>
 __device__ int pcg_solve(const R* opS, const R* opP, int T, const R* g, const BlockVecs<NB, R>& w, R* red,
                          int max_iter, R eps) {
   using Gm = Geo<NB, R>;
-  matvec_partials<NB, OPS_SMEM>(opS, T, w.x, w.d, w.lo, w.up0, w.up1);
+  constexpr int VEC = Gm::VEC;
+  matvec_partials<NB, OPS_SMEM>(opS, T, w.x, w);
   __syncthreads();
-  TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { w.r[o] = g[o] - (w.d[o] + w.lo[o] + w.up0[o] + w.up1[o]); }
+  TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+    R y[VEC], gg[VEC];
+    gather_y<NB>(y, w, o);
+    ld128(gg, g + o);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) y[k] = gg[k] - y[k];
+    st128(w.r + o, y);
+  }
   __syncthreads();
-  matvec_partials<NB, OPS_SMEM>(opP, T, w.r, w.d, w.lo, w.up0, w.up1);
+  matvec_partials<NB, OPS_SMEM>(opP, T, w.r, w);
   __syncthreads();
   R part = R(0);
-  TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) {
-    const R zz = w.d[o] + w.lo[o] + w.up0[o] + w.up1[o];
-    w.z[o] = zz;
-    w.p[o] = zz;
-    part = fma(w.r[o], zz, part);
+  TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+    R zz[VEC], rr[VEC];
+    gather_y<NB>(zz, w, o);
+    ld128(rr, w.r + o);
+    st128(w.z + o, zz);
+    st128(w.p + o, zz);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) part = fma(rr[k], zz[k], part);
   }
   R eta = block_sum(part, red);
   const R eta0 = fabs(eta);
@@ -164,34 +199,57 @@ __device__ int pcg_solve(const R* opS, const R* opP, int T, const R* g, const Bl
   for (; it < max_iter; ++it) {
     if (fabs(eta) < R(1e-12) + eps * eta0) break;
     __syncthreads();  // p complete; reduction slots free
-    matvec_partials<NB, OPS_SMEM>(opS, T, w.p, w.d, w.lo, w.up0, w.up1);
+    matvec_partials<NB, OPS_SMEM>(opS, T, w.p, w);
     __syncthreads();
     part = R(0);
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) {
-      const R sp = w.d[o] + w.lo[o] + w.up0[o] + w.up1[o];
-      w.d[o] = sp;
-      part = fma(w.p[o], sp, part);
+    TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+      R sp[VEC], pp[VEC];
+      gather_y<NB>(sp, w, o);
+      ld128(pp, w.p + o);
+      st128(w.d + o, sp);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) part = fma(pp[k], sp[k], part);
     }
     R den = block_sum(part, red + 32);
     if (fabs(den) < R(1e-30)) den = R(1e-30);
     const R alpha = eta / den;
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) {
-      w.x[o] = fma(alpha, w.p[o], w.x[o]);
-      w.r[o] = fma(-alpha, w.d[o], w.r[o]);
+    TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+      R sp[VEC], pp[VEC], xx[VEC], rr[VEC];
+      ld128(sp, w.d + o);
+      ld128(pp, w.p + o);
+      ld128(xx, w.x + o);
+      ld128(rr, w.r + o);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        xx[k] = fma(alpha, pp[k], xx[k]);
+        rr[k] = fma(-alpha, sp[k], rr[k]);
+      }
+      st128(w.x + o, xx);
+      st128(w.r + o, rr);
     }
     __syncthreads();
-    matvec_partials<NB, OPS_SMEM>(opP, T, w.r, w.d, w.lo, w.up0, w.up1);
+    matvec_partials<NB, OPS_SMEM>(opP, T, w.r, w);
     __syncthreads();
     part = R(0);
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) {
-      const R zz = w.d[o] + w.lo[o] + w.up0[o] + w.up1[o];
-      w.z[o] = zz;
-      part = fma(w.r[o], zz, part);
+    TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+      R zz[VEC], rr[VEC];
+      gather_y<NB>(zz, w, o);
+      ld128(rr, w.r + o);
+      st128(w.z + o, zz);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) part = fma(rr[k], zz[k], part);
     }
     const R eta_new = block_sum(part, red);
     const R beta = eta_new / eta;
     eta = eta_new;
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { w.p[o] = fma(beta, w.p[o], w.z[o]); }
+    TMPC_FOR_CHUNKS(o, T, NB, Gm::VSTR, VEC) {
+      R zz[VEC], pp[VEC];
+      ld128(zz, w.z + o);
+      ld128(pp, w.p + o);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) pp[k] = fma(beta, pp[k], zz[k]);
+      st128(w.p + o, pp);
+    }
   }
   __syncthreads();
   return it;

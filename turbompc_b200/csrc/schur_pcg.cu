@@ -94,6 +94,7 @@ int schur_assemble(const TmpcDims* d, const TmpcQP* qp, const R* rho, double sig
                    int32_t* status, cudaStream_t st) {
   int rc = check_dims(d);
   if (rc) return rc;
+  if (d->Nb == 0) return TMPC_OK;
   if (!qp || !rho || !S || !P || !qp->D || !qp->E || !qp->A_minus || !qp->A_plus) return TMPC_ERR_NULL_ARG;
   if (d->n0 > 0 && !qp->A0) return TMPC_ERR_NULL_ARG;
   if (d->m > 0 && !qp->G) return TMPC_ERR_NULL_ARG;
@@ -109,6 +110,7 @@ int schur_assemble_packed(const TmpcDims* d, const TmpcQP* qp, const R* rho, dou
                           int32_t* status, cudaStream_t st) {
   int rc = check_dims(d);
   if (rc) return rc;
+  if (d->Nb == 0) return TMPC_OK;
   if (!qp || !rho || !ops || !qp->D || !qp->E || !qp->A_minus || !qp->A_plus) return TMPC_ERR_NULL_ARG;
   if (d->n0 > 0 && !qp->A0) return TMPC_ERR_NULL_ARG;
   if (d->m > 0 && !qp->G) return TMPC_ERR_NULL_ARG;

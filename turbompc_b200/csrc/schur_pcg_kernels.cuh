@@ -83,10 +83,11 @@ __global__ void __launch_bounds__(max_threads_for(NB)) pcg_packed_kernel(const R
     opP = s_ops + opn;
   }
   const size_t VS = (size_t)T * Gm::VSTR;
-  BlockVecs<NB, R> w{vb, vb + VS, vb + 2 * VS, vb + 3 * VS, vb + 4 * VS, vb + 5 * VS, vb + 6 * VS, vb + 7 * VS};
-  R* g = vb + 8 * VS;
-  R* red = vb + 9 * VS;
-  for (size_t e = threadIdx.x; e < 9 * VS; e += blockDim.x) vb[e] = R(0);
+  BlockVecs<NB, R> w{vb, vb + VS, vb + 2 * VS, vb + 3 * VS, vb + 4 * VS, vb + 5 * VS,
+                     {vb + 6 * VS, vb + 7 * VS, vb + 8 * VS, vb + 9 * VS}};
+  R* g = vb + 10 * VS;
+  R* red = vb + 11 * VS;
+  for (size_t e = threadIdx.x; e < 11 * VS; e += blockDim.x) vb[e] = R(0);
   __syncthreads();
   const int tot = T * n;
   for (int e = threadIdx.x; e < tot; e += blockDim.x) {
@@ -137,7 +138,7 @@ int launch_pcg_packed(const TmpcDims* d, const R* o, const R* rhs, const R* x0, 
   using Gm = Geo<NB, R>;
   const int th = cta_threads(d->T, max_threads_for(NB));
   const int smax = max_dyn_smem();
-  const size_t vec_bytes = (9 * (size_t)d->T * Gm::VSTR + 64) * sizeof(R);
+  const size_t vec_bytes = (11 * (size_t)d->T * Gm::VSTR + 64) * sizeof(R);
   const size_t op_bytes = 2 * Gm::op_elems(d->T) * sizeof(R);
   if ((long)(vec_bytes + op_bytes) <= smax) {
     auto k = pcg_packed_kernel<NB, R, true>;

@@ -28,9 +28,9 @@ constexpr int kMaxThreads = 512;
 // 256 for larger blocks, whose register-resident block tasks need up to 255
 // registers per thread.
 __host__ __device__ constexpr int max_threads_for(int nb) { return nb <= 16 ? 512 : 256; }
-// One thread per matvec task (T diagonal + 2N half blocks), rounded to warps.
+// One thread per matvec task (T diagonal + 4N quarter blocks), rounded to warps.
 inline int cta_threads(int T, int maxt) {
-  int th = ((T + 2 * (T - 1)) + 31) / 32 * 32;
+  int th = ((T + 4 * (T - 1)) + 31) / 32 * 32;
   if (th < 64) th = 64;
   if (th > maxt) th = maxt;
   return th;
