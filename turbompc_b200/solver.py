@@ -1,0 +1,379 @@
+"""TurboMPC SQP solver with the B200 backend
+(mirrors turbompc/solvers/turbompc_solver.py).
+
+    solver = TurboMPCSolver(program, params=load_solver_params(),
+                            forward_backend="b200", backward_backend="b200")
+    guess = solver.initial_guess(problem_params)
+    sol = solver.solve(guess, problem_params, weights={})
+
+Everything is batched: ``sol.states`` is (Nb, N+1, nx).  Each SQP iteration
+builds the QP at the current trajectory on the GPU and solves it with one
+launch of the fused ADMM kernel (``tmpc_admm_solve_*``), warm-started from
+the previous ADMM state; the per-problem SQP loop stops when the first-order
+error is <= tol_convergence (problems that stop early keep their iterate, as
+under jax.vmap of the reference's while_loop).
+"""
+from __future__ import annotations
+
+import copy
+import enum
+from typing import Any, Dict, NamedTuple, Optional, Union
+
+import torch
+
+from . import ops
+from .ops import ADMMState, AdmmConfig
+from .qp_data import QPData, qpdata_from_ocp_blocks
+
+DEFAULT_SOLVER_PARAMS: Dict[str, Any] = {
+    # turbompc/solvers/params/turbompc.yaml:1-23
+    "verbose": False,
+    "tol_convergence": 1e-6,
+    "convergence_criterion": "first_order",
+    "num_sqp_iteration_max": 15,
+    "linesearch": False,
+    "admm": {
+        "rho": 0.1, "sigma": 1e-6, "max_iter": 100, "eps_abs": 1e-9, "eps_rel": 1e-9, "rho_min": 1e-6,
+        "rho_max": 1e6, "check_termination_every": 25, "adapt_rho_every": 25, "adaptive_rho_tolerance": 5.0,
+        "relaxation_parameter": 1.6, "rho_f_factor": 1000.0,
+        "pcg": {"max_iter": 10000, "tol_epsilon": 1e-20},
+    },
+}
+
+
+def load_solver_params(overrides: Optional[Dict[str, Any]] = None) -> Dict[str, Any]:
+    p = copy.deepcopy(DEFAULT_SOLVER_PARAMS)
+    if overrides:
+        _deep_merge(p, overrides)
+    return p
+
+
+def _deep_merge(dst, src):
+    for k, v in src.items():
+        if isinstance(v, dict) and isinstance(dst.get(k), dict):
+            _deep_merge(dst[k], v)
+        else:
+            dst[k] = v
+
+
+class ForwardBackend(enum.IntEnum):
+    """Forward QP backends (turbompc_solver.py:56-64) plus the B200 ones."""
+
+    B200 = 100  # fused ADMM + PCG (drop-in for admm_fused_pcg)
+    B200_DIRECT = 101  # fused ADMM + block-tridiagonal Cholesky (drop-in for admm_fused_cudss)
+
+
+class BackwardBackend(enum.IntEnum):
+    B200 = 100  # direct adjoint KKT solve on the GPU (drop-in for direct_cudss_ffi)
+
+
+_FORWARD_NAMES = {"b200": ForwardBackend.B200, "b200_pcg": ForwardBackend.B200,
+                  "admm_fused_pcg": ForwardBackend.B200, "b200_direct": ForwardBackend.B200_DIRECT,
+                  "admm_fused_cudss": ForwardBackend.B200_DIRECT}
+_BACKWARD_NAMES = {"b200": BackwardBackend.B200, "direct_cudss_ffi": BackwardBackend.B200,
+                   "direct_jax_dense": BackwardBackend.B200}
+
+
+def parse_forward_backend(value: Union[str, ForwardBackend]) -> ForwardBackend:
+    if isinstance(value, ForwardBackend):
+        return value
+    if not isinstance(value, str):
+        raise TypeError(f"Expected str or ForwardBackend, got {type(value)}")
+    try:
+        return _FORWARD_NAMES[value.lower()]
+    except KeyError as exc:
+        raise ValueError(f"Unknown forward backend: {value!r}. Options: {sorted(_FORWARD_NAMES)}") from exc
+
+
+def parse_backward_backend(value: Union[str, BackwardBackend]) -> BackwardBackend:
+    if isinstance(value, BackwardBackend):
+        return value
+    if not isinstance(value, str):
+        raise TypeError(f"Expected str or BackwardBackend, got {type(value)}")
+    try:
+        return _BACKWARD_NAMES[value.lower()]
+    except KeyError as exc:
+        raise ValueError(f"Unknown backward backend: {value!r}. Options: {sorted(_BACKWARD_NAMES)}") from exc
+
+
+class KKTState(NamedTuple):
+    """turbompc_solver.py:194-203 (batched)."""
+
+    states: torch.Tensor
+    controls: torch.Tensor
+    slack: torch.Tensor
+    y_f: torch.Tensor  # (Nb, N+1, nx)
+    y_ineq: torch.Tensor  # (Nb, N+1, m)
+    ineq_active_lower_idx: torch.Tensor
+    ineq_active_upper_idx: torch.Tensor
+
+
+class SolverStats(NamedTuple):
+    admm_num_iters: torch.Tensor  # (Nb, max_iter)
+    eq_constraints_violations: torch.Tensor
+    ineq_constraints_violations: torch.Tensor
+    convergence_errors: torch.Tensor
+
+
+class TurboMPCSolution(NamedTuple):
+    """turbompc_solver.py:225-238 (batched over the leading axis)."""
+
+    states: torch.Tensor
+    controls: torch.Tensor
+    slack: torch.Tensor
+    status: int
+    num_iter: torch.Tensor  # (Nb,)
+    convergence_error: torch.Tensor  # (Nb,)
+    admm_iters: torch.Tensor  # (Nb, max_iter)
+    linesearch_alphas: Optional[torch.Tensor] = None
+    admm_state: Optional[ADMMState] = None
+    solver_stats: Optional[SolverStats] = None
+    dual_backward_guess: Optional[torch.Tensor] = None
+    kkt_state: Optional[KKTState] = None
+
+
+def identify_active_inequalities(g, l, u, eps_abs, eps_rel):
+    """turbompc_solver.py:269-292: min(g-l, u-g) <= eps_abs + eps_rel |bound|."""
+    dl = g - l
+    du = u - g
+    use_upper = du < dl
+    bound = torch.where(use_upper, u.abs(), l.abs())
+    active = torch.minimum(dl, du) <= eps_abs + eps_rel * bound
+    return active & ~use_upper, active & use_upper
+
+
+def _inf(x):
+    return x.reshape(x.shape[0], -1).abs().amax(dim=1) if x.shape[-1] > 0 else torch.zeros(
+        x.shape[0], dtype=x.dtype, device=x.device)
+
+
+class TurboMPCSolver:
+    """SQP solver that uses the fused B200 ADMM kernel for each QP."""
+
+    STATUS_SUCCESS = 0
+    STATUS_FAILED = -1
+
+    def __init__(self, program, params: Optional[Dict[str, Any]] = None, name: str = "TurboMPCSolver", *,
+                 forward_backend: Union[str, ForwardBackend] = "b200",
+                 backward_backend: Union[str, BackwardBackend] = "b200", use_full_hessian: bool = True):
+        self._program = program
+        self._params = load_solver_params(params) if params is not None else load_solver_params()
+        self._name = name
+        self._forward_backend = parse_forward_backend(forward_backend)
+        self._backward_backend = parse_backward_backend(backward_backend)
+        self._use_full_hessian = use_full_hessian
+        crit = self._params.get("convergence_criterion", "first_order")
+        if crit not in ("first_order", "step"):
+            raise ValueError(f"Unknown convergence criterion: {crit!r}")
+        if self._params.get("linesearch", False):
+            raise NotImplementedError("line search is not on the b200 path (turbompc.yaml default: False)")
+        a = self._params["admm"]
+        self._admm_cfg = AdmmConfig(
+            max_iter=int(a["max_iter"]), pcg_max_iter=int(a["pcg"]["max_iter"]),
+            check_every=int(a.get("check_termination_every", 1)), adapt_rho_every=int(a.get("adapt_rho_every", 5)),
+            eps_abs=float(a.get("eps_abs", 1e-4)), eps_rel=float(a.get("eps_rel", 1e-3)), sigma=float(a["sigma"]),
+            rho_f_factor=float(a.get("rho_f_factor", 1000.0)), alpha=float(a.get("relaxation_parameter", 1.0)),
+            pcg_eps=float(a["pcg"].get("tol_epsilon", 1e-8)),
+            adaptive_rho_tolerance=float(a.get("adaptive_rho_tolerance", 5.0)),
+            rho_min=float(a.get("rho_min", 1e-6)), rho_max=float(a.get("rho_max", 1e6)),
+            use_slack=bool(program.use_slack_variables),
+            linsys=1 if self._forward_backend == ForwardBackend.B200_DIRECT else 0)
+        self._workspace = None
+        self.solve = self.get_differentiable_solve_function()
+
+    # -------------------------------------------------------------- props
+    @property
+    def program(self):
+        return self._program
+
+    @property
+    def params(self):
+        return self._params
+
+    @property
+    def name(self):
+        return self._name
+
+    @property
+    def forward_backend(self):
+        return self._forward_backend
+
+    @property
+    def backward_backend(self):
+        return self._backward_backend
+
+    @property
+    def admm_config(self) -> AdmmConfig:
+        return self._admm_cfg
+
+    # --------------------------------------------------------------- API
+    def initial_guess(self, params=None) -> TurboMPCSolution:
+        params = params if params is not None else self._program.params
+        states, controls = self._program.initial_guess(params)
+        Nb = states.shape[0]
+        mi = int(self._params["num_sqp_iteration_max"])
+        m = self._program.num_inequality_constraints
+        z = lambda *s: torch.zeros(*s, dtype=states.dtype, device=states.device)
+        stats = SolverStats(torch.zeros(Nb, mi, dtype=torch.int64, device=states.device), z(Nb, mi), z(Nb, mi),
+                            z(Nb, mi))
+        return TurboMPCSolution(states=states, controls=controls, slack=z(Nb, states.shape[1], m),
+                                status=self.STATUS_SUCCESS, num_iter=torch.zeros(Nb, dtype=torch.int64,
+                                                                                 device=states.device),
+                                convergence_error=z(Nb), admm_iters=torch.zeros(Nb, mi, dtype=torch.int64,
+                                                                                device=states.device),
+                                admm_state=None, solver_stats=stats)
+
+    def make_params_with_weights(self, weights, problem_params=None):
+        base = dict(self._program.params if problem_params is None else problem_params)
+        out = dict(base)
+        for k, v in (weights or {}).items():
+            if isinstance(v, dict) and isinstance(out.get(k), dict):
+                d = dict(out[k])
+                d.update(v)
+                out[k] = d
+            else:
+                out[k] = v
+        return out
+
+    def get_differentiable_solve_function(self):
+        """solve(guess, params, weights) -> TurboMPCSolution.  Gradients w.r.t.
+        tensors in ``weights`` (and initial_state) flow through the adjoint KKT
+        backward when the b200 backward path is available."""
+        from .backward import make_differentiable_solve
+
+        return make_differentiable_solve(self)
+
+    # ------------------------------------------------------------ QP build
+    def _build_qp_data(self, states, controls, params) -> QPData:
+        """turbompc_solver.py:1098-1156."""
+        prog = self._program
+        D, E, q = prog.get_cost_linearized_blocks(states, controls, params)
+        As_next, Bs_next, As, Bs, Cs = prog.get_dynamics_linearized_matrices(states, controls, params)
+        G, l, u = prog.get_inequalities_linearized_matrices(states, controls, params)
+        A0, c0 = prog.get_initial_equality_linearized_matrices(params, states)
+        sw = params.get("slack_penalization_weight", None)
+        if sw is not None:
+            sw = torch.as_tensor(sw, dtype=states.dtype, device=states.device).expand(states.shape[0]).contiguous()
+        c = lambda t: t.contiguous()
+        return qpdata_from_ocp_blocks(c(D), c(E), c(q), c(A0), c(c0), c(As_next), c(Bs_next), c(As), c(Bs),
+                                      c(Cs[:, 1:]), c(G), c(l), c(u), prog.use_slack_variables, sw)
+
+    def _first_order_error(self, qp: QPData, states, controls, slacks, st: ADMMState):
+        """turbompc_solver.py:1158-1225 (first_order criterion)."""
+        x = torch.cat([states, controls], -1)
+        D, E = qp.cost.D, qp.cost.E
+        Px = torch.einsum("btij,btj->bti", D, x)
+        Px[:, 1:] += torch.einsum("btij,btj->bti", E, x[:, :-1])
+        Px[:, :-1] += torch.einsum("btji,btj->bti", E, x[:, 1:])
+        Ct = torch.zeros_like(x)
+        Ct[:, 0] += torch.einsum("bki,bk->bi", qp.eq.A0, st.y_f_0)
+        Ct[:, :-1] += torch.einsum("btki,btk->bti", qp.eq.A_minus, st.y_f_dyn)
+        Ct[:, 1:] += torch.einsum("btki,btk->bti", qp.eq.A_plus, st.y_f_dyn)
+        Gt = torch.einsum("btki,btk->bti", qp.ineq.G, st.y_g)
+        stat = _inf(Px + qp.cost.q + Ct + Gt)
+        Cx0 = torch.einsum("bki,bi->bk", qp.eq.A0, x[:, 0]) - qp.eq.c0
+        Cx = (torch.einsum("btki,bti->btk", qp.eq.A_minus, x[:, :-1])
+              + torch.einsum("btki,bti->btk", qp.eq.A_plus, x[:, 1:]) - qp.eq.c)
+        eq = torch.maximum(_inf(Cx0), _inf(Cx))
+        g = torch.einsum("btki,bti->btk", qp.ineq.G, x)
+        gb = g + slacks if qp.ineq.use_slack_variables else g
+        if qp.m > 0:
+            viol = torch.maximum((qp.ineq.l - gb).clamp_min(0), (gb - qp.ineq.u).clamp_min(0))
+            ineq = _inf(viol)
+        else:
+            ineq = torch.zeros_like(stat)
+        conv = torch.maximum(stat, torch.maximum(eq, ineq))
+        if qp.ineq.use_slack_variables and qp.m > 0:
+            sw = qp.ineq.slack_penalization_weight
+            conv = torch.maximum(conv, _inf(sw[:, None, None] * slacks + st.y_g))
+        return conv, eq, ineq, gb
+
+    def _build_kkt_state(self, states, controls, st: ADMMState, g, l, u) -> KKTState:
+        """turbompc_solver.py:1387-1439."""
+        y_f = torch.cat([st.y_f_0[:, None, :], st.y_f_dyn], 1)
+        y_ineq = st.y_g
+        slack = st.xi_g
+        a = self._params["admm"]
+        if self._program.use_slack_variables:
+            lo, up = slack > 1e-12, slack < -1e-12
+        else:
+            pl, pu = identify_active_inequalities(g, l, u, a["eps_abs"], a["eps_rel"])
+            tol = a["eps_abs"]
+            dl, du = y_ineq < -tol, y_ineq > tol
+            und = ~(dl | du)
+            lo, up = dl | (und & pl), du | (und & pu)
+        return KKTState(states, controls, slack, y_f, y_ineq, lo, up)
+
+    # --------------------------------------------------------------- solve
+    def _solve_impl(self, states, controls, params, admm_state0: Optional[ADMMState] = None) -> TurboMPCSolution:
+        """SQP loop (turbompc_solver.py:1519-1760)."""
+        max_iter = int(self._params["num_sqp_iteration_max"])
+        tol = float(self._params["tol_convergence"])
+        crit = self._params.get("convergence_criterion", "first_order")
+        Nb = states.shape[0]
+        dev, dt = states.device, states.dtype
+        qp = self._build_qp_data(states, controls, params)
+        cfg = self._admm_cfg
+        if admm_state0 is None:
+            admm_state0 = ops.admm_initial_state(qp, self._params["admm"]["rho"])
+        st = admm_state0
+        slacks = st.xi_g
+        z_prev = torch.cat([states, controls], -1)
+        conv = torch.full((Nb,), float("inf"), dtype=dt, device=dev)
+        it_count = torch.zeros(Nb, dtype=torch.int64, device=dev)
+        admm_iters = torch.zeros(Nb, max_iter, dtype=torch.int64, device=dev)
+        eqv = torch.zeros(Nb, max_iter, dtype=dt, device=dev)
+        inv = torch.zeros(Nb, max_iter, dtype=dt, device=dev)
+        cerr = torch.zeros(Nb, max_iter, dtype=dt, device=dev)
+        active = torch.ones(Nb, dtype=torch.bool, device=dev)
+        nx = self._program.num_state_variables
+        kkt = None
+        sw = qp.ineq.slack_penalization_weight
+        for k in range(max_iter):
+            if k > 0 and tol > 0 and not bool(active.any()):
+                break
+            st_new, iters, status = ops.admm_solve(qp, st, cfg, slack_weight=sw, workspace=self._workspace)
+            xb = st_new.x_blocks
+            s_new, c_new = xb[..., :nx], xb[..., nx:]
+            sl_new = st_new.xi_g
+            z_new = torch.cat([s_new, c_new], -1)
+            step = _inf(z_new - z_prev)
+            if sl_new.shape[-1] > 0:
+                step = step + _inf(sl_new - slacks)
+            if crit == "first_order":
+                if k + 1 < max_iter:
+                    qp_next = self._build_qp_data(s_new, c_new, params)
+                    cv, ev, iv, g = self._first_order_error(qp_next, s_new, c_new, sl_new, st_new)
+                else:
+                    qp_next = qp
+                    cv = step if k == 0 else conv
+                    ev = iv = torch.zeros_like(cv)
+                    g = torch.einsum("btki,bti->btk", qp.ineq.G, z_new)
+                    if qp.ineq.use_slack_variables:
+                        g = g + sl_new
+            else:
+                qp_next = self._build_qp_data(s_new, c_new, params) if k + 1 < max_iter else qp
+                cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), torch.einsum(
+                    "btki,bti->btk", qp_next.ineq.G, z_new)
+            kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
+            # Masked update (problems already converged keep their iterate).
+            a3 = active[:, None, None]
+            sel = lambda new, old: torch.where(active.view(-1, *([1] * (new.dim() - 1))), new, old)
+            states, controls, slacks = sel(s_new, states), sel(c_new, controls), sel(sl_new, slacks)
+            st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
+            kkt = kkt_new if kkt is None else KKTState(*(sel(n_, o_) for n_, o_ in zip(kkt_new, kkt)))
+            z_prev = sel(z_new, z_prev)
+            admm_iters[:, k] = torch.where(active, iters, admm_iters[:, k])
+            eqv[:, k], inv[:, k], cerr[:, k] = ev, iv, cv
+            conv = sel(cv, conv)
+            it_count = it_count + active.to(torch.int64)
+            if k + 1 < max_iter:
+                qp = qp_next if bool(active.all()) else QPData(*[type(f)(*[
+                    sel(a_, b_) if isinstance(a_, torch.Tensor) and a_.dim() > 0 else a_
+                    for a_, b_ in zip(vars(f).values(), vars(g_).values())]) for f, g_ in zip(
+                        (qp_next.cost, qp_next.eq, qp_next.ineq), (qp.cost, qp.eq, qp.ineq))])
+            active = active & (conv > tol)
+            del a3
+        return TurboMPCSolution(states=states, controls=controls, slack=st.xi_g, status=self.STATUS_SUCCESS,
+                                num_iter=it_count, convergence_error=conv, admm_iters=admm_iters, admm_state=st,
+                                solver_stats=SolverStats(admm_iters, eqv, inv, cerr), kkt_state=kkt)
