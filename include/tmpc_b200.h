@@ -38,6 +38,7 @@ extern "C" {
 #define TMPC_ERR_UNSUPPORTED (-3)
 #define TMPC_ERR_WORKSPACE (-4)
 #define TMPC_ERR_SMEM (-5)
+#define TMPC_ERR_SCRATCH_LIMIT (-6) /* needs more scratch than the fixed device buffer holds */
 
 /* Per-problem status bits written by solves (status_out[b]). */
 #define TMPC_STATUS_SINGULAR_BLOCK 1 /* a Theta_t / Cholesky / LU pivot was zero or not finite */
@@ -180,6 +181,27 @@ int32_t tmpc_admm_solve_f64(const TmpcDims* dims, const TmpcQP* qp, const TmpcAd
                             const TmpcAdmmConfig* cfg, double* x_out, uint32_t* iters_out,
                             int32_t* status_out, void* workspace, size_t workspace_bytes,
                             tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused ADMM solve that allocates nothing.  No counterpart in the reference:
+ * an addition for callers that cannot allocate device memory (a runtime that
+ * owns all allocations, a handler that may only touch the buffers it is
+ * handed, an embedded controller with a fixed memory plan).  Same arguments
+ * and results as tmpc_admm_solve_f64 without the workspace: when the
+ * operators do not fit in shared memory they go to a statically allocated
+ * device buffer of 64 MiB that every GPU
+ * loading the library holds until process exit.  Batches needing more
+ * return TMPC_ERR_SCRATCH_LIMIT without launching.  The first call on a
+ * device looks up the buffer's device address (make it before any stream
+ * capture).  All calls share the buffer: calls that can overlap on the GPU
+ * (different streams, or different host threads, on one device) race and
+ * must be serialised by the caller.
+ * ------------------------------------------------------------------------- */
+int32_t tmpc_admm_solve_fixed_scratch_f64(const TmpcDims* dims, const TmpcQP* qp,
+                                          const TmpcAdmmState* state_in, const TmpcAdmmState* state_out,
+                                          const double* slack_weight, const TmpcAdmmConfig* cfg,
+                                          double* x_out, uint32_t* iters_out, int32_t* status_out,
+                                          tmpc_stream_t stream);
 
 #ifdef __cplusplus
 }

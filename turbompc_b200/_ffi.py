@@ -47,6 +47,10 @@ _SIGS = {
     "tmpc_error_string": (C.c_char_p, [C.c_int32]),
     "tmpc_packed_operator_bytes": (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32]),
     "tmpc_admm_workspace_bytes": (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32, C.POINTER(TmpcAdmmConfig)]),
+    "tmpc_admm_solve_fixed_scratch_f64": (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP),
+                                                      C.POINTER(TmpcAdmmState), C.POINTER(TmpcAdmmState), C.c_void_p,
+                                                      C.POINTER(TmpcAdmmConfig), C.c_void_p, C.c_void_p, C.c_void_p,
+                                                      C.c_void_p]),
 }
 for _s in ("f32", "f64"):
     _SIGS[f"tmpc_schur_assemble_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, C.c_double,

@@ -54,6 +54,11 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
   });
 }
 
+template int admm_solve<double>(const TmpcDims*, const TmpcQP*, const TmpcAdmmState*, const TmpcAdmmState*,
+                                const double*, const TmpcAdmmConfig*, double*, uint32_t*, int32_t*, void*, size_t,
+                                cudaStream_t);
+template size_t admm_ws_bytes<double>(const TmpcDims&);
+
 }  // namespace tmpc
 
 extern "C" {

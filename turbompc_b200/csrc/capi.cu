@@ -33,6 +33,9 @@ const char* tmpc_error_string(int32_t code) {
     case TMPC_ERR_UNSUPPORTED: return "unsupported configuration (block size n > 32 or unknown option)";
     case TMPC_ERR_WORKSPACE: return "workspace missing or too small";
     case TMPC_ERR_SMEM: return "problem does not fit the shared-memory budget of one CTA";
+    case TMPC_ERR_SCRATCH_LIMIT:
+      return "batch needs more scratch than the fixed device buffer of tmpc_admm_solve_fixed_scratch_f64 holds "
+             "(64 MiB); split the batch or use tmpc_admm_solve_f64 with a workspace";
   }
   if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
   return "unknown error";
