@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   R* vbase = sm + L.vec0;
   BlockVecs<NB, R> w{vbase,          vbase + VS,     vbase + 2 * VS,
                      vbase + 3 * VS, vbase + 4 * VS, vbase + 5 * VS,
-                     {vbase + 6 * VS, vbase + 7 * VS, vbase + 8 * VS, vbase + 9 * VS}};
+                     vbase + 6 * VS, (int)VS};
   R* gam = vbase + 10 * VS;
   R* xold = vbase + 11 * VS;
   R* yf0 = sm + L.yf0;

@@ -24,6 +24,10 @@
 
 namespace tmpc {
 
+// On-chip block vectors (each T*VSTR elements) of one problem.  The four
+// partial buffers up0..up3 are contiguous and selected by pointer arithmetic:
+// indexing an array of pointers with a runtime index would force the struct
+// into local memory.
 template <int NB, typename R>
 struct BlockVecs {
   R* x;
@@ -32,7 +36,9 @@ struct BlockVecs {
   R* p;
   R* d;
   R* lo;
-  R* up[4];
+  R* up0;  // up_q = up0 + q * vs
+  int vs;
+  __device__ R* up(int q) const { return up0 + q * vs; }
 };
 
 template <int NB, bool OPS_SMEM, typename R>
@@ -127,7 +133,7 @@ __device__ __forceinline__ void matvec_partials(const R* op, int T, const R* v, 
       const int q = k / N;  // consecutive threads take consecutive blocks of the same quarter
       const int t = k - q * N;
       quarter_task<NB, OPS_SMEM>(L + (size_t)t * Gm::OSTR, v + t * Gm::VSTR, v + (t + 1) * Gm::VSTR,
-                                 w.lo + (t + 1) * Gm::VSTR, w.up[q] + t * Gm::VSTR, q);
+                                 w.lo + (t + 1) * Gm::VSTR, w.up(q) + t * Gm::VSTR, q);
     }
   }
 }
@@ -143,7 +149,7 @@ __device__ __forceinline__ void gather_y(R* y, const BlockVecs<NB, R>& w, int o)
   for (int k = 0; k < VEC; ++k) y[k] += a[k];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    ld128(b, w.up[q] + o);
+    ld128(b, w.up(q) + o);
 #pragma unroll
     for (int k = 0; k < VEC; ++k) y[k] += b[k];
   }

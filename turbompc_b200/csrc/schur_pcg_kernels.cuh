@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) pcg_packed_kernel(const R
   }
   const size_t VS = (size_t)T * Gm::VSTR;
   BlockVecs<NB, R> w{vb, vb + VS, vb + 2 * VS, vb + 3 * VS, vb + 4 * VS, vb + 5 * VS,
-                     {vb + 6 * VS, vb + 7 * VS, vb + 8 * VS, vb + 9 * VS}};
+                     vb + 6 * VS, (int)VS};
   R* g = vb + 10 * VS;
   R* red = vb + 11 * VS;
   for (size_t e = threadIdx.x; e < 11 * VS; e += blockDim.x) vb[e] = R(0);
