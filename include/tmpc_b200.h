@@ -183,6 +183,25 @@ int32_t tmpc_admm_solve_f64(const TmpcDims* dims, const TmpcQP* qp, const TmpcAd
                             tmpc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Batched block-tridiagonal Cholesky (block Riccati recursion) of the
+ * reference-layout S, written from scratch; replaces the cuDSS direct solve
+ * `cudss_blktridi_cuda[_f64]` (linear_systems_solvers/csrc/cudss_ffi.cc:76-98,
+ * cudss_blktridi.cu:60-184).  The factor occupies
+ * tmpc_riccati_factor_bytes(dims, dtype_bytes) bytes (caller-owned);
+ * status_out[b] = TMPC_STATUS_SINGULAR_BLOCK when S is not positive definite.
+ * dims->nx, n0 and m are not used.
+ * ------------------------------------------------------------------------- */
+size_t tmpc_riccati_factor_bytes(const TmpcDims* dims, int32_t dtype_bytes);
+int32_t tmpc_riccati_factor_f32(const TmpcDims* dims, const float* S, void* factor,
+                                int32_t* status_out, tmpc_stream_t stream);
+int32_t tmpc_riccati_factor_f64(const TmpcDims* dims, const double* S, void* factor,
+                                int32_t* status_out, tmpc_stream_t stream);
+int32_t tmpc_riccati_solve_f32(const TmpcDims* dims, const void* factor, const float* rhs,
+                               float* x_out, tmpc_stream_t stream);
+int32_t tmpc_riccati_solve_f64(const TmpcDims* dims, const void* factor, const double* rhs,
+                               double* x_out, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Fused ADMM solve that allocates nothing.  No counterpart in the reference:
  * an addition for callers that cannot allocate device memory (a runtime that
  * owns all allocations, a handler that may only touch the buffers it is

@@ -27,7 +27,7 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
                const R* slack_weight, const TmpcAdmmConfig* cfg, R* x_out, uint32_t* iters_out, int32_t* status_out,
                void* ws, size_t ws_bytes, cudaStream_t st);  // admm_fused.cu
 template <typename R>
-size_t admm_ws_bytes(const TmpcDims& d);                   // admm_fused.cu
+size_t admm_ws_bytes_cfg(const TmpcDims& d, const TmpcAdmmConfig* cfg);  // admm_fused.cu
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -61,7 +61,7 @@ extern "C" int32_t tmpc_admm_solve_fixed_scratch_f64(const TmpcDims* dims, const
                                                      tmpc_stream_t stream) {
   int rc = tmpc::check_dims(dims);
   if (rc) return rc;
-  const size_t need = tmpc::admm_ws_bytes<double>(*dims);
+  const size_t need = tmpc::admm_ws_bytes_cfg<double>(*dims, cfg);
   if (need > tmpc::kTmpcFixedScratchBytes) return TMPC_ERR_SCRATCH_LIMIT;
   void* ws = nullptr;
   if (need > 0) {

@@ -16,6 +16,19 @@ size_t admm_ws_bytes(const TmpcDims& d) {
   return out;
 }
 
+// Workspace for cfg: the direct solve always keeps its factor in HBM.
+template <typename R>
+size_t admm_ws_bytes_cfg(const TmpcDims& d, const TmpcAdmmConfig* cfg) {
+  if (!cfg || cfg->linsys != TMPC_LINSYS_DIRECT) return admm_ws_bytes<R>(d);
+  size_t out = 0;
+  dispatch_nb(d.n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    out = (size_t)d.Nb * Geo<NB, R>::op_elems(d.T) * sizeof(R);
+    return 0;
+  });
+  return out;
+}
+
 template <typename R>
 int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, const TmpcAdmmState* out,
                const R* slack_weight, const TmpcAdmmConfig* cfg, R* x_out, uint32_t* iters_out, int32_t* status_out,
@@ -31,7 +44,7 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
     return TMPC_ERR_NULL_ARG;
   if (!in->x || !in->y_fdyn || !in->rho_bar || !out->x || !out->y_fdyn || !out->rho_bar) return TMPC_ERR_NULL_ARG;
   if (d->n0 > 0 && (!in->y_f0 || !out->y_f0)) return TMPC_ERR_NULL_ARG;
-  if (cfg->linsys != TMPC_LINSYS_PCG) return TMPC_ERR_UNSUPPORTED;
+  if (cfg->linsys != TMPC_LINSYS_PCG && cfg->linsys != TMPC_LINSYS_DIRECT) return TMPC_ERR_UNSUPPORTED;
   if (d->Nb == 0) return TMPC_OK;
   AdmmParams<R> P;
   P.qp = *qp;
@@ -50,6 +63,7 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
   P.adapt_tol = (R)cfg->adaptive_rho_tolerance; P.rho_min = (R)cfg->rho_min; P.rho_max = (R)cfg->rho_max;
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
+    if (cfg->linsys == TMPC_LINSYS_DIRECT) return launch_admm_direct_nb<NB, R>(P, ws_bytes, st);
     return launch_admm_nb<NB, R>(P, ws_bytes, st);
   });
 }
@@ -58,15 +72,15 @@ template int admm_solve<double>(const TmpcDims*, const TmpcQP*, const TmpcAdmmSt
                                 const double*, const TmpcAdmmConfig*, double*, uint32_t*, int32_t*, void*, size_t,
                                 cudaStream_t);
 template size_t admm_ws_bytes<double>(const TmpcDims&);
+template size_t admm_ws_bytes_cfg<double>(const TmpcDims&, const TmpcAdmmConfig*);
 
 }  // namespace tmpc
 
 extern "C" {
 
 size_t tmpc_admm_workspace_bytes(const TmpcDims* dims, int32_t dtype_bytes, const TmpcAdmmConfig* cfg) {
-  (void)cfg;
   if (tmpc::check_dims(dims)) return 0;
-  return dtype_bytes == 8 ? tmpc::admm_ws_bytes<double>(*dims) : tmpc::admm_ws_bytes<float>(*dims);
+  return dtype_bytes == 8 ? tmpc::admm_ws_bytes_cfg<double>(*dims, cfg) : tmpc::admm_ws_bytes_cfg<float>(*dims, cfg);
 }
 
 int32_t tmpc_admm_solve_f32(const TmpcDims* dims, const TmpcQP* qp, const TmpcAdmmState* state_in,

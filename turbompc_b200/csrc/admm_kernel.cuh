@@ -15,6 +15,7 @@
 #pragma once
 #include "assemble.cuh"
 #include "pcg_core.cuh"
+#include "riccati.cuh"
 #include "launchers.cuh"
 #include "tmpc_common.cuh"
 
@@ -24,8 +25,8 @@ namespace tmpc {
 // Element offsets inside the dynamic shared-memory arena.
 template <int NB, typename R>
 struct AdmmSmem {
-  size_t opS, opP, vec0, yf0, yfd, zg, yg, xig, cx0, cx, gx, ct, gt, red, nelem;
-  __host__ __device__ AdmmSmem(int T, int nx, int n0, int m, bool ops_smem) {
+  size_t opS, opP, vec0, yf0, yfd, zg, yg, xig, cx0, cx, gx, ct, gt, red, fm, nelem;
+  __host__ __device__ AdmmSmem(int T, int nx, int n0, int m, bool ops_smem, int nvec = 12) {
     using Gm = Geo<NB, R>;
     const int N = T - 1;
     auto a4 = [](size_t v) { return (v + 3) & ~size_t(3); };  // 16-byte alignment for both precisions
@@ -36,7 +37,7 @@ struct AdmmSmem {
     opP = o;
     if (ops_smem) o += opn;
     vec0 = o;
-    o += 12 * (size_t)T * Gm::VSTR;  // x r z p d lo up0..up3 gam xold
+    o += (size_t)nvec * T * Gm::VSTR;  // PCG: x r z p d lo up0..3 gam xold; direct: x y gam xold
     yf0 = a4(o); o = yf0 + n0;
     yfd = a4(o); o = yfd + (size_t)N * nx;
     zg = a4(o); o = zg + (size_t)T * m;
@@ -48,6 +49,7 @@ struct AdmmSmem {
     ct = a4(o); o = ct + n0 + (size_t)N * nx;
     gt = a4(o); o = gt + (size_t)T * m;
     red = a4(o); o = red + 64 + 16;
+    fm = a4(o); o = fm + (nvec == 4 ? (size_t)NB * (NB + 1) : 0);  // Cholesky scratch (direct)
     nelem = a4(o);
   }
 };
@@ -217,7 +219,10 @@ __device__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const 
   __syncthreads();
 }
 
-template <int NB, typename R, bool OPS_SMEM>
+// LINSYS: TMPC_LINSYS_PCG (operators on chip or in the workspace, one CTA per
+// problem) or TMPC_LINSYS_DIRECT (block Cholesky factor in the workspace, one
+// warp = one CTA per problem; requires OPS_SMEM == false).
+template <int NB, typename R, bool OPS_SMEM, int LINSYS = TMPC_LINSYS_PCG>
 __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const AdmmParams<R> P) {
   using Gm = Geo<NB, R>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -225,17 +230,20 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   const int b = blockIdx.x;
   if (b >= P.Nb) return;
   const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
-  const AdmmSmem<NB, R> L(T, nx, n0, m, OPS_SMEM);
+  constexpr bool DIRECT = LINSYS == TMPC_LINSYS_DIRECT;
+  constexpr int NVEC = DIRECT ? 4 : 12;
+  const AdmmSmem<NB, R> L(T, nx, n0, m, OPS_SMEM, NVEC);
   const size_t opn = Gm::op_elems(T);
-  R* opS = OPS_SMEM ? sm + L.opS : P.ws + (size_t)b * 2 * opn;
-  R* opP = OPS_SMEM ? sm + L.opP : P.ws + (size_t)b * 2 * opn + opn;
+  R* opS = OPS_SMEM ? sm + L.opS : P.ws + (size_t)b * (DIRECT ? 1 : 2) * opn;
+  R* opP = DIRECT ? nullptr : (OPS_SMEM ? sm + L.opP : P.ws + (size_t)b * 2 * opn + opn);
   const size_t VS = (size_t)T * Gm::VSTR;
   R* vbase = sm + L.vec0;
   BlockVecs<NB, R> w{vbase,          vbase + VS,     vbase + 2 * VS,
                      vbase + 3 * VS, vbase + 4 * VS, vbase + 5 * VS,
                      vbase + 6 * VS, (int)VS};
-  R* gam = vbase + 10 * VS;
-  R* xold = vbase + 11 * VS;
+  R* gam = vbase + (DIRECT ? 2 : 10) * VS;
+  R* xold = vbase + (DIRECT ? 3 : 11) * VS;
+  R* ysolve = vbase + VS;  // direct solve scratch (aliases w.r, unused then)
   R* yf0 = sm + L.yf0;
   R* yfd = sm + L.yfd;
   R* zg = sm + L.zg;
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   const QPView<R> qp = qp_view<R>(P.qp, b, T, n, nx, n0, m);
 
   // ---- load the warm-start state; zero all block vectors (keeps padding 0)
-  for (size_t e = threadIdx.x; e < 12 * VS; e += blockDim.x) vbase[e] = R(0);
+  for (size_t e = threadIdx.x; e < NVEC * VS; e += blockDim.x) vbase[e] = R(0);
   __syncthreads();
   {
     const R* x_in = static_cast<const R*>(P.in.x) + (size_t)b * T * n;
@@ -284,7 +292,19 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   const R al = P.alpha;
   const PackedAcc<NB, R> acc{opS, opP, T};
 
-  assemble_ops<NB>(acc, qp, rho * P.rho_f_factor, rho, P.sigma, T, n, nx, n0, m, &flag);
+  const FactorView<NB, R> F{opS, T};
+  auto build_operators = [&](R rho_now) {
+    if constexpr (DIRECT) {
+      assemble_theta_phi<NB>(acc, qp, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m);
+      __syncthreads();
+      if (!riccati_factor_warp<NB>(F, sm + L.fm, n) && threadIdx.x == 0)
+        flag |= TMPC_STATUS_SINGULAR_BLOCK;
+      __syncthreads();
+    } else {
+      assemble_ops<NB>(acc, qp, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m, &flag);
+    }
+  };
+  build_operators(rho);
 
   uint32_t iters = (uint32_t)P.max_iter;
   for (int it = 0; it < P.max_iter; ++it) {
@@ -298,7 +318,12 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
     compute_gamma<NB>(gam, w.x, qp, ct, gt, P.sigma, T, n, nx, n0, m);
     TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { xold[o] = w.x[o]; }
     __syncthreads();
-    pcg_solve<NB, OPS_SMEM>(opS, opP, T, gam, w, red, P.pcg_max_iter, P.pcg_eps);
+    if constexpr (DIRECT) {
+      riccati_solve_warp<NB>(F, gam, ysolve, w.x);
+      __syncthreads();
+    } else {
+      pcg_solve<NB, OPS_SMEM>(opS, opP, T, gam, w, red, P.pcg_max_iter, P.pcg_eps);
+    }
     apply_constraints<NB>(cx0, cx, gx, w.x, qp, T, n, nx, n0, m);
     __syncthreads();
     TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { w.x[o] = al * w.x[o] + (R(1) - al) * xold[o]; }
@@ -344,7 +369,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
         if (ratio < R(1)) ratio = R(1) / ratio;
         if (ratio >= P.adapt_tol) {
           rho = cand;
-          assemble_ops<NB>(acc, qp, rho * P.rho_f_factor, rho, P.sigma, T, n, nx, n0, m, &flag);
+          build_operators(rho);
         }
       }
       __syncthreads();
@@ -393,6 +418,19 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
 template <int NB, typename R>
 size_t admm_smem_bytes(int T, int nx, int n0, int m, bool ops_smem) {
   return AdmmSmem<NB, R>(T, nx, n0, m, ops_smem).nelem * sizeof(R);
+}
+
+template <int NB, typename R>
+int launch_admm_direct_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st) {
+  const size_t need = (size_t)P.Nb * Geo<NB, R>::op_elems(P.T) * sizeof(R);
+  if (P.ws == nullptr || ws_bytes < need) return TMPC_ERR_WORKSPACE;
+  const size_t smem = AdmmSmem<NB, R>(P.T, P.nx, P.n0, P.m, false, 4).nelem * sizeof(R);
+  if ((long)smem > max_dyn_smem()) return TMPC_ERR_SMEM;
+  auto k = admm_fused_kernel<NB, R, false, TMPC_LINSYS_DIRECT>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return (int)e;
+  k<<<P.Nb, 32, smem, st>>>(P);
+  return (int)cudaPeekAtLastError();
 }
 
 template <int NB, typename R>

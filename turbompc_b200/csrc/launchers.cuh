@@ -11,6 +11,8 @@ template <typename R>
 struct AdmmParams;
 
 template <int NB, typename R>
+int launch_admm_direct_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st);
+template <int NB, typename R>
 int launch_admm_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st);
 template <int NB, typename R>
 size_t admm_smem_bytes(int T, int nx, int n0, int m, bool ops_smem);

@@ -1,0 +1,141 @@
+// Standalone batched block-tridiagonal Cholesky factor / solve entry points
+// (the direct linear-system backend; replaces cudss_blktridi_cuda,
+// turbompc/solvers/linear_systems_solvers/csrc/cudss_ffi.cc:76-98).
+#include "riccati.cuh"
+#include "tmpc_common.cuh"
+
+namespace tmpc {
+
+constexpr int kRicWarps = 4;
+
+// Copy Theta_t / Phi_t out of the reference-layout S into the packed factor
+// slots, then factor.  One warp per problem.
+template <int NB, typename R>
+__global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R* __restrict__ S, R* factor,
+                                                                        int32_t* status, int Nb, int T, int n) {
+  using Gm = Geo<NB, R>;
+  __shared__ R Msh[kRicWarps][NB * (NB + 1)];
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * kRicWarps + wid;
+  if (b >= Nb) return;
+  const size_t opn = Gm::op_elems(T);
+  const FactorView<NB, R> F{factor + (size_t)b * opn, T};
+  const R* Sb = S + (size_t)b * T * n * 3 * n;
+  for (int t = 0; t < T; ++t) {
+    R* th = F.lt(t);
+    for (int e = lane; e < Gm::DSTR; e += 32) {
+      R v = R(0);
+      if (e < Gm::TRI) {
+        const int i = tri_row(e, NB), j = tri_col(e, NB);
+        if (i < n && j < n) v = Sb[((size_t)t * n + i) * 3 * n + n + j];
+      }
+      th[e] = v;
+    }
+    if (t + 1 < T) {
+      R* W = F.w(t);
+      for (int e = lane; e < NB * NB; e += 32) {
+        const int i = e / NB, j = e - i * NB;
+        W[e] = (i < n && j < n) ? Sb[((size_t)(t + 1) * n + i) * 3 * n + j] : R(0);  // S(t+1, t) = Phi_t
+      }
+    }
+  }
+  __syncwarp();
+  const bool ok = riccati_factor_warp<NB>(F, Msh[wid], n);
+  if (lane == 0 && status) status[b] = ok ? 0 : TMPC_STATUS_SINGULAR_BLOCK;
+}
+
+// One warp per problem; b / y / x staged in shared memory as [T][VSTR].
+template <int NB, typename R>
+__global__ void __launch_bounds__(32) riccati_solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs,
+                                                           R* x_out, int Nb, int T, int n) {
+  using Gm = Geo<NB, R>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  R* sm = reinterpret_cast<R*>(smem_raw);
+  const int b = blockIdx.x;
+  if (b >= Nb) return;
+  const size_t VS = (size_t)T * Gm::VSTR;
+  R* bb = sm;
+  R* y = sm + VS;
+  R* x = sm + 2 * VS;
+  for (size_t e = threadIdx.x; e < 3 * VS; e += 32) sm[e] = R(0);
+  __syncwarp();
+  for (int e = threadIdx.x; e < T * n; e += 32) {
+    const int t = e / n, j = e - t * n;
+    bb[t * Gm::VSTR + j] = rhs[(size_t)b * T * n + e];
+  }
+  __syncwarp();
+  const FactorView<NB, R> F{const_cast<R*>(factor) + (size_t)b * Gm::op_elems(T), T};
+  riccati_solve_warp<NB>(F, bb, y, x);
+  for (int e = threadIdx.x; e < T * n; e += 32) {
+    const int t = e / n, j = e - t * n;
+    x_out[(size_t)b * T * n + e] = x[t * Gm::VSTR + j];
+  }
+}
+
+template <typename R>
+int riccati_factor(const TmpcDims* d, const R* S, void* factor, int32_t* status, cudaStream_t st) {
+  if (!d) return TMPC_ERR_NULL_ARG;
+  if (d->Nb < 0 || d->T < 2 || d->n < 1) return TMPC_ERR_BAD_DIMS;
+  if (d->Nb == 0) return TMPC_OK;
+  if (!S || !factor) return TMPC_ERR_NULL_ARG;
+  return dispatch_nb(d->n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    const int grid = (d->Nb + kRicWarps - 1) / kRicWarps;
+    riccati_factor_kernel<NB, R><<<grid, 32 * kRicWarps, 0, st>>>(S, static_cast<R*>(factor), status, d->Nb, d->T,
+                                                                   d->n);
+    return (int)cudaPeekAtLastError();
+  });
+}
+
+template <typename R>
+int riccati_solve(const TmpcDims* d, const void* factor, const R* rhs, R* x, cudaStream_t st) {
+  if (!d) return TMPC_ERR_NULL_ARG;
+  if (d->Nb < 0 || d->T < 2 || d->n < 1) return TMPC_ERR_BAD_DIMS;
+  if (d->Nb == 0) return TMPC_OK;
+  if (!factor || !rhs || !x) return TMPC_ERR_NULL_ARG;
+  return dispatch_nb(d->n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    const size_t smem = 3 * (size_t)d->T * Geo<NB, R>::VSTR * sizeof(R);
+    if ((long)smem > max_dyn_smem()) return (int)TMPC_ERR_SMEM;
+    auto k = riccati_solve_kernel<NB, R>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    k<<<d->Nb, 32, smem, st>>>(static_cast<const R*>(factor), rhs, x, d->Nb, d->T, d->n);
+    return (int)cudaPeekAtLastError();
+  });
+}
+
+}  // namespace tmpc
+
+extern "C" {
+
+size_t tmpc_riccati_factor_bytes(const TmpcDims* d, int32_t dtype_bytes) {
+  if (!d || d->Nb < 0 || d->T < 2 || d->n < 1) return 0;
+  size_t out = 0;
+  tmpc::dispatch_nb(d->n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    out = dtype_bytes == 8 ? (size_t)d->Nb * tmpc::Geo<NB, double>::op_elems(d->T) * sizeof(double)
+                           : (size_t)d->Nb * tmpc::Geo<NB, float>::op_elems(d->T) * sizeof(float);
+    return 0;
+  });
+  return out;
+}
+
+int32_t tmpc_riccati_factor_f32(const TmpcDims* dims, const float* S, void* factor, int32_t* status_out,
+                                tmpc_stream_t stream) {
+  return tmpc::riccati_factor<float>(dims, S, factor, status_out, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_factor_f64(const TmpcDims* dims, const double* S, void* factor, int32_t* status_out,
+                                tmpc_stream_t stream) {
+  return tmpc::riccati_factor<double>(dims, S, factor, status_out, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_solve_f32(const TmpcDims* dims, const void* factor, const float* rhs, float* x_out,
+                               tmpc_stream_t stream) {
+  return tmpc::riccati_solve<float>(dims, factor, rhs, x_out, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_solve_f64(const TmpcDims* dims, const void* factor, const double* rhs, double* x_out,
+                               tmpc_stream_t stream) {
+  return tmpc::riccati_solve<double>(dims, factor, rhs, x_out, (cudaStream_t)stream);
+}
+
+}  // extern "C"

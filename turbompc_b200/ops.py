@@ -215,3 +215,30 @@ def admm_initial_state(qp: QPData, rho_bar, x0: Optional[torch.Tensor] = None) -
     z = torch.minimum(torch.maximum(torch.einsum("btmn,btn->btm", qp.ineq.G, x), qp.ineq.l), qp.ineq.u)
     return ADMMState(x, torch.zeros_like(z), torch.zeros_like(qp.eq.c0), torch.zeros_like(qp.eq.c),
                      z.contiguous(), torch.zeros_like(z), _rho_vec(rho_bar, qp).clone())
+
+
+def riccati_factor(S: torch.Tensor):
+    """Block Cholesky of reference-layout S (Nb, T, n, 3n).  Returns
+    (factor uint8 tensor, status int32 (Nb,))."""
+    lib = _ffi.load()
+    B, T, n = S.shape[:3]
+    d = _ffi.TmpcDims(B, T, n, n, 0, 0)
+    nbytes = lib.tmpc_riccati_factor_bytes(C.byref(d), S.dtype.itemsize)
+    if nbytes == 0 and B > 0:
+        raise ValueError(f"unsupported dimensions for the block Cholesky (n={n})")
+    fac = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=S.device)
+    st = torch.zeros(B, dtype=torch.int32, device=S.device)
+    name = f"tmpc_riccati_factor_{_suffix(S.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), _ptr(S), fac.data_ptr(), _ptr(st), _stream(S.device)))
+    return fac, st
+
+
+def riccati_solve(factor: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """Solve S x = rhs (rhs (Nb, T, n)) with a factor from riccati_factor."""
+    lib = _ffi.load()
+    B, T, n = rhs.shape
+    d = _ffi.TmpcDims(B, T, n, n, 0, 0)
+    x = torch.empty_like(rhs)
+    name = f"tmpc_riccati_solve_{_suffix(rhs.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), factor.data_ptr(), _ptr(rhs), _ptr(x), _stream(rhs.device)))
+    return x
