@@ -202,6 +202,27 @@ int32_t tmpc_riccati_solve_f64(const TmpcDims* dims, const void* factor, const d
                                double* x_out, tmpc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Adjoint KKT solve of the backward pass.  Replaces the dense solve
+ * solve_backward_kkt (turbompc/solvers/backward/backward_kkt_jax.py:177-211)
+ * and the `cudss_sparse_kkt_f32/f64` target
+ * (backward/backward_kkt_cudss_ffi.py:210-224): solves
+ *     [P  C^T] [dz]   [-q]
+ *     [C  R  ] [mu] = [ 0]
+ * with C = [A0; A_minus/A_plus rows; G rows], R = -1e-12 on all-zero G rows.
+ * The QP's G holds the active rows (sign * G, zero rows inactive); c0, c, l,
+ * u are not read.  dz_out [Nb, T, n]; mult_out [Nb, n0 + N*nx + T*m] in the
+ * reference order (A0 rows, dynamics rows, inequality rows).  The caller
+ * provides tmpc_adjoint_kkt_workspace_bytes() bytes of workspace.
+ * ------------------------------------------------------------------------- */
+size_t tmpc_adjoint_kkt_workspace_bytes(const TmpcDims* dims, int32_t dtype_bytes);
+int32_t tmpc_adjoint_kkt_solve_f32(const TmpcDims* dims, const TmpcQP* qp, float* dz_out,
+                                   float* mult_out, int32_t* status_out, void* workspace,
+                                   size_t workspace_bytes, tmpc_stream_t stream);
+int32_t tmpc_adjoint_kkt_solve_f64(const TmpcDims* dims, const TmpcQP* qp, double* dz_out,
+                                   double* mult_out, int32_t* status_out, void* workspace,
+                                   size_t workspace_bytes, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Fused ADMM solve that allocates nothing.  No counterpart in the reference:
  * an addition for callers that cannot allocate device memory (a runtime that
  * owns all allocations, a handler that may only touch the buffers it is

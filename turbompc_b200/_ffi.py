@@ -53,9 +53,12 @@ _SIGS = {
                                                       C.c_void_p]),
 }
 _SIGS["tmpc_riccati_factor_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
+_SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 for _s in ("f32", "f64"):
     _SIGS[f"tmpc_riccati_factor_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_riccati_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
+    _SIGS[f"tmpc_adjoint_kkt_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, _P, _P, _P,
+                                                          C.c_size_t, _P])
     _SIGS[f"tmpc_schur_assemble_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, C.c_double,
                                                       C.c_double, _P, _P, _P, _P])
     _SIGS[f"tmpc_schur_assemble_packed_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P,

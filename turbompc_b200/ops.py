@@ -242,3 +242,22 @@ def riccati_solve(factor: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
     name = f"tmpc_riccati_solve_{_suffix(rhs.dtype)}"
     _ffi.check(name, getattr(lib, name)(C.byref(d), factor.data_ptr(), _ptr(rhs), _ptr(x), _stream(rhs.device)))
     return x
+
+
+def adjoint_kkt_solve(qp: QPData, workspace: Optional[torch.Tensor] = None):
+    """Adjoint KKT solve (backward_kkt_jax.py:177-211) on the GPU.  qp.ineq.G
+    holds the active rows (sign * G, zero rows inactive).  Returns
+    (dz (Nb, T, n), multipliers (Nb, n0 + N*nx + T*m), status)."""
+    lib = _ffi.load()
+    d, q = dims_of(qp), _qp_c(qp)
+    B, T, n, nx, n0, m = qp.Nb, qp.T, qp.n, qp.nx, qp.n0, qp.m
+    dz = torch.empty(B, T, n, dtype=qp.dtype, device=qp.device)
+    mult = torch.empty(B, n0 + (T - 1) * nx + T * m, dtype=qp.dtype, device=qp.device)
+    st = torch.zeros(B, dtype=torch.int32, device=qp.device)
+    need = int(lib.tmpc_adjoint_kkt_workspace_bytes(C.byref(d), qp.dtype.itemsize))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=qp.device)
+    name = f"tmpc_adjoint_kkt_solve_{_suffix(qp.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), _ptr(dz), _ptr(mult), _ptr(st), workspace.data_ptr(),
+                                        need, _stream(qp.device)))
+    return dz, mult, st
