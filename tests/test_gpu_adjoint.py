@@ -19,6 +19,9 @@ def _backward_blocks(nx, nu, N, m, seed, active_frac=0.4):
     if m:
         sign = rng.choice([-1.0, 0.0, 1.0], size=b["G"].shape[:3], p=[active_frac / 2, 1 - active_frac, active_frac / 2])
         b["G"] = b["G"] * sign[..., None]
+        # x0 is fixed by the A0 rows; active rows at t = 0 on top of them would
+        # violate LICQ (singular KKT, non-unique multipliers).
+        b["G"][:, 0] = 0.0
     return b
 
 
