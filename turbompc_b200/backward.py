@@ -1,11 +1,162 @@
-"""Differentiable solve (the role of jax.custom_vjp in
-turbompc/solvers/turbompc_solver.py:1020-1096)."""
+"""Differentiable solve: the role of jax.custom_vjp in
+turbompc/solvers/turbompc_solver.py:1020-1096.
+
+Forward: the SQP solve.  Backward (turbompc_solver.py:1052-1093):
+  1. backward QP at the solution (turbompc_solver.py:544-618): cost/dynamics
+     blocks at (states, controls), optionally D += lambda^T Hess f + mu^T Hess g
+     (use_full_hessian), c0 = c = 0, G_active = (lower - upper) * G,
+     q = -[dL/dstates, dL/dcontrols];
+  2. the adjoint KKT solve on the GPU (tmpc_adjoint_kkt_solve_*) -> dz,
+     equality multipliers y_eq_lin, inequality multipliers y_ineq_lin;
+  3. mixed derivatives (turbompc_solver.py:781-966):
+       dL/dtheta = -d/dtheta [ grad_z(f + y_eq*.g + y_ineq*.h) . dz
+                               + g . y_eq_lin + h . y_ineq_lin ]
+     with y_eq* / y_ineq* the forward multipliers (y_ineq* = -(lower - upper) y_g),
+     g the equality constraints and h = lower (g - l) + upper (u - g) the active
+     inequalities, evaluated by PyTorch autograd at the solution.
+theta ranges over the tensors in ``weights`` (and ``initial_state``) that
+require grad; the initial-state cotangent equals the x0-row multipliers.
+"""
 from __future__ import annotations
+
+from typing import Any, Dict, List, Tuple
+
+import torch
+
+from . import ops
+from .qp_data import QPCostBlocks, QPData, QPEqualityBlocks, QPInequalityBlocks
+
+
+def _leaves(weights: Dict[str, Any], params: Dict[str, Any]) -> List[Tuple[Tuple[str, ...], torch.Tensor]]:
+    out = []
+
+    def walk(prefix, d):
+        for k, v in d.items():
+            if isinstance(v, dict):
+                walk(prefix + (k,), v)
+            elif isinstance(v, torch.Tensor) and v.requires_grad:
+                out.append((prefix + (k,), v))
+
+    walk((), weights or {})
+    x0 = params.get("initial_state")
+    if isinstance(x0, torch.Tensor) and x0.requires_grad and ("initial_state",) not in [p for p, _ in out]:
+        out.append((("initial_state",), x0))
+    return out
+
+
+def _replace(params: Dict[str, Any], path: Tuple[str, ...], value) -> Dict[str, Any]:
+    p = dict(params)
+    if len(path) == 1:
+        p[path[0]] = value
+    else:
+        p[path[0]] = _replace(dict(p.get(path[0]) or {}), path[1:], value)
+    return p
+
+
+def _detach_params(params):
+    out = {}
+    for k, v in params.items():
+        if isinstance(v, dict):
+            out[k] = _detach_params(v)
+        elif isinstance(v, torch.Tensor):
+            out[k] = v.detach()
+        else:
+            out[k] = v
+    return out
+
+
+def backward_qp(solver, sol, params, dl_dstates, dl_dcontrols) -> QPData:
+    """turbompc_solver.py:544-618 (hard inequalities)."""
+    prog = solver.program
+    kkt = sol.kkt_state
+    qp = solver._build_qp_data(kkt.states, kkt.controls, params)
+    D = qp.cost.D
+    if solver._use_full_hessian:
+        D = D + prog.get_dynamics_lagrangian_hessian(kkt.states, kkt.controls, params, sol.admm_state.y_f_dyn)
+        if qp.m > 0:
+            active = (kkt.ineq_active_lower_idx | kkt.ineq_active_upper_idx).to(D.dtype)
+            D = D + prog.get_inequality_lagrangian_hessian(kkt.states, kkt.controls, params,
+                                                           active * sol.admm_state.y_g)
+    sign = kkt.ineq_active_lower_idx.to(D.dtype) - kkt.ineq_active_upper_idx.to(D.dtype)
+    G = (qp.ineq.G * sign[..., None]).contiguous()
+    q = -torch.cat([dl_dstates, dl_dcontrols], -1).to(D.dtype).contiguous()
+    return QPData(QPCostBlocks(D.contiguous(), qp.cost.E, q),
+                  QPEqualityBlocks(qp.eq.A0, qp.eq.A_minus, qp.eq.A_plus, torch.zeros_like(qp.eq.c0),
+                                   torch.zeros_like(qp.eq.c)),
+                  QPInequalityBlocks(G, torch.zeros_like(qp.ineq.l), torch.zeros_like(qp.ineq.u),
+                                     qp.ineq.slack_penalization_weight, False))
+
+
+class _SolveFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, solver, sol, params, paths, *leaf_values):
+        ctx.solver, ctx.sol, ctx.params, ctx.paths = solver, sol, params, paths
+        ctx.saved_leaf_values = [v.detach() for v in leaf_values]
+        return sol.states.clone(), sol.controls.clone(), sol.slack.clone()
+
+    @staticmethod
+    def backward(ctx, g_states, g_controls, g_slack):
+        solver, sol, params, paths = ctx.solver, ctx.sol, ctx.params, ctx.paths
+        prog = solver.program
+        if prog.use_slack_variables:
+            raise NotImplementedError("gradients through soft (slack) constraints are not on the b200 path yet")
+        kkt = sol.kkt_state
+        dt = sol.states.dtype
+        if g_states is None:
+            g_states = torch.zeros_like(sol.states)
+        if g_controls is None:
+            g_controls = torch.zeros_like(sol.controls)
+        with torch.no_grad():
+            bq = backward_qp(solver, sol, params, g_states.to(dt), g_controls.to(dt))
+            dz, mult, status = ops.adjoint_kkt_solve(bq)
+        nx = prog.num_state_variables
+        Nb, T, m = sol.states.shape[0], sol.states.shape[1], bq.m
+        n_eq = bq.n0 + (T - 1) * nx
+        y_eq_lin = mult[:, :n_eq]
+        y_ineq_lin = mult[:, n_eq:].reshape(Nb, T, m)
+        st = sol.admm_state
+        y_eq_star = torch.cat([st.y_f_0, st.y_f_dyn.reshape(Nb, -1)], 1)
+        sign = kkt.ineq_active_lower_idx.to(dt) - kkt.ineq_active_upper_idx.to(dt)
+        y_ineq_star = -sign * st.y_g
+        lo_m, up_m = kkt.ineq_active_lower_idx.to(dt), kkt.ineq_active_upper_idx.to(dt)
+
+        with torch.enable_grad():
+            leaves = [torch.nn.Parameter(v.detach().clone()) for v in ctx.saved_leaf_values]
+            p = params
+            for path, leaf in zip(paths, leaves):
+                p = _replace(p, path, leaf)
+            xs = kkt.states.detach().clone().requires_grad_(True)
+            us = kkt.controls.detach().clone().requires_grad_(True)
+
+            def h_fn(x, u):
+                g, l, uu = prog.inequality_values(x, u, p)
+                return lo_m * (g - l) + up_m * (uu - g)
+
+            F = prog.cost(xs, us, p).sum() + (y_eq_star * prog.equality_constraints(xs, us, p)).sum()
+            if m > 0:
+                F = F + (y_ineq_star * h_fn(xs, us)).sum()
+            gx, gu = torch.autograd.grad(F, (xs, us), create_graph=True)
+            phi = (gx * dz[..., :nx]).sum() + (gu * dz[..., nx:]).sum()
+            phi = phi + (prog.equality_constraints(xs, us, p) * y_eq_lin).sum()
+            if m > 0:
+                phi = phi + (h_fn(xs, us) * y_ineq_lin).sum()
+            grads = torch.autograd.grad(phi, leaves, allow_unused=True)
+        out = [None if g is None else -g for g in grads]
+        return (None, None, None, None, *out)
 
 
 def make_differentiable_solve(solver):
     def solve(initial_guess, problem_params, weights=None):
         params = solver.make_params_with_weights(weights or {}, problem_params)
-        return solver._solve_impl(initial_guess.states, initial_guess.controls, params, initial_guess.admm_state)
+        leaves = _leaves(weights or {}, params) if torch.is_grad_enabled() else []
+        pdet = _detach_params(params)
+        sol = solver._solve_impl(initial_guess.states.detach(), initial_guess.controls.detach(), pdet,
+                                 initial_guess.admm_state)
+        if not leaves:
+            return sol
+        paths = [p for p, _ in leaves]
+        vals = [v for _, v in leaves]
+        states, controls, slack = _SolveFn.apply(solver, sol, pdet, paths, *vals)
+        return sol._replace(states=states, controls=controls, slack=slack)
 
     return solve

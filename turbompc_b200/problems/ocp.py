@@ -279,6 +279,83 @@ class OptimalControlProblem:
     def _extra_inequalities_linearized(self, states, controls, params):
         return None
 
+    # ------------------------------------- nonlinear constraint functions (backward)
+    def equality_constraints(self, states, controls, params):
+        """[x_0 - initial_state, f(x_t, u_t) - x_{t+1}] flattened per problem,
+        (Nb, n0 + N*nx) (optimal_control_problem.py:841-912, explicit schemes);
+        its Jacobian is the QP's [A0; A_minus/A_plus] rows."""
+        x0c = states[:, 0] - _t(params["initial_state"], states)
+        dyn = self.next_states(states, controls, params) - states[:, 1:]
+        return torch.cat([x0c, dyn.reshape(states.shape[0], -1)], dim=1)
+
+    def inequality_values(self, states, controls, params):
+        """Nonlinear g(x, u) with its bounds, each (Nb, T, m), in the row order of
+        get_inequalities_linearized_matrices."""
+        Nb, T, _ = states.shape
+        z = torch.cat([states, controls], -1)
+        nx = self.num_state_variables
+        sm, cm = self._state_mask.to(states.device), self._control_mask.to(states.device)
+        g = torch.cat([states[..., sm], controls[..., cm]], -1)
+        lo, hi = self._box(params, states, Nb, T)
+        extra = self._extra_inequality_values(states, controls, params)
+        if extra is not None:
+            g = torch.cat([g, extra[0]], -1)
+            lo = torch.cat([lo, extra[1]], -1)
+            hi = torch.cat([hi, extra[2]], -1)
+        del z, nx
+        return g, lo, hi
+
+    def _extra_inequality_values(self, states, controls, params):
+        return None
+
+    def _stagewise_hessian(self, fn, z):
+        """Per-stage Hessians of sum(fn(z)) where fn is separable over (Nb, T):
+        z (Nb, T', n) -> (Nb, T', n, n), one forward-over-reverse pass per
+        column (the stage blocks are independent, so one tangent serves all)."""
+        n = z.shape[-1]
+
+        def grad_fn(zz):
+            with torch.enable_grad():
+                zz = zz.detach().requires_grad_(True) if not zz.requires_grad else zz
+                return torch.autograd.grad(fn(zz).sum(), zz, create_graph=True)[0]
+
+        cols = []
+        for k in range(n):
+            v = torch.zeros_like(z)
+            v[..., k] = 1.0
+            _, hv = torch.func.jvp(lambda zz: torch.func.grad(lambda q: fn(q).sum())(zz), (z,), (v,))
+            cols.append(hv)
+        del grad_fn
+        return torch.stack(cols, dim=-1)
+
+    def get_dynamics_lagrangian_hessian(self, states, controls, params, lambdas):
+        """sum_i lambda_{t,i} Hess_{(x,u)} [f(x_t, u_t)]_i for t < N, zero at N
+        (optimal_control_problem.py:1334-1442, explicit schemes)."""
+        nx = self.num_state_variables
+        N = self.horizon
+        dt = float(params["discretization_resolution"])
+        dp = self._dyn_params(params, states)
+        lam = lambdas.detach()
+
+        def fn(zz):
+            return (lam * predict_next_state(self._dynamics, dt, self._scheme, dp, zz[..., :nx], zz[..., nx:])).sum(-1)
+
+        z = torch.cat([states[:, :N], controls[:, :N]], -1).detach()
+        H = self._stagewise_hessian(fn, z)
+        return torch.cat([H, torch.zeros_like(H[:, :1])], dim=1)
+
+    def get_inequality_lagrangian_hessian(self, states, controls, params, mus):
+        """sum_i mu_{t,i} Hess_{(x,u)} g_i(x_t, u_t) (optimal_control_problem.py:1444-1481)."""
+        nx = self.num_state_variables
+        mu = mus.detach()
+
+        def fn(zz):
+            g, _, _ = self.inequality_values(zz[..., :nx], zz[..., nx:], params)
+            return (mu * g).sum(-1)
+
+        z = torch.cat([states, controls], -1).detach()
+        return self._stagewise_hessian(fn, z)
+
     def get_initial_equality_linearized_matrices(self, params, like):
         """A0 = [I 0], c0 = initial_state (optimal_control_problem.py:914-980)."""
         nx, nu = self.num_state_variables, self.num_control_variables
@@ -296,6 +373,14 @@ class OptimalControlProblemObstacle(OptimalControlProblem):
 
     def _num_extra_inequalities(self) -> int:
         return int(torch.as_tensor(self._params["obstacles_radii"]).shape[-1])
+
+    def _extra_inequality_values(self, states, controls, params):
+        dim = int(params["obstacles_dimension"])
+        c = _t(params["obstacles_centers"], states)
+        r = _t(params["obstacles_radii"], states)
+        diff = states[..., :dim][:, :, None, :] - c[:, None, :, :]
+        g = 1.0 - diff.norm(dim=-1) / (r[:, None, :] + 0.001)
+        return g, torch.full_like(g, -1e9), torch.zeros_like(g)
 
     def _extra_inequalities_linearized(self, states, controls, params):
         dim = int(params["obstacles_dimension"])
