@@ -175,7 +175,10 @@ def main():
     import torch
 
     from turbompc_b200 import _ffi, ops
-    from turbompc_b200.problems.quadrotor import make_quadrotor_problem
+    from turbompc_b200.dynamics import Quadrotor12Dynamics
+    from turbompc_b200.problems.ocp import OptimalControlProblem
+    from turbompc_b200.problems.quadrotor import quadrotor_params
+    from turbompc_b200.sharding import gather_batch, shard_params, shard_range
     from turbompc_b200.solver import TurboMPCSolver
 
     torch.cuda.set_device(local)
@@ -186,9 +189,12 @@ def main():
 
         dist.init_process_group("nccl", device_id=dev)
     _ffi.load(build_if_missing=False)
-    shard = args.batch // world
-    lo = rank * shard
-    ocp, params = make_quadrotor_problem(shard, N=N_HORIZON, seed=1000 + rank, dtype=torch.float32, device=dev)
+    lo, hi = shard_range(args.batch, world, rank)
+    shard = hi - lo
+    full = quadrotor_params(args.batch, N=N_HORIZON, seed=1000, dtype=torch.float32, device="cpu")
+    params = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v)
+              for k, v in shard_params(full, args.batch, lo, hi).items()}
+    ocp = OptimalControlProblem(Quadrotor12Dynamics(), params)
     sp = {"num_sqp_iteration_max": SQP, "tol_convergence": 0.0,
           "admm": {"max_iter": ADMM, "check_termination_every": 0, "adapt_rho_every": 0, "eps_abs": 0.0,
                    "eps_rel": 0.0, "pcg": {"max_iter": PCG, "tol_epsilon": 0.0}}}
@@ -243,7 +249,7 @@ def main():
     # ---- end-to-end through the public API with host buffers
     x0_host = params["initial_state"].cpu().pin_memory()
     ref_host = params["reference_state_trajectory"].cpu().pin_memory()
-    u0_host = torch.empty(shard, 4, dtype=torch.float32).pin_memory()
+    u0_host = torch.empty(args.batch if rank == 0 else 1, 4, dtype=torch.float32).pin_memory()
     e2e_steps = max(1, args.steps)
     if dist:
         dist.barrier()
@@ -256,7 +262,11 @@ def main():
         p2["reference_state_trajectory"] = ref_host.to(dev, non_blocking=True)
         g2 = solver.initial_guess(p2)
         s2 = solver.solve(g2, p2)
-        u0_host.copy_(s2.controls[:, 0], non_blocking=True)
+        u0 = s2.controls[:, 0].contiguous()
+        if dist:
+            u0 = gather_batch(u0, args.batch)  # the only collective: the final gather
+        if rank == 0:
+            u0_host.copy_(u0, non_blocking=True)
     a1.record()
     torch.cuda.synchronize()
     e2e_ms = a0.elapsed_time(a1) / e2e_steps
@@ -265,7 +275,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = t.item()
     h2d = (x0_host.numel() + ref_host.numel()) * 4 * world
-    d2h = u0_host.numel() * 4 * world
+    d2h = args.batch * 4 * 4
 
     if rank == 0:
         qp = solver._build_qp_data(guess.states, guess.controls, params)
