@@ -156,6 +156,21 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def admm_only(nb):
+    import torch
+
+    from turbompc_b200 import ops
+    from turbompc_b200.problems import synthetic
+
+    b = synthetic.random_lti(nb, 12, 4, N_HORIZON, seed=0)
+    qd = synthetic.to_qpdata(b, dtype=torch.float32, device="cuda")
+    cfg = ops.AdmmConfig(max_iter=ADMM, pcg_max_iter=PCG, check_every=0, adapt_rho_every=0, eps_abs=0.0,
+                         eps_rel=0.0, pcg_eps=0.0)
+    out, it, st = ops.admm_solve(qd, ops.admm_initial_state(qd, 0.1), cfg)
+    torch.cuda.synchronize()
+    print(json.dumps({"admm_only": nb, "status_nonzero": int((st != 0).sum())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -164,7 +179,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--admm-only", type=int, default=0, metavar="NB",
+                    help="profiling aid: one fused ADMM launch (30 ADMM x 30 PCG, fp32) on NB quadrotor-shaped "
+                         "synthetic QPs, then exit")
     args = ap.parse_args()
+    if args.admm_only:
+        return admm_only(args.admm_only)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
