@@ -156,19 +156,31 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def admm_only(nb):
+def admm_only(nb, linsys="auto", reps=3, pcg=PCG):
+    """One warm-up and `reps` timed fused ADMM launches (30 ADMM x 30 PCG, fp32)
+    on nb quadrotor-shaped LTI QPs; prints ms per launch (CUDA events)."""
     import torch
 
-    from turbompc_b200 import ops
+    from turbompc_b200 import _ffi, ops
     from turbompc_b200.problems import synthetic
 
     b = synthetic.random_lti(nb, 12, 4, N_HORIZON, seed=0)
     qd = synthetic.to_qpdata(b, dtype=torch.float32, device="cuda")
-    cfg = ops.AdmmConfig(max_iter=ADMM, pcg_max_iter=PCG, check_every=0, adapt_rho_every=0, eps_abs=0.0,
-                         eps_rel=0.0, pcg_eps=0.0)
-    out, it, st = ops.admm_solve(qd, ops.admm_initial_state(qd, 0.1), cfg)
+    ls = _ffi.LINSYS_PCG if linsys == "auto" else _ffi.LINSYS_PCG_PACKED
+    cfg = ops.AdmmConfig(max_iter=ADMM, pcg_max_iter=pcg, check_every=0, adapt_rho_every=0, eps_abs=0.0,
+                         eps_rel=0.0, pcg_eps=0.0, linsys=ls)
+    s0 = ops.admm_initial_state(qd, 0.1)
+    out, it, st = ops.admm_solve(qd, s0, cfg)
     torch.cuda.synchronize()
-    print(json.dumps({"admm_only": nb, "status_nonzero": int((st != 0).sum())}))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ops.admm_solve(qd, s0, cfg, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    print(json.dumps({"admm_only": nb, "linsys": linsys, "pcg_iters": pcg, "ms_per_launch": round(ms, 3),
+                      "us_per_problem": round(1e3 * ms / nb, 3), "status_nonzero": int((st != 0).sum())}))
 
 
 def main():
@@ -182,9 +194,12 @@ def main():
     ap.add_argument("--admm-only", type=int, default=0, metavar="NB",
                     help="profiling aid: one fused ADMM launch (30 ADMM x 30 PCG, fp32) on NB quadrotor-shaped "
                          "synthetic QPs, then exit")
+    ap.add_argument("--admm-linsys", default="auto", choices=["auto", "packed"],
+                    help="with --admm-only: auto (register-resident kernel where it applies) or the packed kernel")
+    ap.add_argument("--admm-pcg", type=int, default=PCG, help="with --admm-only: PCG iterations per ADMM iteration")
     args = ap.parse_args()
     if args.admm_only:
-        return admm_only(args.admm_only)
+        return admm_only(args.admm_only, args.admm_linsys, pcg=args.admm_pcg)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

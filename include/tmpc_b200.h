@@ -84,6 +84,9 @@ typedef struct TmpcAdmmState {
 
 #define TMPC_LINSYS_PCG 0    /* preconditioned CG on the Schur system (admm_fused_pcg) */
 #define TMPC_LINSYS_DIRECT 1 /* block-tridiagonal Cholesky (replaces admm_fused_cudss) */
+/* PCG as TMPC_LINSYS_PCG, but always on the shared-memory packed-operator kernel
+ * (TMPC_LINSYS_PCG picks the register-resident kernel for fp32, 8 < n <= 16, T <= 52). */
+#define TMPC_LINSYS_PCG_PACKED 2
 
 /* Mirrors ADMMConfig (turbompc/solvers/admm/csrc/admm_fused.cuh:6-22). */
 typedef struct TmpcAdmmConfig {

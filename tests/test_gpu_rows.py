@@ -1,0 +1,120 @@
+"""GPU parity of the register-resident fused ADMM kernel (fp32, 8 < n <= 16,
+T <= 52; chosen automatically for TMPC_LINSYS_PCG) against the NumPy oracle,
+and against the shared-memory packed kernel (TMPC_LINSYS_PCG_PACKED).
+Tolerance: 1e-3 relative (||a-b||_inf / ||b||_inf), the fp32 bar."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import admm_ref as ref
+from tests.helpers import dense_blocks, oracle_qp, rel_err
+from turbompc_b200 import _ffi, ops
+from turbompc_b200.problems import synthetic
+
+pytestmark = pytest.mark.gpu
+
+FIXED = dict(max_iter=30, pcg_max_iter=30, check_every=0, adapt_rho_every=0, eps_abs=0.0, eps_rel=0.0,
+             pcg_eps=0.0, rho_f_factor=1000.0, alpha=1.6, sigma=1e-6)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _solve(blocks, cfg_kw, linsys=_ffi.LINSYS_PCG, slack=None, rho=0.1):
+    Nb = blocks["D"].shape[0]
+    sw = None if slack is None else np.full(Nb, slack)
+    qd = synthetic.to_qpdata(blocks, dtype=torch.float32, device="cuda", slack_weight=sw,
+                             use_slack=slack is not None)
+    cfg = ops.AdmmConfig(**cfg_kw, use_slack=slack is not None, linsys=linsys)
+    return ops.admm_solve(qd, ops.admm_initial_state(qd, rho), cfg, slack_weight=sw)
+
+
+def _oracle(blocks, cfg_kw, slack=None, rho=0.1):
+    Nb = blocks["D"].shape[0]
+    sw = None if slack is None else np.full(Nb, slack)
+    qo = oracle_qp(blocks, slack_weight=sw, use_slack=slack is not None)
+    return ref.admm_solve(qo, ref.initial_state(qo, rho), ref.ADMMConfig(**cfg_kw, use_slack=slack is not None))
+
+
+@pytest.mark.parametrize("nx,nu,N,m", [(12, 4, 50, 4),   # quadrotor shape (n = 16, T = 51)
+                                       (12, 4, 51, 4),   # T = 52: every thread owns a stage
+                                       (6, 3, 30, 3),    # n = 9: padded rows
+                                       (10, 2, 1, 2),    # T = 2
+                                       (8, 5, 17, 0),    # no inequalities
+                                       (11, 5, 40, 7)])
+def test_rows_kernel_matches_oracle(nx, nu, N, m):
+    b = dense_blocks(6, nx, nu, N, m, seed=100 + N + m)
+    out, iters, status = _solve(b, FIXED)
+    so, _ = _oracle(b, FIXED)
+    assert (_np(status) == 0).all()
+    assert (_np(iters) == FIXED["max_iter"]).all()
+    assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+    assert rel_err(_np(out.y_f_dyn), so.y_fdyn) < 1e-3
+    assert rel_err(_np(out.y_f_0), so.y_f0) < 1e-3
+    if m:
+        assert rel_err(_np(out.z_g), so.z_g) < 1e-3
+        assert rel_err(_np(out.y_g), so.y_g) < 1e-3
+
+
+def test_rows_kernel_lti_config_matches_packed_kernel():
+    """Quadrotor-sized LTI batch: register-resident and packed kernels agree to
+    fp32 rounding (and are different code paths: not bit-identical)."""
+    b = synthetic.random_lti(64, 12, 4, 50, seed=5)
+    a, _, sa = _solve(b, FIXED)
+    p, _, sp = _solve(b, FIXED, linsys=_ffi.LINSYS_PCG_PACKED)
+    so, _ = _oracle(b, FIXED)
+    assert (_np(sa) == 0).all() and (_np(sp) == 0).all()
+    assert rel_err(_np(a.x_blocks), _np(p.x_blocks)) < 1e-3
+    assert rel_err(_np(a.x_blocks), so.x) < 1e-3
+    assert not torch.equal(a.x_blocks, p.x_blocks)
+
+
+def test_rows_kernel_slack_residual_checks_and_rho_adaptation():
+    """Soft constraints, residual checks every 5 iterations and OSQP rho
+    updates with the on-chip rebuild of the register-resident operators (eps
+    small enough that no problem stops: the rho path is compared, not the stop
+    decision).  The rho rule rho * sqrt(p / d) amplifies the fp32 rounding of
+    the residual norms, so the bar is the packed fp32 kernel's own distance to
+    the fp64 oracle (or 1e-3, whichever is larger)."""
+    b = dense_blocks(6, 10, 4, 12, 3, seed=3)
+    kw = dict(max_iter=60, pcg_max_iter=6, check_every=5, adapt_rho_every=10, eps_abs=1e-9, eps_rel=1e-9,
+              pcg_eps=0.0, rho_f_factor=100.0, alpha=1.6, sigma=1e-6)
+    out, iters, status = _solve(b, kw, slack=10.0)
+    pk, _, _ = _solve(b, kw, slack=10.0, linsys=_ffi.LINSYS_PCG_PACKED)
+    so, io = _oracle(b, kw, slack=10.0)
+    assert (_np(status) == 0).all()
+    assert (io == 60).all() and (_np(iters) == 60).all()
+    assert (np.abs(so.rho - 0.1) > 1e-3).any(), "the case must exercise a rho update"
+    for got, pgot, want in ((out.rho_bar, pk.rho_bar, so.rho), (out.x_blocks, pk.x_blocks, so.x),
+                            (out.xi_g, pk.xi_g, so.xi_g)):
+        bar = max(1e-3, 2.0 * rel_err(_np(pgot), want))
+        assert rel_err(_np(got), want) < bar
+
+
+def test_rows_kernel_convergence_stop():
+    """Per-problem early termination at a residual check: the stop iteration
+    is within one check period of the fp64 oracle's (fp32 residual norms can
+    move a borderline check), and equal for most problems."""
+    b = synthetic.random_lti(8, 10, 4, 12, seed=3)
+    kw = dict(max_iter=200, pcg_max_iter=20, check_every=5, adapt_rho_every=0, eps_abs=1e-2, eps_rel=1e-2,
+              pcg_eps=0.0, rho_f_factor=100.0, alpha=1.6, sigma=1e-6)
+    out, iters, status = _solve(b, kw)
+    so, io = _oracle(b, kw)
+    it = _np(iters)
+    assert (_np(status) == 0).all()
+    assert (io < 200).all(), "every problem must stop early in the oracle"
+    assert (np.abs(it - io) <= 5).all()
+    same = it == io
+    assert same.sum() >= 6
+    assert rel_err(_np(out.x_blocks)[same], so.x[same]) < 1e-2
+
+
+def test_rows_kernel_pcg_early_stop():
+    """PCG tolerance > 0: the per-solve stop test |eta| < 1e-12 + eps |eta0|."""
+    b = dense_blocks(4, 12, 4, 20, 4, seed=9)
+    kw = dict(FIXED, max_iter=10, pcg_max_iter=50, pcg_eps=1e-4)
+    out, _, status = _solve(b, kw)
+    so, _ = _oracle(b, kw)
+    assert (_np(status) == 0).all()
+    assert rel_err(_np(out.x_blocks), so.x) < 1e-3

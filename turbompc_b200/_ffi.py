@@ -39,6 +39,7 @@ class TmpcAdmmConfig(C.Structure):
 
 LINSYS_PCG = 0
 LINSYS_DIRECT = 1
+LINSYS_PCG_PACKED = 2
 
 # name -> (restype, argtypes)
 _P = C.c_void_p

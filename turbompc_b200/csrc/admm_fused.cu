@@ -44,8 +44,8 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
     return TMPC_ERR_NULL_ARG;
   if (!in->x || !in->y_fdyn || !in->rho_bar || !out->x || !out->y_fdyn || !out->rho_bar) return TMPC_ERR_NULL_ARG;
   if (d->n0 > 0 && (!in->y_f0 || !out->y_f0)) return TMPC_ERR_NULL_ARG;
-  if (cfg->linsys != TMPC_LINSYS_PCG && cfg->linsys != TMPC_LINSYS_DIRECT) return TMPC_ERR_UNSUPPORTED;
-  if (d->Nb == 0) return TMPC_OK;
+  if (cfg->linsys != TMPC_LINSYS_PCG && cfg->linsys != TMPC_LINSYS_DIRECT && cfg->linsys != TMPC_LINSYS_PCG_PACKED)
+    return TMPC_ERR_UNSUPPORTED;
   AdmmParams<R> P;
   P.qp = *qp;
   P.in = *in;
@@ -61,6 +61,10 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
   P.eps_abs = (R)cfg->eps_abs; P.eps_rel = (R)cfg->eps_rel; P.sigma = (R)cfg->sigma;
   P.rho_f_factor = (R)cfg->rho_f_factor; P.alpha = (R)cfg->alpha; P.pcg_eps = (R)cfg->pcg_eps;
   P.adapt_tol = (R)cfg->adaptive_rho_tolerance; P.rho_min = (R)cfg->rho_min; P.rho_max = (R)cfg->rho_max;
+  if constexpr (std::is_same<R, float>::value) {
+    if (cfg->linsys == TMPC_LINSYS_PCG && admm_rows_ok(d->T, d->n, d->nx, d->n0, d->m))
+      return launch_admm_rows(P, st);
+  }
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
     if (cfg->linsys == TMPC_LINSYS_DIRECT) return launch_admm_direct_nb<NB, R>(P, ws_bytes, st);

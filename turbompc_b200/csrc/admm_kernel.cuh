@@ -66,25 +66,56 @@ __device__ void compute_gamma(R* gam, const R* x, const QPView<R>& qp, const R* 
     if (j < n) {
       val = sigma * x[o] - qp.q[t * n + j];
       R eq = R(0);
+      // Loops unrolled by 4 so that four independent global loads are in
+      // flight per thread (the QP blocks are read from L2 every iteration).
       if (t == 0) {
+#pragma unroll 4
         for (int k = 0; k < n0; ++k) eq += qp.A0[k * n + j] * ct[k];
-        if (N > 0)
+        if (N > 0) {
+#pragma unroll 4
           for (int k = 0; k < nx; ++k) eq += qp.Am[k * n + j] * ct[n0 + k];
+        }
       } else {
         const R* ap = qp.Ap + (size_t)(t - 1) * nx * n;
+#pragma unroll 4
         for (int k = 0; k < nx; ++k) eq += ap[k * n + j] * ct[n0 + (t - 1) * nx + k];
         if (t < N) {
           const R* am = qp.Am + (size_t)t * nx * n;
+#pragma unroll 4
           for (int k = 0; k < nx; ++k) eq += am[k * n + j] * ct[n0 + t * nx + k];
         }
       }
       val += eq;
       R iq = R(0);
+#pragma unroll 4
       for (int k = 0; k < m; ++k) iq += qp.G[((size_t)t * m + k) * n + j] * gt[t * m + k];
       val += iq;
     }
     gam[o] = val;
   }
+}
+
+// s += a . v over n entries: 128-bit loads of the global row a when n is a
+// multiple of the vector width and the row starts 16-byte aligned, else a
+// scalar loop unrolled by 4.  v is an on-chip block-vector row (aligned).
+template <typename R>
+__device__ __forceinline__ R row_dot(const R* __restrict__ a, const R* __restrict__ v, int n) {
+  constexpr int VEC = 16 / (int)sizeof(R);
+  R s = R(0);
+  if (n % VEC == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+#pragma unroll 4
+    for (int c = 0; c < n; c += VEC) {
+      R w[VEC], x[VEC];
+      ldg128(w, a + c);
+      ld128(x, v + c);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) s = fma(w[e], x[e], s);
+    }
+  } else {
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) s = fma(a[j], v[j], s);
+  }
+  return s;
 }
 
 // Cx0 = A0 x_0, Cx_t = Am_t x_t + Ap_t x_{t+1}, Gx_t = G_t x_t.
@@ -96,25 +127,15 @@ __device__ void apply_constraints(R* cx0, R* cx, R* gx, const R* x, const QPView
   const int tot = n0 + N * nx + T * m;
   for (int e = threadIdx.x; e < tot; e += blockDim.x) {
     if (e < n0) {
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += qp.A0[e * n + j] * x[j];
-      cx0[e] = s;
+      cx0[e] = row_dot(qp.A0 + (size_t)e * n, x, n);
     } else if (e < n0 + N * nx) {
       const int k = e - n0, t = k / nx, i = k - t * nx;
       const R* am = qp.Am + ((size_t)t * nx + i) * n;
       const R* ap = qp.Ap + ((size_t)t * nx + i) * n;
-      const R* xt = x + t * Gm::VSTR;
-      const R* xt1 = x + (t + 1) * Gm::VSTR;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += am[j] * xt[j] + ap[j] * xt1[j];
-      cx[k] = s;
+      cx[k] = row_dot(am, x + t * Gm::VSTR, n) + row_dot(ap, x + (t + 1) * Gm::VSTR, n);
     } else {
       const int k = e - n0 - N * nx, t = k / m, i = k - t * m;
-      const R* g = qp.G + ((size_t)t * m + i) * n;
-      const R* xt = x + t * Gm::VSTR;
-      R s = R(0);
-      for (int j = 0; j < n; ++j) s += g[j] * xt[j];
-      gx[k] = s;
+      gx[k] = row_dot(qp.G + ((size_t)t * m + i) * n, x + t * Gm::VSTR, n);
     }
   }
 }
@@ -219,6 +240,80 @@ __device__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const 
   __syncthreads();
 }
 
+// ct = rho_f c - y_f (equality rows, c0 first), gt = rho z_g - y_g.
+template <typename R>
+__device__ __forceinline__ void admm_targets(R* ct, R* gt, const QPView<R>& qp, const R* yf0, const R* yfd,
+                                             const R* zg, const R* yg, R rho, R rho_f, int T, int nx, int n0, int m) {
+  const int N = T - 1;
+  for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
+    if (e < n0) ct[e] = rho_f * qp.c0[e] - yf0[e];
+    else if (e < n0 + N * nx) ct[e] = rho_f * qp.c[e - n0] - yfd[e - n0];
+    else gt[e - n0 - N * nx] = rho * zg[e - n0 - N * nx] - yg[e - n0 - N * nx];
+  }
+}
+
+// Over-relaxation of x and the slack / dual updates (admm.py:884-930, in the
+// order of admm_fused.cu:760-860).  Caller syncs before and after.
+template <int NB, typename R>
+__device__ __forceinline__ void admm_relax_duals(R* x, const R* xold, R* yf0, R* yfd, R* zg, R* yg, R* xig,
+                                                 const R* cx0, const R* cx, const R* gx, const QPView<R>& qp, R rho,
+                                                 R rho_f, R al, R sw, bool use_slack, int T, int nx, int n0, int m) {
+  using Gm = Geo<NB, R>;
+  const int N = T - 1;
+  TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { x[o] = al * x[o] + (R(1) - al) * xold[o]; }
+  for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
+    if (e < n0) {
+      yf0[e] += rho_f * al * (cx0[e] - qp.c0[e]);
+    } else if (e < n0 + N * nx) {
+      const int k = e - n0;
+      yfd[k] += rho_f * al * (cx[k] - qp.c[k]);
+    } else {
+      const int k = e - n0 - N * nx;
+      const R zold = zg[k];
+      const R zt = al * gx[k] + (R(1) - al) * zold + yg[k] / rho;
+      R cl = zt;
+      const R lb = qp.l[k], ub = qp.u[k];
+      if (cl < lb) cl = lb;
+      if (cl > ub) cl = ub;
+      R znew;
+      if (use_slack) {
+        const R f = sw / (sw + rho);
+        znew = (R(1) - f) * zt + f * cl;
+        xig[k] = (rho / (sw + rho)) * (cl - zt);
+      } else {
+        znew = cl;
+      }
+      zg[k] = znew;
+      yg[k] += rho * (al * gx[k] + (R(1) - al) * zold - znew);
+    }
+  }
+}
+
+// Residual check every check_every iterations (admm.py:266-331 and the OSQP
+// rho rule of admm_fused.cu:870-925).  Returns 1 when converged, 2 when rho
+// should change to *rho_new, 0 otherwise.  All threads call it.
+template <int NB, typename R>
+__device__ __forceinline__ int admm_check(R* sc, R* red, const R* x, const R* zg, const R* yg, const R* xig,
+                                          const R* yf0, const R* yfd, const QPView<R>& qp, R sw,
+                                          const AdmmParams<R>& P, int it, R rho, R* rho_new, int T, int n, int nx,
+                                          int n0, int m) {
+  compute_residuals<NB>(sc, red, x, zg, yg, xig, yf0, yfd, qp, sw, P.use_slack != 0, T, n, nx, n0, m);
+  const bool conv = (sc[0] < P.eps_abs + P.eps_rel * sc[4]) && (sc[1] < P.eps_abs + P.eps_rel * sc[5]);
+  if (conv) return 1;
+  if (P.adapt_every > 0 && it >= 2 && (it % P.adapt_every) == 0) {
+    R cand = rho * sqrt(sc[2] / (sc[3] + R(1e-30)));
+    if (cand < P.rho_min) cand = P.rho_min;
+    if (cand > P.rho_max) cand = P.rho_max;
+    R ratio = cand / rho;
+    if (ratio < R(1)) ratio = R(1) / ratio;
+    if (ratio >= P.adapt_tol) {
+      *rho_new = cand;
+      return 2;
+    }
+  }
+  return 0;
+}
+
 // LINSYS: TMPC_LINSYS_PCG (operators on chip or in the workspace, one CTA per
 // problem) or TMPC_LINSYS_DIRECT (block Cholesky factor in the workspace, one
 // warp = one CTA per problem; requires OPS_SMEM == false).
@@ -309,11 +404,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   uint32_t iters = (uint32_t)P.max_iter;
   for (int it = 0; it < P.max_iter; ++it) {
     const R rho_f = rho * P.rho_f_factor;
-    for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
-      if (e < n0) ct[e] = rho_f * qp.c0[e] - yf0[e];
-      else if (e < n0 + N * nx) ct[e] = rho_f * qp.c[e - n0] - yfd[e - n0];
-      else gt[e - n0 - N * nx] = rho * zg[e - n0 - N * nx] - yg[e - n0 - N * nx];
-    }
+    admm_targets(ct, gt, qp, yf0, yfd, zg, yg, rho, rho_f, T, nx, n0, m);
     __syncthreads();
     compute_gamma<NB>(gam, w.x, qp, ct, gt, P.sigma, T, n, nx, n0, m);
     TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { xold[o] = w.x[o]; }
@@ -326,51 +417,19 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
     }
     apply_constraints<NB>(cx0, cx, gx, w.x, qp, T, n, nx, n0, m);
     __syncthreads();
-    TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { w.x[o] = al * w.x[o] + (R(1) - al) * xold[o]; }
-    for (int e = threadIdx.x; e < n0 + N * nx + T * m; e += blockDim.x) {
-      if (e < n0) {
-        yf0[e] += rho_f * al * (cx0[e] - qp.c0[e]);
-      } else if (e < n0 + N * nx) {
-        const int k = e - n0;
-        yfd[k] += rho_f * al * (cx[k] - qp.c[k]);
-      } else {
-        const int k = e - n0 - N * nx;
-        const R zold = zg[k];
-        const R zt = al * gx[k] + (R(1) - al) * zold + yg[k] / rho;
-        R cl = zt;
-        const R lb = qp.l[k], ub = qp.u[k];
-        if (cl < lb) cl = lb;
-        if (cl > ub) cl = ub;
-        R znew;
-        if (P.use_slack) {
-          const R f = sw / (sw + rho);
-          znew = (R(1) - f) * zt + f * cl;
-          xig[k] = (rho / (sw + rho)) * (cl - zt);
-        } else {
-          znew = cl;
-        }
-        zg[k] = znew;
-        yg[k] += rho * (al * gx[k] + (R(1) - al) * zold - znew);
-      }
-    }
+    admm_relax_duals<NB>(w.x, xold, yf0, yfd, zg, yg, xig, cx0, cx, gx, qp, rho, rho_f, al, sw, P.use_slack != 0, T,
+                         nx, n0, m);
     __syncthreads();
     if (P.check_every > 0 && (it % P.check_every) == 0) {
-      compute_residuals<NB>(sc, red, w.x, zg, yg, xig, yf0, yfd, qp, sw, P.use_slack != 0, T, n, nx, n0, m);
-      const bool conv = (sc[0] < P.eps_abs + P.eps_rel * sc[4]) && (sc[1] < P.eps_abs + P.eps_rel * sc[5]);
-      if (conv) {
+      R rho_new;
+      const int st = admm_check<NB>(sc, red, w.x, zg, yg, xig, yf0, yfd, qp, sw, P, it, rho, &rho_new, T, n, nx, n0, m);
+      if (st == 1) {
         iters = (uint32_t)(it + 1);
         break;
       }
-      if (P.adapt_every > 0 && it >= 2 && (it % P.adapt_every) == 0) {
-        R cand = rho * sqrt(sc[2] / (sc[3] + R(1e-30)));
-        if (cand < P.rho_min) cand = P.rho_min;
-        if (cand > P.rho_max) cand = P.rho_max;
-        R ratio = cand / rho;
-        if (ratio < R(1)) ratio = R(1) / ratio;
-        if (ratio >= P.adapt_tol) {
-          rho = cand;
-          build_operators(rho);
-        }
+      if (st == 2) {
+        rho = rho_new;
+        build_operators(rho);
       }
       __syncthreads();
     }

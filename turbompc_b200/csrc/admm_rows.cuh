@@ -1,0 +1,415 @@
+// Fused ADMM solve with register-resident operators: stage blocks of width 16
+// (n <= 16), fp32, horizons up to T = 52 (the quadrotor configuration has
+// n = 16, T = 51).
+//
+// Same algorithm and iteration order as admm_fused_kernel (admm_kernel.cuh);
+// only the linear-system layer differs.  Eight threads own one stage block t,
+// thread q owning rows q and q + 8, and keep in registers
+//   Theta_t^-1 rows        (16 + 16 values)
+//   S(t, t-1) = Phi_{t-1}  rows
+//   S(t, t+1) = Phi_t^T    rows (= columns of Phi_t)
+// so every product is a row-times-vector with the vector broadcast from
+// shared memory and every output row is produced by the thread that owns it:
+// no partial-sum buffers and no cross-thread reductions inside a matvec.
+// Only the diagonal blocks Theta_t of S stay in shared memory.
+//
+// The block-tridiagonal preconditioner of the reference (admm.py:123-153)
+//   Phiinv = blocktridiag(Theta_t^-1 Phi_{t-1} Theta_{t-1}^-1, -Theta_t^-1,
+//                         Theta_t^-1 Phi_t^T Theta_{t+1}^-1)
+// equals Dth (Phi_off - Theta) Dth with Dth = blockdiag(Theta_t^-1) and
+// Phi_off the off-diagonal part of S, so it is applied in factored form:
+//   w = Dth r ;  u = Phi_off w ;  z = Dth u - w
+// which needs no storage beyond S's blocks and Theta^-1 (the same operator up
+// to rounding; parity is checked at the fp32 tolerance).
+#pragma once
+
+#include "admm_kernel.cuh"
+
+namespace tmpc {
+
+struct RowsGeo {
+  static constexpr int NB = 16;
+  static constexpr int TPB = 8;           // threads per stage block
+  static constexpr int VSTR = 20;         // block-vector row stride (80 B: odd multiple of 16 B)
+  static constexpr int BSTR = 24;         // broadcast-buffer row stride: 8-word windows of 4 consecutive
+                                          // stages land on disjoint banks (24 t mod 32 = 0, 24, 16, 8)
+  static constexpr int TSTR = 20;         // row stride of a Theta block in shared memory
+  static constexpr int TBLK = 16 * TSTR;  // Theta block stride
+  static constexpr int SQ = 256;          // dense 16 x 16 scratch block
+  static constexpr int TMAX = 52;
+  static constexpr int MAX_THREADS = TPB * TMAX;  // 416
+  static constexpr int BUF = (TMAX + 3) * BSTR;   // one broadcast buffer (zero rows around the stages)
+};
+static_assert(Geo<16, float>::VSTR == RowsGeo::VSTR, "block-vector stride shared with the ADMM helpers");
+
+__host__ __device__ constexpr int rows_threads(int T) { return (T * RowsGeo::TPB + 31) / 32 * 32; }
+__host__ __device__ constexpr int rows_tpad(int T) { return rows_threads(T) / RowsGeo::TPB; }
+
+// Element offsets inside the dynamic shared-memory arena.  The four broadcast
+// buffers (p, w, r, u) have a zero row before stage 0 and zero rows after
+// stage T-1, so row index t + 1 holds stage t and neighbours need no bounds
+// tests.
+struct RowsSmem {
+  size_t th, phi, tinv, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0, cx, gx, ct, gt, red, nelem;
+  __host__ __device__ RowsSmem(int T, int nx, int n0, int m) {
+    using G = RowsGeo;
+    const int N = T - 1, TP = rows_tpad(T);
+    auto a4 = [](size_t v) { return (v + 3) & ~size_t(3); };
+    size_t o = 0;
+    th = o; o += (size_t)TP * G::TBLK;
+    phi = o; o += (size_t)(N > 0 ? N : 1) * G::SQ;
+    tinv = o; o += (size_t)T * G::SQ;
+    bb = o; o += 4 * (size_t)G::BUF;  // p, w, r, u broadcast buffers at constant offsets
+    x = o; o += (size_t)T * G::VSTR;
+    gam = o; o += (size_t)T * G::VSTR;
+    xold = o; o += (size_t)T * G::VSTR;
+    yf0 = a4(o); o = yf0 + n0;
+    yfd = a4(o); o = yfd + (size_t)N * nx;
+    zg = a4(o); o = zg + (size_t)T * m;
+    yg = a4(o); o = yg + (size_t)T * m;
+    xig = a4(o); o = xig + (size_t)T * m;
+    cx0 = a4(o); o = cx0 + n0;
+    cx = a4(o); o = cx + (size_t)N * nx;
+    gx = a4(o); o = gx + (size_t)T * m;
+    ct = a4(o); o = ct + n0 + (size_t)N * nx;
+    gt = a4(o); o = gt + (size_t)T * m;
+    red = a4(o); o = red + 64 + 16 + 32;  // block_max slots, residual scalars, 2 x 16 dot slots
+    nelem = a4(o);
+  }
+};
+
+// Assembly destination: Theta full (both triangles) with skewed rows, Phi and
+// -Theta^-1 as dense scratch blocks that are copied into registers.
+struct RowsAcc {
+  float* th;
+  float* phi;
+  float* tinv;
+  __device__ void set_theta(int t, int i, int j, float v) const {
+    th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j] = v;
+    th[t * RowsGeo::TBLK + j * RowsGeo::TSTR + i] = v;
+  }
+  __device__ float get_theta(int t, int i, int j) const { return th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j]; }
+  __device__ void set_phi(int t, int i, int j, float v) const { phi[t * RowsGeo::SQ + i * 16 + j] = v; }
+  __device__ void set_ntinv(int t, int i, int j, float v) const {
+    tinv[t * RowsGeo::SQ + i * 16 + j] = v;
+    tinv[t * RowsGeo::SQ + j * 16 + i] = v;
+  }
+};
+
+struct RowOps {
+  float ti[2][16];  // Theta_t^-1 rows q, q + 8
+  float lr[2][16];  // S(t, t-1) rows
+  float lc[2][16];  // S(t, t+1) rows
+};
+
+// Copies this thread's operator rows out of the assembly scratch.
+__device__ __forceinline__ void rows_load_ops(RowOps& o, const RowsAcc& acc, int t, int q, int T) {
+  const int N = T - 1;
+  const bool act = t < T, has_lo = act && t >= 1, has_up = t < N;
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    const int j = q + 8 * a;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f), w = v;
+      if (act) v = *reinterpret_cast<const float4*>(acc.tinv + t * RowsGeo::SQ + j * 16 + 4 * c);
+      if (has_lo) w = *reinterpret_cast<const float4*>(acc.phi + (t - 1) * RowsGeo::SQ + j * 16 + 4 * c);
+      o.ti[a][4 * c] = -v.x; o.ti[a][4 * c + 1] = -v.y; o.ti[a][4 * c + 2] = -v.z; o.ti[a][4 * c + 3] = -v.w;
+      o.lr[a][4 * c] = w.x; o.lr[a][4 * c + 1] = w.y; o.lr[a][4 * c + 2] = w.z; o.lr[a][4 * c + 3] = w.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) o.lc[a][k] = has_up ? acc.phi[t * RowsGeo::SQ + k * 16 + j] : 0.f;
+  }
+}
+
+// a_i += m_i . v for the two owned rows; v is a broadcast 16-vector in shared memory.
+__device__ __forceinline__ void rows_bdot(float& a0, float& a1, const float (&m0)[16], const float (&m1)[16],
+                                          const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 w = *reinterpret_cast<const float4*>(v + 4 * c);
+    a0 = fmaf(m0[4 * c], w.x, a0); a1 = fmaf(m1[4 * c], w.x, a1);
+    a0 = fmaf(m0[4 * c + 1], w.y, a0); a1 = fmaf(m1[4 * c + 1], w.y, a1);
+    a0 = fmaf(m0[4 * c + 2], w.z, a0); a1 = fmaf(m1[4 * c + 2], w.z, a1);
+    a0 = fmaf(m0[4 * c + 3], w.w, a0); a1 = fmaf(m1[4 * c + 3], w.w, a1);
+  }
+}
+
+// Same with the two matrix rows read from shared memory (Theta rows).
+__device__ __forceinline__ void rows_sdot(float& a0, float& a1, const float* r0, const float* r1, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 w = *reinterpret_cast<const float4*>(v + 4 * c);
+    const float4 m0 = *reinterpret_cast<const float4*>(r0 + 4 * c);
+    const float4 m1 = *reinterpret_cast<const float4*>(r1 + 4 * c);
+    a0 = fmaf(m0.x, w.x, a0); a1 = fmaf(m1.x, w.x, a1);
+    a0 = fmaf(m0.y, w.y, a0); a1 = fmaf(m1.y, w.y, a1);
+    a0 = fmaf(m0.z, w.z, a0); a1 = fmaf(m1.z, w.z, a1);
+    a0 = fmaf(m0.w, w.w, a0); a1 = fmaf(m1.w, w.w, a1);
+  }
+}
+
+// y = (S v) at the owned rows; vt points at row t of the buffer holding v
+// (row t + 1 is stage t).
+__device__ __forceinline__ void rows_smv(float (&y)[2], const RowOps& o, const float* th_row, const float* vt) {
+  float l0 = 0.f, l1 = 0.f, d0 = 0.f, d1 = 0.f, u0 = 0.f, u1 = 0.f;
+  rows_bdot(l0, l1, o.lr[0], o.lr[1], vt);
+  rows_sdot(d0, d1, th_row, th_row + 8 * RowsGeo::TSTR, vt + RowsGeo::BSTR);
+  rows_bdot(u0, u1, o.lc[0], o.lc[1], vt + 2 * RowsGeo::BSTR);
+  y[0] = (l0 + d0) + u0;
+  y[1] = (l1 + d1) + u1;
+}
+
+// z = Phiinv r in factored form.  bt points at row t (stage t - 1) of the p
+// buffer; the r, w, u buffers follow at constant offsets.  Contains one
+// __syncthreads (all threads call it).
+__device__ __forceinline__ void rows_prec(float (&z)[2], const float (&r)[2], const RowOps& o, float* bt, int q) {
+  constexpr int VS = RowsGeo::BSTR;
+  float* wb = bt + RowsGeo::BUF;      // row t of the w buffer
+  float* rrow = bt + 2 * RowsGeo::BUF + VS;
+  float* urow = bt + 3 * RowsGeo::BUF + VS;
+  rrow[q] = r[0];
+  rrow[q + 8] = r[1];
+  __syncwarp();  // the eight threads of a stage block share a warp
+  float w0 = 0.f, w1 = 0.f;
+  rows_bdot(w0, w1, o.ti[0], o.ti[1], rrow);
+  float* wrow = wb + VS;
+  wrow[q] = w0;
+  wrow[q + 8] = w1;
+  __syncthreads();
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  rows_bdot(a0, a1, o.lr[0], o.lr[1], wb);
+  rows_bdot(b0, b1, o.lc[0], o.lc[1], wb + 2 * VS);
+  urow[q] = a0 + b0;
+  urow[q + 8] = a1 + b1;
+  __syncwarp();
+  float v0 = 0.f, v1 = 0.f;
+  rows_bdot(v0, v1, o.ti[0], o.ti[1], urow);
+  z[0] = v0 - w0;
+  z[1] = v1 - w1;
+}
+
+// Deterministic block sum: warp sums into 16 slots (unused slots stay zero),
+// then every thread adds the slots in a fixed tree order from 4 vector loads.
+__device__ __forceinline__ float rows_block_sum(float v, float* slots) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) slots[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const float4 a = *reinterpret_cast<const float4*>(slots);
+  const float4 b = *reinterpret_cast<const float4*>(slots + 4);
+  const float4 c = *reinterpret_cast<const float4*>(slots + 8);
+  const float4 d = *reinterpret_cast<const float4*>(slots + 12);
+  return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
+         (((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w)));
+}
+
+// PCG with the stopping rule and recurrences of admm_fused.cu:54-161 (see
+// pcg_core.cuh).  xs / gam are [T][VSTR] block vectors in shared memory; x is
+// read from and written back to xs.  The operator rows are (re)loaded into
+// registers here, so they are live only inside the PCG loop.  Returns the
+// iteration count.
+__device__ __forceinline__ int rows_pcg(const RowsAcc& acc, float* bb, float* xs, const float* gam, int T,
+                                        int max_iter, float eps, float* slots) {
+  constexpr int VS = RowsGeo::VSTR;
+  const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
+  const bool act = t < T;
+  RowOps o;
+  rows_load_ops(o, acc, t, q, T);
+  const float* th_row = acc.th + t * RowsGeo::TBLK + q * RowsGeo::TSTR;
+  float* bt = bb + t * RowsGeo::BSTR;
+  float* prow = bt + RowsGeo::BSTR;
+  float x[2], r[2], p[2], z[2], y[2];
+  x[0] = act ? xs[t * VS + q] : 0.f;
+  x[1] = act ? xs[t * VS + q + 8] : 0.f;
+  prow[q] = x[0];
+  prow[q + 8] = x[1];
+  __syncthreads();
+  rows_smv(y, o, th_row, bt);
+  r[0] = (act ? gam[t * VS + q] : 0.f) - y[0];
+  r[1] = (act ? gam[t * VS + q + 8] : 0.f) - y[1];
+  rows_prec(z, r, o, bt, q);
+  p[0] = z[0];
+  p[1] = z[1];
+  float eta = rows_block_sum(fmaf(r[1], z[1], r[0] * z[0]), slots);
+  const float eta0 = fabsf(eta);
+  int it = 0;
+  for (; it < max_iter; ++it) {
+    if (fabsf(eta) < 1e-12f + eps * eta0) break;
+    prow[q] = p[0];
+    prow[q + 8] = p[1];
+    __syncthreads();
+    rows_smv(y, o, th_row, bt);
+    float den = rows_block_sum(fmaf(p[1], y[1], p[0] * y[0]), slots + 16);
+    if (fabsf(den) < 1e-30f) den = 1e-30f;
+    const float alpha = eta / den;
+    x[0] = fmaf(alpha, p[0], x[0]);
+    x[1] = fmaf(alpha, p[1], x[1]);
+    r[0] = fmaf(-alpha, y[0], r[0]);
+    r[1] = fmaf(-alpha, y[1], r[1]);
+    rows_prec(z, r, o, bt, q);
+    const float en = rows_block_sum(fmaf(r[1], z[1], r[0] * z[0]), slots);
+    const float beta = en / eta;
+    eta = en;
+    p[0] = fmaf(beta, p[0], z[0]);
+    p[1] = fmaf(beta, p[1], z[1]);
+  }
+  if (act) {
+    xs[t * VS + q] = x[0];
+    xs[t * VS + q + 8] = x[1];
+  }
+  __syncthreads();
+  return it;
+}
+
+__global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(const AdmmParams<float> P) {
+  using R = float;
+  constexpr int NB = 16;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  R* sm = reinterpret_cast<R*>(smem_raw);
+  const int b = blockIdx.x;
+  if (b >= P.Nb) return;
+  const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
+  const RowsSmem L(T, nx, n0, m);
+  const int TP = rows_tpad(T);
+  R* xs = sm + L.x;
+  R* gam = sm + L.gam;
+  R* xold = sm + L.xold;
+  R* yf0 = sm + L.yf0;
+  R* yfd = sm + L.yfd;
+  R* zg = sm + L.zg;
+  R* yg = sm + L.yg;
+  R* xig = sm + L.xig;
+  R* cx0 = sm + L.cx0;
+  R* cx = sm + L.cx;
+  R* gx = sm + L.gx;
+  R* ct = sm + L.ct;
+  R* gt = sm + L.gt;
+  R* red = sm + L.red;
+  R* sc = red + 64;
+  R* slots = red + 80;
+  const RowsAcc acc{sm + L.th, sm + L.phi, sm + L.tinv};
+  __shared__ int flag;
+  if (threadIdx.x == 0) flag = 0;
+
+  const QPView<R> qp = qp_view<R>(P.qp, b, T, n, nx, n0, m);
+
+  // ---- zero Theta (incl. the padding blocks) and every vector region; load the warm start
+  for (size_t e = threadIdx.x; e < (size_t)TP * RowsGeo::TBLK; e += blockDim.x) acc.th[e] = R(0);
+  for (size_t e = L.bb + threadIdx.x; e < L.yf0; e += blockDim.x) sm[e] = R(0);
+  for (int e = threadIdx.x; e < 32; e += blockDim.x) slots[e] = R(0);
+  __syncthreads();
+  {
+    const R* x_in = static_cast<const R*>(P.in.x) + (size_t)b * T * n;
+    for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
+      const int t = e / n, j = e - t * n;
+      xs[t * RowsGeo::VSTR + j] = x_in[e];
+    }
+    if (n0 > 0) {
+      const R* a = static_cast<const R*>(P.in.y_f0) + (size_t)b * n0;
+      for (int e = threadIdx.x; e < n0; e += blockDim.x) yf0[e] = a[e];
+    }
+    const R* a = static_cast<const R*>(P.in.y_fdyn) + (size_t)b * N * nx;
+    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) yfd[e] = a[e];
+    if (m > 0) {
+      const R* z = static_cast<const R*>(P.in.z_g) + (size_t)b * T * m;
+      const R* y = static_cast<const R*>(P.in.y_g) + (size_t)b * T * m;
+      const R* xi = static_cast<const R*>(P.in.xi_g) + (size_t)b * T * m;
+      for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
+        zg[e] = z[e];
+        yg[e] = y[e];
+        xig[e] = xi[e];
+      }
+    }
+  }
+  R rho = static_cast<const R*>(P.in.rho_bar)[b];
+  const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
+  const R al = P.alpha;
+
+  // Theta and Phi into shared memory and -Theta^-1 by warp Gauss-Jordan; the
+  // PCG copies its rows into registers.  Ends with a barrier.
+  auto build_operators = [&](R rho_now) {
+    assemble_theta_phi<NB>(acc, qp, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m);
+    __syncthreads();
+    invert_thetas<NB, R>(acc, T, n, &flag);
+    __syncthreads();
+  };
+  build_operators(rho);
+
+  uint32_t iters = (uint32_t)P.max_iter;
+  for (int it = 0; it < P.max_iter; ++it) {
+    const R rho_f = rho * P.rho_f_factor;
+    admm_targets(ct, gt, qp, yf0, yfd, zg, yg, rho, rho_f, T, nx, n0, m);
+    __syncthreads();
+    compute_gamma<NB>(gam, xs, qp, ct, gt, P.sigma, T, n, nx, n0, m);
+    TMPC_FOR_ENTRIES(e, o, T, NB, RowsGeo::VSTR) { xold[o] = xs[o]; }
+    __syncthreads();
+    rows_pcg(acc, sm + L.bb, xs, gam, T, P.pcg_max_iter, P.pcg_eps, slots);
+    apply_constraints<NB>(cx0, cx, gx, xs, qp, T, n, nx, n0, m);
+    __syncthreads();
+    admm_relax_duals<NB>(xs, xold, yf0, yfd, zg, yg, xig, cx0, cx, gx, qp, rho, rho_f, al, sw, P.use_slack != 0, T,
+                         nx, n0, m);
+    __syncthreads();
+    if (P.check_every > 0 && (it % P.check_every) == 0) {
+      R rho_new;
+      const int st = admm_check<NB>(sc, red, xs, zg, yg, xig, yf0, yfd, qp, sw, P, it, rho, &rho_new, T, n, nx, n0, m);
+      if (st == 1) {
+        iters = (uint32_t)(it + 1);
+        break;
+      }
+      if (st == 2) {
+        rho = rho_new;
+        build_operators(rho);
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---- store
+  bool nonfinite = false;
+  {
+    R* xo = static_cast<R*>(P.out.x) + (size_t)b * T * n;
+    R* xo2 = P.x_out ? P.x_out + (size_t)b * T * n : nullptr;
+    for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
+      const int t = e / n, j = e - t * n;
+      const R v = xs[t * RowsGeo::VSTR + j];
+      if (!isfinite(v)) nonfinite = true;
+      xo[e] = v;
+      if (xo2) xo2[e] = v;
+    }
+    if (n0 > 0) {
+      R* a = static_cast<R*>(P.out.y_f0) + (size_t)b * n0;
+      for (int e = threadIdx.x; e < n0; e += blockDim.x) a[e] = yf0[e];
+    }
+    R* a = static_cast<R*>(P.out.y_fdyn) + (size_t)b * N * nx;
+    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) a[e] = yfd[e];
+    if (m > 0) {
+      R* z = static_cast<R*>(P.out.z_g) + (size_t)b * T * m;
+      R* y = static_cast<R*>(P.out.y_g) + (size_t)b * T * m;
+      R* xi = static_cast<R*>(P.out.xi_g) + (size_t)b * T * m;
+      for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
+        z[e] = zg[e];
+        y[e] = yg[e];
+        xi[e] = xig[e];
+      }
+    }
+  }
+  if (nonfinite) atomicOr(&flag, TMPC_STATUS_NONFINITE);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    static_cast<R*>(P.out.rho_bar)[b] = rho;
+    if (P.iters_out) P.iters_out[b] = iters;
+    if (P.status_out) P.status_out[b] = flag;
+  }
+}
+
+inline size_t admm_rows_smem_bytes(int T, int nx, int n0, int m) {
+  return RowsSmem(T, nx, n0, m).nelem * sizeof(float);
+}
+
+// True when the register-resident kernel handles these dimensions.
+inline bool admm_rows_applicable(int T, int n, int nx, int n0, int m) {
+  return n > 8 && n <= 16 && T >= 2 && T <= RowsGeo::TMAX &&
+         (long)admm_rows_smem_bytes(T, nx, n0, m) <= max_dyn_smem();
+}
+
+}  // namespace tmpc
