@@ -48,7 +48,7 @@ struct AdmmSmem {
     gx = a4(o); o = gx + (size_t)T * m;
     ct = a4(o); o = ct + n0 + (size_t)N * nx;
     gt = a4(o); o = gt + (size_t)T * m;
-    red = a4(o); o = red + 64 + 16;
+    red = a4(o); o = red + kRedSize;
     fm = a4(o); o = fm + (nvec == 4 ? (size_t)NB * (NB + 1) : 0);  // Cholesky scratch (direct)
     nelem = a4(o);
   }
@@ -95,7 +95,7 @@ __device__ void compute_gamma(R* gam, const R* x, const QPView<R>& qp, const R* 
   }
 }
 
-// s += a . v over n entries: 128-bit loads of the global row a when n is a
+// s += a . v over n entries: 128-bit loads of the row a when n is a
 // multiple of the vector width and the row starts 16-byte aligned, else a
 // scalar loop unrolled by 4.  v is an on-chip block-vector row (aligned).
 template <typename R>
@@ -106,7 +106,7 @@ __device__ __forceinline__ R row_dot(const R* __restrict__ a, const R* __restric
 #pragma unroll 4
     for (int c = 0; c < n; c += VEC) {
       R w[VEC], x[VEC];
-      ldg128(w, a + c);
+      ld128(w, a + c);  // generic load: a is global or a shared-memory copy
       ld128(x, v + c);
 #pragma unroll
       for (int e = 0; e < VEC; ++e) s = fma(w[e], x[e], s);
@@ -142,7 +142,7 @@ __device__ void apply_constraints(R* cx0, R* cx, R* gx, const R* x, const QPView
 
 // Residuals of admm.py:266-331 (primal, dual, normalised), written to sc[0..5].
 template <int NB, typename R>
-__device__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const R* yg, const R* xig, const R* yf0,
+__device__ __noinline__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const R* yg, const R* xig, const R* yf0,
                                   const R* yfd, const QPView<R>& qp, R slack_w, bool use_slack, int T, int n, int nx,
                                   int n0, int m) {
   using Gm = Geo<NB, R>;
@@ -217,12 +217,22 @@ __device__ void compute_residuals(R* sc, R* red, const R* x, const R* zg, const 
       nyg = fmax(nyg, fabs(yg[e]));
     }
   }
-  R vals[11] = {pr, ncx, nc, ngx, nz, du, npx, naty, nq, nxi, nyg};
+  // Per-warp maxima into the 11 x 32 table, one barrier, thread 0 finishes.
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  auto put = [&](int k, R v) {
+    v = warp_max(v);
+    if (lane == 0) red[k * 32 + wid] = v;
+  };
+  put(0, pr); put(1, ncx); put(2, nc); put(3, ngx); put(4, nz);
+  put(5, du); put(6, npx); put(7, naty); put(8, nq); put(9, nxi); put(10, nyg);
+  __syncthreads();
   R outv[11];
-#pragma unroll
-  for (int k = 0; k < 11; ++k) {
-    outv[k] = block_max(vals[k], red + (k & 1) * 32);
-    __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < 11; ++k) {
+      R v = R(0);
+      for (int w = 0; w < nw; ++w) v = fmax(v, red[k * 32 + w]);
+      outv[k] = v;
+    }
   }
   if (threadIdx.x == 0) {
     const R prim = outv[0];
@@ -350,7 +360,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
   R* ct = sm + L.ct;
   R* gt = sm + L.gt;
   R* red = sm + L.red;
-  R* sc = red + 64;
+  R* sc = red + kRedSc;
   __shared__ int flag;
   if (threadIdx.x == 0) flag = 0;
 

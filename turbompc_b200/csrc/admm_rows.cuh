@@ -50,15 +50,33 @@ __host__ __device__ constexpr int rows_tpad(int T) { return rows_threads(T) / Ro
 // stage T-1, so row index t + 1 holds stage t and neighbours need no bounds
 // tests.
 struct RowsSmem {
-  size_t th, phi, tinv, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0, cx, gx, ct, gt, red, nelem;
-  __host__ __device__ RowsSmem(int T, int nx, int n0, int m) {
+  // stage: during assembly the Phi / -Theta^-1 scratch; afterwards a copy of
+  // the QP data the ADMM-level steps read every iteration (q, A0, Am, Ap, G,
+  // c0, c, l, u), so those steps run from shared memory instead of L2.
+  size_t th, stage, phi, tinv, sq, sa0, sam, sap, sg, sc0, sc, sl, su, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0,
+      cx, gx, ct, gt, red, nelem;
+  RowsSmem() = default;
+  __host__ __device__ RowsSmem(int T, int n, int nx, int n0, int m) {
     using G = RowsGeo;
     const int N = T - 1, TP = rows_tpad(T);
     auto a4 = [](size_t v) { return (v + 3) & ~size_t(3); };
     size_t o = 0;
     th = o; o += (size_t)TP * G::TBLK;
-    phi = o; o += (size_t)(N > 0 ? N : 1) * G::SQ;
-    tinv = o; o += (size_t)T * G::SQ;
+    stage = o;
+    phi = stage;
+    tinv = phi + (size_t)(N > 0 ? N : 1) * G::SQ;
+    const size_t scratch_end = tinv + (size_t)T * G::SQ;
+    size_t s = stage;
+    sq = s; s = a4(s + (size_t)T * n);
+    sa0 = s; s = a4(s + (size_t)n0 * n);
+    sam = s; s = a4(s + (size_t)N * nx * n);
+    sap = s; s = a4(s + (size_t)N * nx * n);
+    sg = s; s = a4(s + (size_t)T * m * n);
+    sc0 = s; s = a4(s + n0);
+    sc = s; s = a4(s + (size_t)N * nx);
+    sl = s; s = a4(s + (size_t)T * m);
+    su = s; s = a4(s + (size_t)T * m);
+    o = s > scratch_end ? s : scratch_end;
     bb = o; o += 4 * (size_t)G::BUF;  // p, w, r, u broadcast buffers at constant offsets
     x = o; o += (size_t)T * G::VSTR;
     gam = o; o += (size_t)T * G::VSTR;
@@ -73,10 +91,35 @@ struct RowsSmem {
     gx = a4(o); o = gx + (size_t)T * m;
     ct = a4(o); o = ct + n0 + (size_t)N * nx;
     gt = a4(o); o = gt + (size_t)T * m;
-    red = a4(o); o = red + 64 + 16 + 32;  // block_max slots, residual scalars, 2 x 16 dot slots
+    red = a4(o); o = red + kRedSize;  // residual table and scalars, 2 x 16 dot slots
     nelem = a4(o);
   }
 };
+
+// Copies the per-iteration QP data of one problem into the stage area (D and
+// E stay in global memory: only the residual checks read them).
+__device__ __forceinline__ void rows_stage_qp(float* sm, const RowsSmem& L, const QPView<float>& g, int T,
+                                                       int n, int nx, int n0, int m) {
+  const int N = T - 1;
+  auto copy = [](float* dst, const float* src, int cnt) {
+    if (src == nullptr) return;
+    if ((cnt & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      for (int e = threadIdx.x; e < cnt / 4; e += blockDim.x)
+        reinterpret_cast<float4*>(dst)[e] = __ldg(reinterpret_cast<const float4*>(src) + e);
+    } else {
+      for (int e = threadIdx.x; e < cnt; e += blockDim.x) dst[e] = __ldg(src + e);
+    }
+  };
+  copy(sm + L.sq, g.q, T * n);
+  copy(sm + L.sa0, g.A0, n0 * n);
+  copy(sm + L.sam, g.Am, N * nx * n);
+  copy(sm + L.sap, g.Ap, N * nx * n);
+  copy(sm + L.sg, g.G, T * m * n);
+  copy(sm + L.sc0, g.c0, n0);
+  copy(sm + L.sc, g.c, N * nx);
+  copy(sm + L.sl, g.l, T * m);
+  copy(sm + L.su, g.u, T * m);
+}
 
 // Assembly destination: Theta full (both triangles) with skewed rows, Phi and
 // -Theta^-1 as dense scratch blocks that are copied into registers.
@@ -203,19 +246,45 @@ __device__ __forceinline__ float rows_block_sum(float v, float* slots) {
          (((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w)));
 }
 
+// The operator rows of a thread are saved once per assembly to a volatile
+// per-thread local array (L1/L2 backed) and reloaded at the start of every PCG
+// solve, so they occupy registers only inside the PCG loop and the ADMM-level
+// steps around it get the register file.
+struct RowOpsSave {
+  volatile float v[96];
+  __device__ __forceinline__ void store(const RowOps& o) {
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        v[a * 16 + k] = o.ti[a][k];
+        v[32 + a * 16 + k] = o.lr[a][k];
+        v[64 + a * 16 + k] = o.lc[a][k];
+      }
+  }
+  __device__ __forceinline__ void load(RowOps& o) const {
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        o.ti[a][k] = v[a * 16 + k];
+        o.lr[a][k] = v[32 + a * 16 + k];
+        o.lc[a][k] = v[64 + a * 16 + k];
+      }
+  }
+};
+
 // PCG with the stopping rule and recurrences of admm_fused.cu:54-161 (see
 // pcg_core.cuh).  xs / gam are [T][VSTR] block vectors in shared memory; x is
-// read from and written back to xs.  The operator rows are (re)loaded into
-// registers here, so they are live only inside the PCG loop.  Returns the
-// iteration count.
-__device__ __forceinline__ int rows_pcg(const RowsAcc& acc, float* bb, float* xs, const float* gam, int T,
-                                        int max_iter, float eps, float* slots) {
+// read from and written back to xs.  Returns the iteration count.
+__device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
+                                        const float* gam, int T, int max_iter, float eps, float* slots) {
   constexpr int VS = RowsGeo::VSTR;
+  RowOps o;
+  saved.load(o);
   const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
   const bool act = t < T;
-  RowOps o;
-  rows_load_ops(o, acc, t, q, T);
-  const float* th_row = acc.th + t * RowsGeo::TBLK + q * RowsGeo::TSTR;
+  const float* th_row = th + t * RowsGeo::TBLK + q * RowsGeo::TSTR;
   float* bt = bb + t * RowsGeo::BSTR;
   float* prow = bt + RowsGeo::BSTR;
   float x[2], r[2], p[2], z[2], y[2];
@@ -261,97 +330,143 @@ __device__ __forceinline__ int rows_pcg(const RowsAcc& acc, float* bb, float* xs
   return it;
 }
 
+// Assembly of Theta / Phi / -Theta^-1 into shared memory (not inlined: the
+// kernel's resident operator registers are dead here, and a call boundary
+// keeps the Gauss-Jordan register demand out of the ADMM loop's allocation).
+__device__ __noinline__ void rows_assemble(const RowsAcc acc, const QPView<float> qg, float rho_f, float rho,
+                                           float sigma, int T, int n, int nx, int n0, int m, int* flag) {
+  assemble_theta_phi<16>(acc, qg, rho_f, rho, sigma, T, n, nx, n0, m);
+  __syncthreads();
+  invert_thetas<16, float>(acc, T, n, flag);
+  __syncthreads();
+}
+
+// Staged QP view rebuilt at each use from the offsets in shared memory (kept
+// out of registers across the PCG loop).
+__device__ __forceinline__ QPView<float> rows_qp_view(float* sm, const RowsSmem& L, const TmpcQP& g, int b, int T,
+                                                      int n, int nx, int n0, int m) {
+  QPView<float> v = qp_view<float>(g, b, T, n, nx, n0, m);
+  v.q = sm + L.sq;
+  v.A0 = n0 > 0 ? sm + L.sa0 : nullptr;
+  v.Am = sm + L.sam;
+  v.Ap = sm + L.sap;
+  v.G = m > 0 ? sm + L.sg : nullptr;
+  v.c0 = (n0 > 0 && g.c0) ? sm + L.sc0 : nullptr;
+  v.c = g.c ? sm + L.sc : nullptr;
+  v.l = (m > 0 && g.l) ? sm + L.sl : nullptr;
+  v.u = (m > 0 && g.u) ? sm + L.su : nullptr;
+  return v;
+}
+
+// Register budget: the operator rows (96 registers) are live inside the PCG
+// loop only; state that lives across the loop is kept in shared memory (arena
+// offsets) or re-read from the kernel parameters.
 __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(const AdmmParams<float> P) {
   using R = float;
   constexpr int NB = 16;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   R* sm = reinterpret_cast<R*>(smem_raw);
+  __shared__ RowsSmem Ls;
+  __shared__ int flag;
   const int b = blockIdx.x;
   if (b >= P.Nb) return;
-  const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
-  const RowsSmem L(T, nx, n0, m);
-  const int TP = rows_tpad(T);
-  R* xs = sm + L.x;
-  R* gam = sm + L.gam;
-  R* xold = sm + L.xold;
-  R* yf0 = sm + L.yf0;
-  R* yfd = sm + L.yfd;
-  R* zg = sm + L.zg;
-  R* yg = sm + L.yg;
-  R* xig = sm + L.xig;
-  R* cx0 = sm + L.cx0;
-  R* cx = sm + L.cx;
-  R* gx = sm + L.gx;
-  R* ct = sm + L.ct;
-  R* gt = sm + L.gt;
-  R* red = sm + L.red;
-  R* sc = red + 64;
-  R* slots = red + 80;
-  const RowsAcc acc{sm + L.th, sm + L.phi, sm + L.tinv};
-  __shared__ int flag;
-  if (threadIdx.x == 0) flag = 0;
-
-  const QPView<R> qp = qp_view<R>(P.qp, b, T, n, nx, n0, m);
-
-  // ---- zero Theta (incl. the padding blocks) and every vector region; load the warm start
-  for (size_t e = threadIdx.x; e < (size_t)TP * RowsGeo::TBLK; e += blockDim.x) acc.th[e] = R(0);
-  for (size_t e = L.bb + threadIdx.x; e < L.yf0; e += blockDim.x) sm[e] = R(0);
-  for (int e = threadIdx.x; e < 32; e += blockDim.x) slots[e] = R(0);
+#define TMPC_RS(f) (sm + Ls.f)
+  if (threadIdx.x == 0) {
+    Ls = RowsSmem(P.T, P.n, P.nx, P.n0, P.m);
+    flag = 0;
+  }
   __syncthreads();
   {
+    const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
+    // ---- zero Theta (incl. the padding blocks) and every vector region; load the warm start
+    for (size_t e = threadIdx.x; e < (size_t)rows_tpad(T) * RowsGeo::TBLK; e += blockDim.x) TMPC_RS(th)[e] = R(0);
+    for (size_t e = Ls.bb + threadIdx.x; e < Ls.yf0; e += blockDim.x) sm[e] = R(0);
+    for (int e = threadIdx.x; e < 32; e += blockDim.x) TMPC_RS(red)[kRedSlots + e] = R(0);
+    __syncthreads();
     const R* x_in = static_cast<const R*>(P.in.x) + (size_t)b * T * n;
     for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
       const int t = e / n, j = e - t * n;
-      xs[t * RowsGeo::VSTR + j] = x_in[e];
+      TMPC_RS(x)[t * RowsGeo::VSTR + j] = x_in[e];
     }
     if (n0 > 0) {
       const R* a = static_cast<const R*>(P.in.y_f0) + (size_t)b * n0;
-      for (int e = threadIdx.x; e < n0; e += blockDim.x) yf0[e] = a[e];
+      for (int e = threadIdx.x; e < n0; e += blockDim.x) TMPC_RS(yf0)[e] = a[e];
     }
     const R* a = static_cast<const R*>(P.in.y_fdyn) + (size_t)b * N * nx;
-    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) yfd[e] = a[e];
+    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) TMPC_RS(yfd)[e] = a[e];
     if (m > 0) {
       const R* z = static_cast<const R*>(P.in.z_g) + (size_t)b * T * m;
       const R* y = static_cast<const R*>(P.in.y_g) + (size_t)b * T * m;
       const R* xi = static_cast<const R*>(P.in.xi_g) + (size_t)b * T * m;
       for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
-        zg[e] = z[e];
-        yg[e] = y[e];
-        xig[e] = xi[e];
+        TMPC_RS(zg)[e] = z[e];
+        TMPC_RS(yg)[e] = y[e];
+        TMPC_RS(xig)[e] = xi[e];
       }
     }
   }
   R rho = static_cast<const R*>(P.in.rho_bar)[b];
-  const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
-  const R al = P.alpha;
 
-  // Theta and Phi into shared memory and -Theta^-1 by warp Gauss-Jordan; the
-  // PCG copies its rows into registers.  Ends with a barrier.
+  // Theta and Phi into shared memory, -Theta^-1 by warp Gauss-Jordan, the
+  // operator rows into the per-thread save area, then the QP copy into the
+  // stage area that held the scratch.  Ends with a barrier.
+  RowOpsSave ops;
   auto build_operators = [&](R rho_now) {
-    assemble_theta_phi<NB>(acc, qp, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m);
+    const int T = P.T, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
+    const RowsAcc acc{TMPC_RS(th), TMPC_RS(phi), TMPC_RS(tinv)};
+    const QPView<R> qg = qp_view<R>(P.qp, b, T, n, nx, n0, m);
+    rows_assemble(acc, qg, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m, &flag);
+    {
+      RowOps o;
+      rows_load_ops(o, acc, threadIdx.x >> 3, threadIdx.x & 7, T);
+      ops.store(o);
+    }
     __syncthreads();
-    invert_thetas<NB, R>(acc, T, n, &flag);
+    rows_stage_qp(sm, Ls, qg, T, n, nx, n0, m);
     __syncthreads();
   };
   build_operators(rho);
 
   uint32_t iters = (uint32_t)P.max_iter;
   for (int it = 0; it < P.max_iter; ++it) {
+    const int T = P.T, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
     const R rho_f = rho * P.rho_f_factor;
-    admm_targets(ct, gt, qp, yf0, yfd, zg, yg, rho, rho_f, T, nx, n0, m);
-    __syncthreads();
-    compute_gamma<NB>(gam, xs, qp, ct, gt, P.sigma, T, n, nx, n0, m);
-    TMPC_FOR_ENTRIES(e, o, T, NB, RowsGeo::VSTR) { xold[o] = xs[o]; }
-    __syncthreads();
-    rows_pcg(acc, sm + L.bb, xs, gam, T, P.pcg_max_iter, P.pcg_eps, slots);
-    apply_constraints<NB>(cx0, cx, gx, xs, qp, T, n, nx, n0, m);
-    __syncthreads();
-    admm_relax_duals<NB>(xs, xold, yf0, yfd, zg, yg, xig, cx0, cx, gx, qp, rho, rho_f, al, sw, P.use_slack != 0, T,
-                         nx, n0, m);
-    __syncthreads();
+    {
+      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+      admm_targets(TMPC_RS(ct), TMPC_RS(gt), qp, TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg), TMPC_RS(yg), rho, rho_f,
+                   T, nx, n0, m);
+      __syncthreads();
+    }
+    {
+      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+      compute_gamma<NB>(TMPC_RS(gam), TMPC_RS(x), qp, TMPC_RS(ct), TMPC_RS(gt), P.sigma, T, n, nx, n0, m);
+      R* xs = TMPC_RS(x);
+      R* xold = TMPC_RS(xold);
+      TMPC_FOR_ENTRIES(e, o, T, NB, RowsGeo::VSTR) { xold[o] = xs[o]; }
+      __syncthreads();
+    }
+    rows_pcg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
+             TMPC_RS(red) + kRedSlots);
+    {
+      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+      apply_constraints<NB>(TMPC_RS(cx0), TMPC_RS(cx), TMPC_RS(gx), TMPC_RS(x), qp, T, n, nx, n0, m);
+      __syncthreads();
+    }
+    {
+      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+      const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
+      admm_relax_duals<NB>(TMPC_RS(x), TMPC_RS(xold), TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg), TMPC_RS(yg),
+                           TMPC_RS(xig), TMPC_RS(cx0), TMPC_RS(cx), TMPC_RS(gx), qp, rho, rho_f, P.alpha, sw,
+                           P.use_slack != 0, T, nx, n0, m);
+      __syncthreads();
+    }
     if (P.check_every > 0 && (it % P.check_every) == 0) {
+      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+      const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
       R rho_new;
-      const int st = admm_check<NB>(sc, red, xs, zg, yg, xig, yf0, yfd, qp, sw, P, it, rho, &rho_new, T, n, nx, n0, m);
+      const int st = admm_check<NB>(TMPC_RS(red) + kRedSc, TMPC_RS(red), TMPC_RS(x), TMPC_RS(zg), TMPC_RS(yg),
+                                    TMPC_RS(xig), TMPC_RS(yf0), TMPC_RS(yfd), qp, sw, P, it, rho, &rho_new, T, n, nx,
+                                    n0, m);
       if (st == 1) {
         iters = (uint32_t)(it + 1);
         break;
@@ -367,32 +482,34 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   // ---- store
   bool nonfinite = false;
   {
+    const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
     R* xo = static_cast<R*>(P.out.x) + (size_t)b * T * n;
     R* xo2 = P.x_out ? P.x_out + (size_t)b * T * n : nullptr;
     for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
       const int t = e / n, j = e - t * n;
-      const R v = xs[t * RowsGeo::VSTR + j];
+      const R v = TMPC_RS(x)[t * RowsGeo::VSTR + j];
       if (!isfinite(v)) nonfinite = true;
       xo[e] = v;
       if (xo2) xo2[e] = v;
     }
     if (n0 > 0) {
       R* a = static_cast<R*>(P.out.y_f0) + (size_t)b * n0;
-      for (int e = threadIdx.x; e < n0; e += blockDim.x) a[e] = yf0[e];
+      for (int e = threadIdx.x; e < n0; e += blockDim.x) a[e] = TMPC_RS(yf0)[e];
     }
     R* a = static_cast<R*>(P.out.y_fdyn) + (size_t)b * N * nx;
-    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) a[e] = yfd[e];
+    for (int e = threadIdx.x; e < N * nx; e += blockDim.x) a[e] = TMPC_RS(yfd)[e];
     if (m > 0) {
       R* z = static_cast<R*>(P.out.z_g) + (size_t)b * T * m;
       R* y = static_cast<R*>(P.out.y_g) + (size_t)b * T * m;
       R* xi = static_cast<R*>(P.out.xi_g) + (size_t)b * T * m;
       for (int e = threadIdx.x; e < T * m; e += blockDim.x) {
-        z[e] = zg[e];
-        y[e] = yg[e];
-        xi[e] = xig[e];
+        z[e] = TMPC_RS(zg)[e];
+        y[e] = TMPC_RS(yg)[e];
+        xi[e] = TMPC_RS(xig)[e];
       }
     }
   }
+#undef TMPC_RS
   if (nonfinite) atomicOr(&flag, TMPC_STATUS_NONFINITE);
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -402,14 +519,14 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   }
 }
 
-inline size_t admm_rows_smem_bytes(int T, int nx, int n0, int m) {
-  return RowsSmem(T, nx, n0, m).nelem * sizeof(float);
+inline size_t admm_rows_smem_bytes(int T, int n, int nx, int n0, int m) {
+  return RowsSmem(T, n, nx, n0, m).nelem * sizeof(float);
 }
 
 // True when the register-resident kernel handles these dimensions.
 inline bool admm_rows_applicable(int T, int n, int nx, int n0, int m) {
   return n > 8 && n <= 16 && T >= 2 && T <= RowsGeo::TMAX &&
-         (long)admm_rows_smem_bytes(T, nx, n0, m) <= max_dyn_smem();
+         (long)admm_rows_smem_bytes(T, n, nx, n0, m) <= max_dyn_smem();
 }
 
 }  // namespace tmpc

@@ -67,6 +67,14 @@ __host__ __device__ inline int tri_col(int idx, int nb) {
   return i + idx;
 }
 
+// Layout of the per-CTA reduction region ("red") of the fused ADMM kernels:
+// [0, 352) an 11 x 32 table of per-warp partial maxima for the residual check
+// (also the block_sum slots of the packed PCG), residual scalars at 352, the
+// register-resident kernel's dot-product slots at 368.
+constexpr int kRedSc = 352;
+constexpr int kRedSlots = 368;
+constexpr int kRedSize = 400;
+
 template <int NB, typename R>
 struct Geo {
   static constexpr int VEC = 16 / (int)sizeof(R);                // elements per 128-bit load
