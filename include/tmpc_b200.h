@@ -246,6 +246,32 @@ int32_t tmpc_admm_solve_fixed_scratch_f64(const TmpcDims* dims, const TmpcQP* qp
                                           double* x_out, uint32_t* iters_out, int32_t* status_out,
                                           tmpc_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Linearised discrete dynamics of a built-in model, batched over (problem,
+ * stage t < N): the QP's dynamics rows, as produced in the reference by
+ * get_dynamics_linearized_matrices (turbompc/problems/
+ * optimal_control_problem.py:1217-1272, explicit schemes, forward-mode
+ * Jacobian).  With F one step of `scheme` (turbompc/dynamics/integrators.py)
+ * of the model's x_dot:
+ *   A_minus[b][t] = [dF/dx, dF/du] at (x_t, u_t)        [Nb][N][nx][n]
+ *   c[b][t]       = -F(x_t, u_t) + A_minus[b][t] [x_t; u_t]   [Nb][N][nx]
+ * states [Nb][T][nx], controls [Nb][T][nu]; dims: Nb, T, n = nx + nu, nx
+ * (n0, m unused).  params (host array):
+ *   TMPC_MODEL_QUADROTOR12         {mass, Jx, Jy, Jz, arm_length, yaw_coefficient}
+ *   TMPC_MODEL_CLOHESSY_WILTSHIRE  {mean_motion}
+ * ------------------------------------------------------------------------- */
+#define TMPC_MODEL_QUADROTOR12 1
+#define TMPC_MODEL_CLOHESSY_WILTSHIRE 2
+#define TMPC_SCHEME_EULER 0
+#define TMPC_SCHEME_MIDPOINT 1
+#define TMPC_SCHEME_RK4 2
+int32_t tmpc_linearize_dynamics_f32(const TmpcDims* dims, int32_t model, int32_t scheme, double dt,
+                                    const float* states, const float* controls, const double* params,
+                                    int32_t n_params, float* A_minus, float* c, tmpc_stream_t stream);
+int32_t tmpc_linearize_dynamics_f64(const TmpcDims* dims, int32_t model, int32_t scheme, double dt,
+                                    const double* states, const double* controls, const double* params,
+                                    int32_t n_params, double* A_minus, double* c, tmpc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,8 @@ class TmpcAdmmConfig(C.Structure):
 LINSYS_PCG = 0
 LINSYS_DIRECT = 1
 LINSYS_PCG_PACKED = 2
+MODEL_QUADROTOR12 = 1
+MODEL_CLOHESSY_WILTSHIRE = 2
 
 # name -> (restype, argtypes)
 _P = C.c_void_p
@@ -57,6 +59,8 @@ _SIGS["tmpc_riccati_factor_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int3
 _SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 for _s in ("f32", "f64"):
     _SIGS[f"tmpc_riccati_factor_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
+    _SIGS[f"tmpc_linearize_dynamics_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, C.c_int32, C.c_double, _P,
+                                                          _P, _P, C.c_int32, _P, _P, _P])
     _SIGS[f"tmpc_riccati_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_adjoint_kkt_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, _P, _P, _P,
                                                           C.c_size_t, _P])

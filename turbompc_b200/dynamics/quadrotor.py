@@ -33,6 +33,19 @@ class Quadrotor12Dynamics(Dynamics):
             "names_states": ["x", "y", "z", "roll", "pitch", "yaw", "vx", "vy", "vz", "wx", "wy", "wz"],
             "names_controls": ["f1", "f2", "f3", "f4"]})
 
+    def cuda_model(self, params=None):
+        """(model id, parameter list) for the CUDA linearisation kernel, or
+        None when a parameter is a tensor (per-problem values)."""
+        params = params or {}
+        m = params.get("mass", DEFAULTS["mass"])
+        J = params.get("inertia", DEFAULTS["inertia"])
+        L = params.get("arm_length", DEFAULTS["arm_length"])
+        k = params.get("yaw_coefficient", DEFAULTS["yaw_coefficient"])
+        vals = [m, *(J if not isinstance(J, torch.Tensor) else [None]), L, k]
+        if any(v is None or isinstance(v, torch.Tensor) for v in vals) or len(vals) != 6:
+            return None
+        return 1, [float(v) for v in vals]
+
     def state_dot(self, state, control, params=None):
         params = params or {}
         m = params.get("mass", DEFAULTS["mass"])

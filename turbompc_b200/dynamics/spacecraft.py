@@ -16,6 +16,13 @@ class ClohessyWiltshireDynamics(Dynamics):
         super().__init__({"num_states": 6, "num_controls": 3,
                           "names_states": ["x", "y", "z", "vx", "vy", "vz"], "names_controls": ["ax", "ay", "az"]})
 
+    def cuda_model(self, params=None):
+        """(model id, parameter list) for the CUDA linearisation kernel, or None."""
+        n = (params or {}).get("mean_motion", 0.0011)
+        if isinstance(n, torch.Tensor):
+            return None
+        return 2, [float(n)]
+
     def state_dot(self, state, control, params=None):
         n = (params or {}).get("mean_motion", 0.0011)
         x, z = state[..., 0], state[..., 2]

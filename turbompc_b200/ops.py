@@ -261,3 +261,22 @@ def adjoint_kkt_solve(qp: QPData, workspace: Optional[torch.Tensor] = None):
     _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), _ptr(dz), _ptr(mult), _ptr(st), workspace.data_ptr(),
                                         need, _stream(qp.device)))
     return dz, mult, st
+
+
+def linearize_dynamics(model: int, params, scheme: int, dt: float, states: torch.Tensor, controls: torch.Tensor):
+    """Dynamics rows of the QP for a built-in model (tmpc_linearize_dynamics_*):
+    returns (A_minus (Nb, N, nx, n), c (Nb, N, nx)) at the stages t < N."""
+    lib = _ffi.load()
+    states, controls = states.contiguous(), controls.contiguous()
+    Nb, T, nx = states.shape
+    nu = controls.shape[-1]
+    N = T - 1
+    Am = torch.empty(Nb, N, nx, nx + nu, dtype=states.dtype, device=states.device)
+    c = torch.empty(Nb, N, nx, dtype=states.dtype, device=states.device)
+    d = _ffi.TmpcDims(Nb, T, nx + nu, nx, 0, 0)
+    pa = (C.c_double * max(1, len(params)))(*[float(v) for v in params])
+    name = f"tmpc_linearize_dynamics_{_suffix(states.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), int(model), int(scheme), float(dt), _ptr(states),
+                                        _ptr(controls, states.dtype, states.device), pa, len(params), _ptr(Am),
+                                        _ptr(c), _stream(states.device)))
+    return Am, c

@@ -101,6 +101,19 @@ class OptimalControlProblem:
     def _num_extra_inequalities(self) -> int:
         return 0
 
+    @property
+    def state_independent_cost(self) -> bool:
+        """True: the tracking cost's blocks (D, E, q) depend on the parameters
+        only, not on the linearisation point (subclasses with a nonquadratic
+        cost return False)."""
+        return True
+
+    @property
+    def state_independent_inequalities(self) -> bool:
+        """True when the inequality rows (box bounds only) do not depend on
+        the linearisation point."""
+        return self._num_extra_inequalities() == 0
+
     # --------------------------------------------------------------- bounds
     def _set_active_bounds(self, params):
         """Active box bounds: any finite entry with |bound| < 1e6 (optimal_control_problem.py:177-186)."""
@@ -146,6 +159,21 @@ class OptimalControlProblem:
         N = self.horizon
         return predict_next_state(self._dynamics, dt, self._scheme, self._dyn_params(params, states),
                                   states[:, :N], controls[:, :N])
+
+    def linearized_dynamics_rows(self, states, controls, params):
+        """(A_minus (Nb, N, nx, n), c (Nb, N, nx)) of the QP: from the CUDA
+        linearisation kernel for a built-in model with scalar parameters on a
+        CUDA device, else from get_dynamics_linearized_matrices (forward-mode
+        autodiff of the integrator in PyTorch, any dynamics)."""
+        cm = getattr(self._dynamics, "cuda_model", None)
+        spec = cm(self._dyn_params(params, states)) if (cm is not None and states.is_cuda) else None
+        if spec is not None and self._scheme in (DiscretizationScheme.EULER, DiscretizationScheme.MIDPOINT,
+                                                 DiscretizationScheme.RUNGEKUTTA4):
+            from .. import ops
+            return ops.linearize_dynamics(spec[0], spec[1], int(self._scheme),
+                                          float(params["discretization_resolution"]), states, controls)
+        _, _, As, Bs, Cs = self.get_dynamics_linearized_matrices(states, controls, params)
+        return torch.cat([As, Bs], dim=-1).contiguous(), Cs[:, 1:].contiguous()
 
     def get_dynamics_linearized_matrices(self, states, controls, params):
         """Explicit integrators (optimal_control_problem.py:1217-1272):

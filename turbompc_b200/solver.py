@@ -23,7 +23,7 @@ import torch
 
 from . import ops
 from .ops import ADMMState, AdmmConfig
-from .qp_data import QPData, qpdata_from_ocp_blocks
+from .qp_data import QPCostBlocks, QPData, QPEqualityBlocks, QPInequalityBlocks, qpdata_from_ocp_blocks
 
 DEFAULT_SOLVER_PARAMS: Dict[str, Any] = {
     # turbompc/solvers/params/turbompc.yaml:1-23
@@ -244,19 +244,34 @@ class TurboMPCSolver:
         return make_differentiable_solve(self)
 
     # ------------------------------------------------------------ QP build
-    def _build_qp_data(self, states, controls, params) -> QPData:
-        """turbompc_solver.py:1098-1156."""
+    def _build_qp_data(self, states, controls, params, prev: Optional[QPData] = None) -> QPData:
+        """turbompc_solver.py:1098-1156.  With ``prev`` (the previous SQP
+        iterate's QP of the same solve) the blocks that do not depend on the
+        linearisation point are reused: the tracking cost (D, E, q), the
+        initial-state rows (A0, c0), A_plus = [-I 0] and, without extra
+        nonlinear inequalities, the box rows (G, l, u).  The dynamics rows
+        (A_minus, c) are recomputed."""
         prog = self._program
+        A_minus, c_dyn = prog.linearized_dynamics_rows(states, controls, params)
+        if prev is not None and getattr(prog, "state_independent_cost", False):
+            ineq = prev.ineq
+            if not prog.state_independent_inequalities:
+                G, l, u = prog.get_inequalities_linearized_matrices(states, controls, params)
+                ineq = QPInequalityBlocks(G.contiguous(), l.contiguous(), u.contiguous(),
+                                          prev.ineq.slack_penalization_weight, prev.ineq.use_slack_variables)
+            return QPData(prev.cost, QPEqualityBlocks(prev.eq.A0, A_minus, prev.eq.A_plus, prev.eq.c0, c_dyn), ineq)
         D, E, q = prog.get_cost_linearized_blocks(states, controls, params)
-        As_next, Bs_next, As, Bs, Cs = prog.get_dynamics_linearized_matrices(states, controls, params)
         G, l, u = prog.get_inequalities_linearized_matrices(states, controls, params)
         A0, c0 = prog.get_initial_equality_linearized_matrices(params, states)
+        Nb, T, nx = states.shape
+        A_plus = torch.zeros_like(A_minus)
+        A_plus[..., :nx] = -torch.eye(nx, dtype=states.dtype, device=states.device)
         sw = params.get("slack_penalization_weight", None)
         if sw is not None:
             sw = torch.as_tensor(sw, dtype=states.dtype, device=states.device).expand(states.shape[0]).contiguous()
         c = lambda t: t.contiguous()
-        return qpdata_from_ocp_blocks(c(D), c(E), c(q), c(A0), c(c0), c(As_next), c(Bs_next), c(As), c(Bs),
-                                      c(Cs[:, 1:]), c(G), c(l), c(u), prog.use_slack_variables, sw)
+        return QPData(QPCostBlocks(c(D), c(E), c(q)), QPEqualityBlocks(c(A0), A_minus, A_plus, c(c0), c_dyn),
+                      QPInequalityBlocks(c(G), c(l), c(u), sw, prog.use_slack_variables))
 
     def _first_order_error(self, qp: QPData, states, controls, slacks, st: ADMMState):
         """turbompc_solver.py:1158-1225 (first_order criterion)."""
@@ -342,7 +357,7 @@ class TurboMPCSolver:
                 step = step + _inf(sl_new - slacks)
             if crit == "first_order":
                 if k + 1 < max_iter:
-                    qp_next = self._build_qp_data(s_new, c_new, params)
+                    qp_next = self._build_qp_data(s_new, c_new, params, prev=qp)
                     cv, ev, iv, g = self._first_order_error(qp_next, s_new, c_new, sl_new, st_new)
                 else:
                     qp_next = qp
@@ -352,7 +367,7 @@ class TurboMPCSolver:
                     if qp.ineq.use_slack_variables:
                         g = g + sl_new
             else:
-                qp_next = self._build_qp_data(s_new, c_new, params) if k + 1 < max_iter else qp
+                qp_next = self._build_qp_data(s_new, c_new, params, prev=qp) if k + 1 < max_iter else qp
                 cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), torch.einsum(
                     "btki,bti->btk", qp_next.ineq.G, z_new)
             kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
@@ -368,8 +383,9 @@ class TurboMPCSolver:
             conv = sel(cv, conv)
             it_count = it_count + active.to(torch.int64)
             if k + 1 < max_iter:
+                # Fields shared with the previous QP (reused blocks) need no select.
                 qp = qp_next if bool(active.all()) else QPData(*[type(f)(*[
-                    sel(a_, b_) if isinstance(a_, torch.Tensor) and a_.dim() > 0 else a_
+                    sel(a_, b_) if isinstance(a_, torch.Tensor) and a_.dim() > 0 and a_ is not b_ else a_
                     for a_, b_ in zip(vars(f).values(), vars(g_).values())]) for f, g_ in zip(
                         (qp_next.cost, qp_next.eq, qp_next.ineq), (qp.cost, qp.eq, qp.ineq))])
             active = active & (conv > tol)
