@@ -162,7 +162,7 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def admm_only(nb, linsys="auto", reps=3, pcg=PCG):
+def admm_only(nb, linsys="auto", reps=3, pcg=PCG, admm=ADMM):
     """One warm-up and `reps` timed fused ADMM launches (30 ADMM x 30 PCG, fp32)
     on nb quadrotor-shaped LTI QPs; prints ms per launch (CUDA events)."""
     import torch
@@ -173,7 +173,7 @@ def admm_only(nb, linsys="auto", reps=3, pcg=PCG):
     b = synthetic.random_lti(nb, 12, 4, N_HORIZON, seed=0)
     qd = synthetic.to_qpdata(b, dtype=torch.float32, device="cuda")
     ls = _ffi.LINSYS_PCG if linsys == "auto" else _ffi.LINSYS_PCG_PACKED
-    cfg = ops.AdmmConfig(max_iter=ADMM, pcg_max_iter=pcg, check_every=0, adapt_rho_every=0, eps_abs=0.0,
+    cfg = ops.AdmmConfig(max_iter=admm, pcg_max_iter=pcg, check_every=0, adapt_rho_every=0, eps_abs=0.0,
                          eps_rel=0.0, pcg_eps=0.0, linsys=ls)
     s0 = ops.admm_initial_state(qd, 0.1)
     out, it, st = ops.admm_solve(qd, s0, cfg)
@@ -185,8 +185,92 @@ def admm_only(nb, linsys="auto", reps=3, pcg=PCG):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    print(json.dumps({"admm_only": nb, "linsys": linsys, "pcg_iters": pcg, "ms_per_launch": round(ms, 3),
+    print(json.dumps({"admm_only": nb, "linsys": linsys, "admm_iters": admm, "pcg_iters": pcg, "ms_per_launch": round(ms, 3),
                       "us_per_problem": round(1e3 * ms / nb, 3), "status_nonzero": int((st != 0).sum())}))
+
+
+def pcg_sweep(points, reps=3, pcg_iters=PCG):
+    """Config 2 (linear-system kernel sweep): standalone PCG (fixed iterations,
+    tol 0) on assembled packed operators and the direct block-Cholesky solve,
+    timed with CUDA events and reported against the HBM roofline with the
+    streaming model B_pcg = 2(2T-1)n^2 w per PCG iteration (factor:
+    read S + write the factor; solve: read the factor).  Operators of 64
+    seeded LTI problems are tiled to the batch (same values, distinct memory)."""
+    import torch
+
+    from turbompc_b200 import _ffi, ops
+    from turbompc_b200.problems import synthetic
+
+    peak, pk_kind = peaks()
+    for (nx, nu, N, batch, dt) in points:
+        tdt = torch.float32 if dt == "f32" else torch.float64
+        w = 4 if dt == "f32" else 8
+        n, T = nx + nu, N + 1
+        small = synthetic.to_qpdata(synthetic.random_lti(64, nx, nu, N, seed=1000 + nx + N), dtype=tdt,
+                                    device="cuda")
+        dims = _ffi.TmpcDims(batch, T, n, nx, 0, 0)
+        g = torch.Generator(device="cuda").manual_seed(7)
+        rhs = torch.randn(batch, T, n, generator=g, device="cuda", dtype=tdt)
+        x0 = torch.zeros_like(rhs)
+        b_pcg = 2 * (2 * T - 1) * n * n * w
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        for kind in ("stream", "packed"):
+            if kind == "stream":
+                o64, st = ops.schur_assemble_stream(small, 0.1, 1e-6, 1000.0)
+                solve = ops.pcg_solve_stream
+            else:
+                o64, st = ops.schur_assemble_packed(small, 0.1, 1e-6, 1000.0)
+                solve = ops.pcg_solve_packed
+            per = o64.numel() // 64
+            opsb = o64[:64 * per].view(64, per).repeat((batch + 63) // 64, 1)[:batch].contiguous().view(-1)
+            try:
+                x, it = solve(opsb, dims, rhs, x0, 0.0, pcg_iters)
+            except Exception as exc:  # e.g. the packed kernel's vectors exceed shared memory
+                print(json.dumps({"sweep": "pcg_" + kind, "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+                                  "unavailable": str(exc)}), flush=True)
+                del opsb
+                continue
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                solve(opsb, dims, rhs, x0, 0.0, pcg_iters)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            gbs = batch * pcg_iters * b_pcg / (ms / 1e3) / 1e9
+            line = {"sweep": "pcg_" + kind, "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+                    "pcg_iters": pcg_iters, "iters_ok": bool((it == pcg_iters).all()), "ms": round(ms, 3),
+                    "solves_per_s": round(batch / (ms / 1e3), 1), "model_GBps": round(gbs, 1),
+                    "frac_of_peak": round(gbs / peak, 3), "peak": peak, "peak_source": pk_kind}
+            print(json.dumps(line), flush=True)
+            del opsb
+        # direct solve on reference-layout S
+        S, P, _ = ops.schur_assemble(small, 0.1, 1e-6, 1000.0)
+        Sb = S.repeat((batch + 63) // 64, 1, 1, 1)[:batch].contiguous()
+        del P
+        fac, fst = ops.riccati_factor(Sb)
+        xr = ops.riccati_solve(fac, rhs)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fac, fst = ops.riccati_factor(Sb)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_f = e0.elapsed_time(e1) / reps
+        e0.record()
+        for _ in range(reps):
+            ops.riccati_solve(fac, rhs)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_s = e0.elapsed_time(e1) / reps
+        b_f = (T * n * 3 * n + (2 * T - 1) * n * n) * w  # read S (reference layout) + write the factor
+        b_s = (2 * T - 1) * n * n * w + 2 * T * n * w
+        print(json.dumps({"sweep": "riccati", "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+                          "factor_ms": round(ms_f, 3), "solve_ms": round(ms_s, 3),
+                          "factor_model_GBps": round(batch * b_f / (ms_f / 1e3) / 1e9, 1),
+                          "solve_model_GBps": round(batch * b_s / (ms_s / 1e3) / 1e9, 1),
+                          "status_nonzero": int((fst != 0).sum())}), flush=True)
+        del Sb, fac
 
 
 def main():
@@ -203,9 +287,22 @@ def main():
     ap.add_argument("--admm-linsys", default="auto", choices=["auto", "packed"],
                     help="with --admm-only: auto (register-resident kernel where it applies) or the packed kernel")
     ap.add_argument("--admm-pcg", type=int, default=PCG, help="with --admm-only: PCG iterations per ADMM iteration")
+    ap.add_argument("--admm-iters", type=int, default=ADMM, help="with --admm-only: ADMM iterations per launch")
+    ap.add_argument("--pcg-sweep", default="", metavar="POINTS",
+                    help="config-2 linear-system sweep: ';'-separated nx,nu,N,batch,dtype points "
+                         "(e.g. '24,8,128,4096,f32'); 'default' runs a representative set")
     args = ap.parse_args()
+    if args.pcg_sweep:
+        spec = args.pcg_sweep
+        if spec == "default":
+            spec = "6,3,32,65536,f32;12,4,64,16384,f32;24,8,128,4096,f32;24,8,128,2048,f64"
+        pts = []
+        for item in spec.split(";"):
+            a = item.split(",")
+            pts.append((int(a[0]), int(a[1]), int(a[2]), int(a[3]), a[4]))
+        return pcg_sweep(pts)
     if args.admm_only:
-        return admm_only(args.admm_only, args.admm_linsys, pcg=args.admm_pcg)
+        return admm_only(args.admm_only, args.admm_linsys, pcg=args.admm_pcg, admm=args.admm_iters)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

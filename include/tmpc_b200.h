@@ -247,6 +247,27 @@ int32_t tmpc_admm_solve_fixed_scratch_f64(const TmpcDims* dims, const TmpcQP* qp
                                           tmpc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * HBM-streaming PCG for operators too large to stay on chip (long horizons,
+ * large n).  Same math, arguments and results as tmpc_pcg_solve_* (the
+ * pcg_blktridi_cuda target, pcg_ffi.cc:115-147), on operators in the stream
+ * layout written by tmpc_schur_assemble_stream_*: per problem S then Phiinv,
+ * each T full NB x NB diagonal blocks followed by N full NB x NB sub-diagonal
+ * blocks, row-major (NB = the compiled block size >= n, zero padded).  Every
+ * PCG iteration reads each operator once from HBM.
+ * ------------------------------------------------------------------------- */
+size_t tmpc_stream_operator_bytes(const TmpcDims* dims, int32_t dtype_bytes);
+int32_t tmpc_schur_assemble_stream_f32(const TmpcDims* dims, const TmpcQP* qp, const float* rho_bar, double sigma,
+                                       double rho_f_factor, float* ops, int32_t* status, tmpc_stream_t stream);
+int32_t tmpc_schur_assemble_stream_f64(const TmpcDims* dims, const TmpcQP* qp, const double* rho_bar, double sigma,
+                                       double rho_f_factor, double* ops, int32_t* status, tmpc_stream_t stream);
+int32_t tmpc_pcg_solve_stream_f32(const TmpcDims* dims, const float* ops, const float* rhs, const float* x0,
+                                  float* x_out, uint32_t* iters_out, double eps, int32_t max_iters,
+                                  tmpc_stream_t stream);
+int32_t tmpc_pcg_solve_stream_f64(const TmpcDims* dims, const double* ops, const double* rhs, const double* x0,
+                                  double* x_out, uint32_t* iters_out, double eps, int32_t max_iters,
+                                  tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Linearised discrete dynamics of a built-in model, batched over (problem,
  * stage t < N): the QP's dynamics rows, as produced in the reference by
  * get_dynamics_linearized_matrices (turbompc/problems/

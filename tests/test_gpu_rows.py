@@ -71,25 +71,25 @@ def test_rows_kernel_lti_config_matches_packed_kernel():
 
 
 def test_rows_kernel_slack_residual_checks_and_rho_adaptation():
-    """Soft constraints, residual checks every 5 iterations and OSQP rho
-    updates with the on-chip rebuild of the register-resident operators (eps
-    small enough that no problem stops: the rho path is compared, not the stop
-    decision).  The rho rule rho * sqrt(p / d) amplifies the fp32 rounding of
-    the residual norms, so the bar is the packed fp32 kernel's own distance to
-    the fp64 oracle (or 1e-3, whichever is larger)."""
+    """Soft constraints, residual checks every 5 iterations and an OSQP rho
+    update at iteration 10 with the on-chip rebuild of the operators, followed
+    by two iterations on the rebuilt operators.  Tolerance 1.0 makes every
+    problem take the update (no borderline accept/reject decision); stopping
+    after one update keeps the rho rule rho * sqrt(p / d) well conditioned
+    (later updates, near convergence, amplify fp32 rounding of the residual
+    norms by orders of magnitude, in the fp32 oracle as much as here)."""
     b = dense_blocks(6, 10, 4, 12, 3, seed=3)
-    kw = dict(max_iter=60, pcg_max_iter=6, check_every=5, adapt_rho_every=10, eps_abs=1e-9, eps_rel=1e-9,
-              pcg_eps=0.0, rho_f_factor=100.0, alpha=1.6, sigma=1e-6)
+    kw = dict(max_iter=12, pcg_max_iter=6, check_every=5, adapt_rho_every=10, eps_abs=1e-9, eps_rel=1e-9,
+              pcg_eps=0.0, rho_f_factor=100.0, alpha=1.6, sigma=1e-6, adaptive_rho_tolerance=1.0)
     out, iters, status = _solve(b, kw, slack=10.0)
-    pk, _, _ = _solve(b, kw, slack=10.0, linsys=_ffi.LINSYS_PCG_PACKED)
     so, io = _oracle(b, kw, slack=10.0)
     assert (_np(status) == 0).all()
-    assert (io == 60).all() and (_np(iters) == 60).all()
-    assert (np.abs(so.rho - 0.1) > 1e-3).any(), "the case must exercise a rho update"
-    for got, pgot, want in ((out.rho_bar, pk.rho_bar, so.rho), (out.x_blocks, pk.x_blocks, so.x),
-                            (out.xi_g, pk.xi_g, so.xi_g)):
-        bar = max(1e-3, 2.0 * rel_err(_np(pgot), want))
-        assert rel_err(_np(got), want) < bar
+    assert (io == 12).all() and (_np(iters) == 12).all()
+    assert (np.abs(so.rho - 0.1) > 1e-2).all(), "every problem must take the rho update"
+    assert rel_err(_np(out.rho_bar), so.rho) < 1e-3
+    assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+    assert rel_err(_np(out.xi_g), so.xi_g) < 1e-3
+    assert rel_err(_np(out.y_g), so.y_g) < 1e-3
 
 
 def test_rows_kernel_convergence_stop():

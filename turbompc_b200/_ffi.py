@@ -56,11 +56,16 @@ _SIGS = {
                                                       C.c_void_p]),
 }
 _SIGS["tmpc_riccati_factor_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
+_SIGS["tmpc_stream_operator_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 _SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 for _s in ("f32", "f64"):
     _SIGS[f"tmpc_riccati_factor_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_linearize_dynamics_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, C.c_int32, C.c_double, _P,
                                                           _P, _P, C.c_int32, _P, _P, _P])
+    _SIGS[f"tmpc_schur_assemble_stream_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P,
+                                                             C.c_double, C.c_double, _P, _P, _P])
+    _SIGS[f"tmpc_pcg_solve_stream_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P, _P, C.c_double,
+                                                        C.c_int32, _P])
     _SIGS[f"tmpc_riccati_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_adjoint_kkt_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, _P, _P, _P,
                                                           C.c_size_t, _P])
@@ -81,7 +86,9 @@ _lock = threading.Lock()
 
 
 def lib_path() -> str:
-    return _build.LIB
+    """The in-tree library, or the file named by TMPC_B200_LIB (a variant
+    build, e.g. one compiled with phase timers)."""
+    return os.environ.get("TMPC_B200_LIB") or _build.LIB
 
 
 def load(build_if_missing: bool = True):

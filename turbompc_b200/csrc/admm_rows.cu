@@ -25,3 +25,14 @@ int launch_admm_rows(const AdmmParams<float>& P, cudaStream_t st) {
 }
 
 }  // namespace tmpc
+
+#ifdef TMPC_ROWS_PROFILE
+extern "C" int32_t tmpc_debug_rows_profile(unsigned long long* out16, int32_t reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(out16, tmpc::g_rows_prof, sizeof(unsigned long long) * 16);
+  if (e == cudaSuccess && reset) {
+    unsigned long long z[16] = {};
+    e = cudaMemcpyToSymbol(tmpc::g_rows_prof, z, sizeof(z));
+  }
+  return (int32_t)e;
+}
+#endif

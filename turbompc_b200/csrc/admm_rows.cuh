@@ -27,6 +27,27 @@
 
 namespace tmpc {
 
+// Optional phase timers (build with -DTMPC_ROWS_PROFILE): thread 0 of every
+// CTA adds the clock64 cycles of each phase to g_rows_prof, read back with
+// tmpc_debug_rows_profile.  Compiled out of the regular library.
+#ifdef TMPC_ROWS_PROFILE
+__device__ unsigned long long g_rows_prof[16];
+#define TMPC_PROF_INIT long long prof_t0_ = clock64();
+#define TMPC_PROF(k)                                                   \
+  do {                                                                 \
+    if (threadIdx.x == 0) {                                            \
+      const long long now_ = clock64();                                \
+      atomicAdd(&g_rows_prof[k], (unsigned long long)(now_ - prof_t0_)); \
+      prof_t0_ = now_;                                                 \
+    }                                                                  \
+  } while (0)
+#else
+#define TMPC_PROF_INIT
+#define TMPC_PROF(k) \
+  do {               \
+  } while (0)
+#endif
+
 struct RowsGeo {
   static constexpr int NB = 16;
   static constexpr int TPB = 8;           // threads per stage block
@@ -50,10 +71,10 @@ __host__ __device__ constexpr int rows_tpad(int T) { return rows_threads(T) / Ro
 // stage T-1, so row index t + 1 holds stage t and neighbours need no bounds
 // tests.
 struct RowsSmem {
-  // stage: during assembly the Phi / -Theta^-1 scratch; afterwards a copy of
-  // the QP data the ADMM-level steps read every iteration (q, A0, Am, Ap, G,
-  // c0, c, l, u), so those steps run from shared memory instead of L2.
-  size_t th, stage, phi, tinv, sq, sa0, sam, sap, sg, sc0, sc, sl, su, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0,
+  // stage: a copy of the QP data the assembly and the ADMM-level steps read
+  // (q, A0, Am, Ap, G, c0, c, l, u); tslot: one 16 x 16 block per warp for
+  // handing -Theta_t^-1 from the Gauss-Jordan warp to the block's owners.
+  size_t th, stage, sq, sa0, sam, sap, sg, sc0, sc, sl, su, tslot, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0,
       cx, gx, ct, gt, red, nelem;
   RowsSmem() = default;
   __host__ __device__ RowsSmem(int T, int n, int nx, int n0, int m) {
@@ -63,20 +84,16 @@ struct RowsSmem {
     size_t o = 0;
     th = o; o += (size_t)TP * G::TBLK;
     stage = o;
-    phi = stage;
-    tinv = phi + (size_t)(N > 0 ? N : 1) * G::SQ;
-    const size_t scratch_end = tinv + (size_t)T * G::SQ;
-    size_t s = stage;
-    sq = s; s = a4(s + (size_t)T * n);
-    sa0 = s; s = a4(s + (size_t)n0 * n);
-    sam = s; s = a4(s + (size_t)N * nx * n);
-    sap = s; s = a4(s + (size_t)N * nx * n);
-    sg = s; s = a4(s + (size_t)T * m * n);
-    sc0 = s; s = a4(s + n0);
-    sc = s; s = a4(s + (size_t)N * nx);
-    sl = s; s = a4(s + (size_t)T * m);
-    su = s; s = a4(s + (size_t)T * m);
-    o = s > scratch_end ? s : scratch_end;
+    sq = o; o = a4(o + (size_t)T * n);
+    sa0 = o; o = a4(o + (size_t)n0 * n);
+    sam = o; o = a4(o + (size_t)N * nx * n);
+    sap = o; o = a4(o + (size_t)N * nx * n);
+    sg = o; o = a4(o + (size_t)T * m * n);
+    sc0 = o; o = a4(o + n0);
+    sc = o; o = a4(o + (size_t)N * nx);
+    sl = o; o = a4(o + (size_t)T * m);
+    su = o; o = a4(o + (size_t)T * m);
+    tslot = o; o += (size_t)(rows_threads(T) / 32) * G::SQ;
     bb = o; o += 4 * (size_t)G::BUF;  // p, w, r, u broadcast buffers at constant offsets
     x = o; o += (size_t)T * G::VSTR;
     gam = o; o += (size_t)T * G::VSTR;
@@ -104,6 +121,7 @@ __device__ __forceinline__ void rows_stage_qp(float* sm, const RowsSmem& L, cons
   auto copy = [](float* dst, const float* src, int cnt) {
     if (src == nullptr) return;
     if ((cnt & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll 4
       for (int e = threadIdx.x; e < cnt / 4; e += blockDim.x)
         reinterpret_cast<float4*>(dst)[e] = __ldg(reinterpret_cast<const float4*>(src) + e);
     } else {
@@ -121,21 +139,17 @@ __device__ __forceinline__ void rows_stage_qp(float* sm, const RowsSmem& L, cons
   copy(sm + L.su, g.u, T * m);
 }
 
-// Assembly destination: Theta full (both triangles) with skewed rows, Phi and
-// -Theta^-1 as dense scratch blocks that are copied into registers.
-struct RowsAcc {
-  float* th;
-  float* phi;
-  float* tinv;
-  __device__ void set_theta(int t, int i, int j, float v) const {
-    th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j] = v;
-    th[t * RowsGeo::TBLK + j * RowsGeo::TSTR + i] = v;
-  }
+// Gauss-Jordan source / destination: Theta from its shared-memory blocks,
+// -Theta_t^-1 into the slot of the warp that inverts it (t - base).
+struct RowsInvAcc {
+  const float* th;
+  float* tslot;
+  int base;
   __device__ float get_theta(int t, int i, int j) const { return th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j]; }
-  __device__ void set_phi(int t, int i, int j, float v) const { phi[t * RowsGeo::SQ + i * 16 + j] = v; }
   __device__ void set_ntinv(int t, int i, int j, float v) const {
-    tinv[t * RowsGeo::SQ + i * 16 + j] = v;
-    tinv[t * RowsGeo::SQ + j * 16 + i] = v;
+    float* b = tslot + (t - base) * RowsGeo::SQ;
+    b[i * 16 + j] = v;
+    b[j * 16 + i] = v;
   }
 };
 
@@ -144,26 +158,6 @@ struct RowOps {
   float lr[2][16];  // S(t, t-1) rows
   float lc[2][16];  // S(t, t+1) rows
 };
-
-// Copies this thread's operator rows out of the assembly scratch.
-__device__ __forceinline__ void rows_load_ops(RowOps& o, const RowsAcc& acc, int t, int q, int T) {
-  const int N = T - 1;
-  const bool act = t < T, has_lo = act && t >= 1, has_up = t < N;
-#pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    const int j = q + 8 * a;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f), w = v;
-      if (act) v = *reinterpret_cast<const float4*>(acc.tinv + t * RowsGeo::SQ + j * 16 + 4 * c);
-      if (has_lo) w = *reinterpret_cast<const float4*>(acc.phi + (t - 1) * RowsGeo::SQ + j * 16 + 4 * c);
-      o.ti[a][4 * c] = -v.x; o.ti[a][4 * c + 1] = -v.y; o.ti[a][4 * c + 2] = -v.z; o.ti[a][4 * c + 3] = -v.w;
-      o.lr[a][4 * c] = w.x; o.lr[a][4 * c + 1] = w.y; o.lr[a][4 * c + 2] = w.z; o.lr[a][4 * c + 3] = w.w;
-    }
-#pragma unroll
-    for (int k = 0; k < 16; ++k) o.lc[a][k] = has_up ? acc.phi[t * RowsGeo::SQ + k * 16 + j] : 0.f;
-  }
-}
 
 // a_i += m_i . v for the two owned rows; v is a broadcast 16-vector in shared memory.
 __device__ __forceinline__ void rows_bdot(float& a0, float& a1, const float (&m0)[16], const float (&m1)[16],
@@ -255,44 +249,38 @@ __device__ __forceinline__ void rows_prec(float (&z)[2], const float (&r)[2], co
 }
 
 // Deterministic block sum: warp sums into 16 slots (unused slots stay zero),
-// then every thread adds the slots in a fixed tree order from 4 vector loads.
+// then lane i of every warp reads slot i & 15 and the warp adds them with the
+// same shuffle tree, so every thread gets the same value.  Each lane reads 4
+// bytes instead of the 64-byte slot table.
 __device__ __forceinline__ float rows_block_sum(float v, float* slots) {
   v = warp_sum(v);
   if ((threadIdx.x & 31) == 0) slots[threadIdx.x >> 5] = v;
   __syncthreads();
-  const float4 a = *reinterpret_cast<const float4*>(slots);
-  const float4 b = *reinterpret_cast<const float4*>(slots + 4);
-  const float4 c = *reinterpret_cast<const float4*>(slots + 8);
-  const float4 d = *reinterpret_cast<const float4*>(slots + 12);
-  return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
-         (((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w)));
+  float s = slots[threadIdx.x & 15];
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
 }
 
-// The operator rows of a thread are saved once per assembly to a volatile
-// per-thread local array (L1/L2 backed) and reloaded at the start of every PCG
-// solve, so they occupy registers only inside the PCG loop and the ADMM-level
-// steps around it get the register file.
-struct RowOpsSave {
-  volatile float v[96];
-  __device__ __forceinline__ void store(const RowOps& o) {
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        v[a * 16 + k] = o.ti[a][k];
-        v[32 + a * 16 + k] = o.lr[a][k];
-        v[64 + a * 16 + k] = o.lc[a][k];
-      }
-  }
+// The operator rows of a thread are written by rows_build (a call that
+// receives the area's address, so the area lives in per-thread local memory,
+// L1/L2 backed) and loaded at the start of every PCG solve with 128-bit
+// loads, so they occupy registers only inside the PCG loop and the
+// ADMM-level steps around it get the register file.
+struct __align__(16) RowOpsSave {
+  float v[96];  // ti rows (0..31), lr rows (32..63), lc rows (64..95)
   __device__ __forceinline__ void load(RowOps& o) const {
+    const float4* p = reinterpret_cast<const float4*>(v);
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        o.ti[a][k] = v[a * 16 + k];
-        o.lr[a][k] = v[32 + a * 16 + k];
-        o.lc[a][k] = v[64 + a * 16 + k];
-      }
+    for (int c = 0; c < 24; ++c) {
+      const float4 w = p[c];
+      float* dst = c < 8 ? &o.ti[c >> 2][(c & 3) * 4] : (c < 16 ? &o.lr[(c - 8) >> 2][(c & 3) * 4]
+                                                               : &o.lc[(c - 16) >> 2][(c & 3) * 4]);
+      dst[0] = w.x;
+      dst[1] = w.y;
+      dst[2] = w.z;
+      dst[3] = w.w;
+    }
   }
 };
 
@@ -302,6 +290,7 @@ struct RowOpsSave {
 __device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
                                         const float* gam, int T, int max_iter, float eps, float* slots) {
   constexpr int VS = RowsGeo::VSTR;
+  TMPC_PROF_INIT
   RowOps o;
   saved.load(o);
   const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
@@ -329,8 +318,11 @@ __device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th
     prow[q] = p[0];
     prow[q + 8] = p[1];
     __syncthreads();
+    TMPC_PROF(12);
     rows_smv(y, o, th_row, bt);
+    TMPC_PROF(13);
     float den = rows_block_sum(fmaf(p[1], y[1], p[0] * y[0]), slots + 16);
+    TMPC_PROF(14);
     if (fabsf(den) < 1e-30f) den = 1e-30f;
     const float alpha = eta / den;
     x[0] = fmaf(alpha, p[0], x[0]);
@@ -338,6 +330,7 @@ __device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th
     r[0] = fmaf(-alpha, y[0], r[0]);
     r[1] = fmaf(-alpha, y[1], r[1]);
     rows_prec(z, r, o, bt, q);
+    TMPC_PROF(15);
     const float en = rows_block_sum(fmaf(r[1], z[1], r[0] * z[0]), slots);
     const float beta = en / eta;
     eta = en;
@@ -352,15 +345,106 @@ __device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th
   return it;
 }
 
-// Assembly of Theta / Phi / -Theta^-1 into shared memory (not inlined: the
-// kernel's resident operator registers are dead here, and a call boundary
-// keeps the Gauss-Jordan register demand out of the ADMM loop's allocation).
-__device__ __noinline__ void rows_assemble(const RowsAcc acc, const QPView<float> qg, float rho_f, float rho,
-                                           float sigma, int T, int n, int nx, int n0, int m, int* flag) {
-  assemble_theta_phi<16>(acc, qg, rho_f, rho, sigma, T, n, nx, n0, m);
+// Operator build for one rho (the math of admm.py:71-154, restated per owner
+// thread): Theta_t into shared memory from the staged QP (D and E from global
+// memory), -Theta_t^-1 by warp Gauss-Jordan in rounds of one block per warp
+// handed over through the warp's slot, and the Phi rows computed directly by
+// the threads that own them.  Every thread's operator rows go to its save
+// area.  Not inlined: the Gauss-Jordan register demand stays out of the ADMM
+// loop's allocation.  Ends with a barrier.
+__device__ __noinline__ void rows_build(float* sm, const RowsSmem* Lp, const QPView<float> qg,
+                                        const QPView<float> qs, float rho_f, float rho, float sigma, int T, int n,
+                                        int nx, int n0, int m, int* flag, RowOpsSave* save) {
+  const RowsSmem& L = *Lp;
+  float* th = sm + L.th;
+  const int N = T - 1;
+  TMPC_PROF_INIT
+#pragma unroll 4
+  for (int e = threadIdx.x; e < T * 256; e += blockDim.x) {
+    const int t = e >> 8, i = (e >> 4) & 15, j = e & 15;
+    float val = 0.f;
+    if (i < n && j < n) {
+      val = qg.D[((size_t)t * n + i) * n + j];
+      if (i == j) val += sigma;
+      float gtg = 0.f;
+      for (int k = 0; k < m; ++k) gtg += qs.G[(t * m + k) * n + i] * qs.G[(t * m + k) * n + j];
+      val += rho * gtg;
+      float ata = 0.f;
+      if (t == 0) {
+        for (int k = 0; k < n0; ++k) ata += qs.A0[k * n + i] * qs.A0[k * n + j];
+        if (N > 0)
+          for (int k = 0; k < nx; ++k) ata += qs.Am[k * n + i] * qs.Am[k * n + j];
+      } else {
+        const float* ap = qs.Ap + (t - 1) * nx * n;
+        for (int k = 0; k < nx; ++k) ata += ap[k * n + i] * ap[k * n + j];
+        if (t < N) {
+          const float* am = qs.Am + t * nx * n;
+          for (int k = 0; k < nx; ++k) ata += am[k * n + i] * am[k * n + j];
+        }
+      }
+      val += rho_f * ata;
+    }
+    th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j] = val;
+  }
   __syncthreads();
-  invert_thetas<16, float>(acc, T, n, flag);
+  TMPC_PROF(2);
+  const int t_own = threadIdx.x >> 3, q = threadIdx.x & 7;
+  const int nw = blockDim.x >> 5;
+  for (int base = 0; base < T; base += nw) {
+    const RowsInvAcc ia{th, sm + L.tslot, base};
+    invert_thetas<16, float>(ia, T, n, flag, base, base + nw < T ? base + nw : T);
+    __syncthreads();
+    if (t_own >= base && t_own < base + nw && t_own < T) {
+      const float* blk = sm + L.tslot + (t_own - base) * RowsGeo::SQ;
+      for (int a = 0; a < 2; ++a)
+        for (int k = 0; k < 16; ++k) save->v[a * 16 + k] = -blk[(q + 8 * a) * 16 + k];
+    }
+    __syncthreads();
+  }
+  TMPC_PROF(3);
+  // E entries first (16 global loads in flight per row), then the sums from
+  // the staged Ap / Am.
+#pragma unroll 1
+  for (int a = 0; a < 2; ++a) {
+    const int j = q + 8 * a;
+    if (t_own >= T)
+      for (int k = 0; k < 16; ++k) save->v[a * 16 + k] = 0.f;
+    // S(t, t-1) = Phi_{t-1}: row j, Phi_{t-1}[j][k] = E[j][k] + rho_f sum_kk Ap[kk][j] Am[kk][k]
+    const bool lo = t_own >= 1 && t_own < T && j < n;
+    float ev[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ev[k] = (lo && k < n) ? qg.E[((size_t)(t_own - 1) * n + j) * n + k] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float v = 0.f;
+      if (lo && k < n) {
+        const float* ap = qs.Ap + (t_own - 1) * nx * n;
+        const float* am = qs.Am + (t_own - 1) * nx * n;
+        float sum = 0.f;
+        for (int kk = 0; kk < nx; ++kk) sum += ap[kk * n + j] * am[kk * n + k];
+        v = ev[k] + rho_f * sum;
+      }
+      save->v[32 + a * 16 + k] = v;
+    }
+    // S(t, t+1) = Phi_t^T: row j is column j of Phi_t, Phi_t[k][j] = E[k][j] + rho_f sum_kk Ap[kk][k] Am[kk][j]
+    const bool up = t_own < N && j < n;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ev[k] = (up && k < n) ? qg.E[((size_t)t_own * n + k) * n + j] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float v = 0.f;
+      if (up && k < n) {
+        const float* ap = qs.Ap + t_own * nx * n;
+        const float* am = qs.Am + t_own * nx * n;
+        float sum = 0.f;
+        for (int kk = 0; kk < nx; ++kk) sum += ap[kk * n + k] * am[kk * n + j];
+        v = ev[k] + rho_f * sum;
+      }
+      save->v[64 + a * 16 + k] = v;
+    }
+  }
   __syncthreads();
+  TMPC_PROF(4);
 }
 
 // Staged QP view rebuilt at each use from the offsets in shared memory (kept
@@ -392,6 +476,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   __shared__ int flag;
   const int b = blockIdx.x;
   if (b >= P.Nb) return;
+  TMPC_PROF_INIT
 #define TMPC_RS(f) (sm + Ls.f)
   if (threadIdx.x == 0) {
     Ls = RowsSmem(P.T, P.n, P.nx, P.n0, P.m);
@@ -429,25 +514,25 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   }
   R rho = static_cast<const R*>(P.in.rho_bar)[b];
 
-  // Theta and Phi into shared memory, -Theta^-1 by warp Gauss-Jordan, the
-  // operator rows into the per-thread save area, then the QP copy into the
-  // stage area that held the scratch.  Ends with a barrier.
+  // The QP copy into the stage area (once), then the operator build; the
+  // build is repeated when rho changes.  Both end with a barrier.
   RowOpsSave ops;
+  __syncthreads();
+  TMPC_PROF(0);
+  {
+    const QPView<R> qg = qp_view<R>(P.qp, b, P.T, P.n, P.nx, P.n0, P.m);
+    rows_stage_qp(sm, Ls, qg, P.T, P.n, P.nx, P.n0, P.m);
+    __syncthreads();
+  }
+  TMPC_PROF(1);
   auto build_operators = [&](R rho_now) {
     const int T = P.T, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
-    const RowsAcc acc{TMPC_RS(th), TMPC_RS(phi), TMPC_RS(tinv)};
     const QPView<R> qg = qp_view<R>(P.qp, b, T, n, nx, n0, m);
-    rows_assemble(acc, qg, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m, &flag);
-    {
-      RowOps o;
-      rows_load_ops(o, acc, threadIdx.x >> 3, threadIdx.x & 7, T);
-      ops.store(o);
-    }
-    __syncthreads();
-    rows_stage_qp(sm, Ls, qg, T, n, nx, n0, m);
-    __syncthreads();
+    const QPView<R> qs = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
+    rows_build(sm, &Ls, qg, qs, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m, &flag, &ops);
   };
   build_operators(rho);
+  TMPC_PROF(5);  // (phases 2-4 timed inside the build; this is the call overhead)
 
   uint32_t iters = (uint32_t)P.max_iter;
   for (int it = 0; it < P.max_iter; ++it) {
@@ -467,13 +552,16 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
       TMPC_FOR_ENTRIES(e, o, T, NB, RowsGeo::VSTR) { xold[o] = xs[o]; }
       __syncthreads();
     }
+    TMPC_PROF(6);
     rows_pcg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
              TMPC_RS(red) + kRedSlots);
+    TMPC_PROF(7);
     {
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
       apply_constraints<NB>(TMPC_RS(cx0), TMPC_RS(cx), TMPC_RS(gx), TMPC_RS(x), qp, T, n, nx, n0, m);
       __syncthreads();
     }
+    TMPC_PROF(8);
     {
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
       const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
@@ -482,6 +570,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
                            P.use_slack != 0, T, nx, n0, m);
       __syncthreads();
     }
+    TMPC_PROF(9);
     if (P.check_every > 0 && (it % P.check_every) == 0) {
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
       const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
@@ -502,6 +591,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   }
 
   // ---- store
+  TMPC_PROF(10);
   bool nonfinite = false;
   {
     const int T = P.T, N = T - 1, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
@@ -534,6 +624,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
 #undef TMPC_RS
   if (nonfinite) atomicOr(&flag, TMPC_STATUS_NONFINITE);
   __syncthreads();
+  TMPC_PROF(11);
   if (threadIdx.x == 0) {
     static_cast<R*>(P.out.rho_bar)[b] = rho;
     if (P.iters_out) P.iters_out[b] = iters;

@@ -150,14 +150,16 @@ __device__ void assemble_theta_phi(const Acc& acc, const QPView<R>& qp, R rho_f,
   }
 }
 
-// Phase 2: one warp inverts Theta_t for t = warp, warp + nwarps, ... and
-// stores -Theta_t^-1.  Sets *flag when a pivot is zero or not finite.
+// Phase 2: one warp inverts Theta_t for t = t0 + warp, t0 + warp + nwarps,
+// ... < t1 and stores -Theta_t^-1.  Sets *flag when a pivot is zero or not
+// finite.
 template <int NB, typename R, class Acc>
-__device__ void invert_thetas(const Acc& acc, int T, int n, int* flag) {
+__device__ void invert_thetas(const Acc& acc, int T, int n, int* flag, int t0 = 0, int t1 = -1) {
   constexpr int CPL = (2 * NB + 31) / 32;  // augmented columns per lane
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nw = (blockDim.x + 31) >> 5;
-  for (int t = wid; t < T; t += nw) {
+  if (t1 < 0) t1 = T;
+  for (int t = t0 + wid; t < t1; t += nw) {
     R a[CPL][NB];
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {

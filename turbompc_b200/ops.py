@@ -169,6 +169,35 @@ def pcg_solve_packed(ops: torch.Tensor, dims: _ffi.TmpcDims, rhs: torch.Tensor, 
     return x, it.to(torch.int64) & 0xFFFFFFFF
 
 
+def schur_assemble_stream(qp: QPData, rho_bar, sigma: float, rho_f_factor: float):
+    """S and Phiinv in the stream layout (full blocks, for the HBM-streaming
+    PCG); returns (ops tensor of the QP's dtype, flat, status)."""
+    lib = _ffi.load()
+    d, q = dims_of(qp), _qp_c(qp)
+    nbytes = lib.tmpc_stream_operator_bytes(C.byref(d), qp.dtype.itemsize)
+    if nbytes == 0 and qp.Nb > 0:
+        raise ValueError(f"unsupported dimensions for the stream layout (n={qp.n})")
+    ops = torch.empty(max(nbytes // qp.dtype.itemsize, 4), dtype=qp.dtype, device=qp.device)
+    st = torch.zeros(qp.Nb, dtype=torch.int32, device=qp.device)
+    rho = _rho_vec(rho_bar, qp)
+    name = f"tmpc_schur_assemble_stream_{_suffix(qp.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), C.byref(q), _ptr(rho), float(sigma), float(rho_f_factor),
+                                        ops.data_ptr(), _ptr(st), _stream(qp.device)))
+    return ops, st
+
+
+def pcg_solve_stream(ops: torch.Tensor, dims: _ffi.TmpcDims, rhs: torch.Tensor, x0: torch.Tensor, eps: float,
+                     max_iters: int, x_out: Optional[torch.Tensor] = None):
+    """HBM-streaming PCG on stream-layout operators (schur_assemble_stream)."""
+    lib = _ffi.load()
+    x = torch.empty_like(rhs) if x_out is None else x_out
+    it = torch.empty(rhs.shape[0], dtype=torch.int32, device=rhs.device)
+    name = f"tmpc_pcg_solve_stream_{_suffix(rhs.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(dims), _ptr(ops, rhs.dtype), _ptr(rhs), _ptr(x0, rhs.dtype),
+                                        _ptr(x), _ptr(it), float(eps), int(max_iters), _stream(rhs.device)))
+    return x, it.to(torch.int64) & 0xFFFFFFFF
+
+
 def admm_workspace_bytes(qp: QPData, cfg: AdmmConfig) -> int:
     lib = _ffi.load()
     d = dims_of(qp)
