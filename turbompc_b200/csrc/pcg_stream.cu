@@ -81,57 +81,131 @@ __global__ void __launch_bounds__(256) assemble_stream_kernel(TmpcQP qpa, const 
 
 constexpr int kStreamThreads = 256;
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(a), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Per-warp staging buffer size (elements): 2 slots x stages per pass x {D, L}.
+template <int NB, int G>
+__host__ __device__ constexpr int stream_wbuf_elems() {
+  return 2 * (32 / G) * 2 * NB * NB;
+}
+
+// Lane-local part of one stage: column c of D_t and L_t in dcol / lcol.
+template <int NB, typename R, int G>
+__device__ __forceinline__ void stream_stage(const R (&dcol)[NB], const R (&lcol)[NB], const R* v, R* y, R* lo,
+                                             int t, int c, bool valid, bool hasL) {
+  const bool act = c < NB;
+  const R* vt = v + (size_t)(valid ? t : 0) * NB;
+  const R* vn = v + (size_t)(hasL ? t + 1 : 0) * NB;
+  R acc = R(0), accT = R(0);
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    acc = fma(dcol[k], vt[k], acc);
+    accT = fma(lcol[k], hasL ? vn[k] : R(0), accT);
+  }
+  // (L_t v_t)[k] = sum over the group's lanes c of L[k][c] v_t[c].
+  const R vc = act ? vt[c] : R(0);
+  R part[G];
+#pragma unroll
+  for (int k = 0; k < G; ++k) part[k] = k < NB ? lcol[k] * vc : R(0);
+  // Recursive halving inside the group: after the step with offset o a lane
+  // keeps the half of the current index range selected by its bit o.
+#pragma unroll
+  for (int o = G / 2, len = G / 2; o > 0; o >>= 1, len >>= 1) {
+    const bool up = (c & o) != 0;
+#pragma unroll
+    for (int i = 0; i < len; ++i) {
+      const R send = up ? part[i] : part[i + len];
+      const R keep = up ? part[i + len] : part[i];
+      part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o, 32);
+    }
+  }
+  if (valid && act) {
+    y[(size_t)t * NB + c] = acc + accT;
+    if (hasL) lo[(size_t)(t + 1) * NB + c] = part[0];
+  }
+}
+
 // One matvec y_pre = (D v + L^T v_next), lo = L v (shifted one stage); the
 // caller syncs and adds lo.  v, y, lo: [T][NB] on chip (lo[0] stays zero).
-template <int NB, typename R, int G>
-__device__ __forceinline__ void stream_matvec(const R* __restrict__ op, int T, const R* v, R* y, R* lo) {
+// STAGE: each warp double-buffers its next pass's blocks in shared memory
+// with cp.async (16-byte copies, no registers held), so a warp always has a
+// whole pass of blocks in flight; otherwise the columns are loaded straight
+// into registers.
+template <int NB, typename R, int G, bool STAGE>
+__device__ __forceinline__ void stream_matvec(const R* __restrict__ op, int T, const R* v, R* y, R* lo, R* wbuf) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int sub = lane / G, c = lane % G;  // stage slot in the warp, row / column owned
   constexpr int SPW = 32 / G;              // stages per warp pass
+  constexpr int B2 = NB * NB;
   const int nw = blockDim.x >> 5;
-  const size_t B2 = (size_t)NB * NB;
   const int N = T - 1;
   const bool act = c < NB;
-  for (int t0 = wid * SPW; t0 < T; t0 += nw * SPW) {  // warp-uniform trip count
-    const int t = t0 + sub;
-    const bool valid = t < T;
-    const R* Dt = op + (size_t)(valid ? t : 0) * B2;
-    const R* Lt = op + (size_t)T * B2 + (size_t)(valid && t < N ? t : 0) * B2;
-    const bool hasL = valid && t < N;
-    R dcol[NB], lcol[NB];
+  if constexpr (!STAGE) {
+    for (int t0 = wid * SPW; t0 < T; t0 += nw * SPW) {  // warp-uniform trip count
+      const int t = t0 + sub;
+      const bool valid = t < T;
+      const bool hasL = valid && t < N;
+      const R* Dt = op + (size_t)(valid ? t : 0) * B2;
+      const R* Lt = op + (size_t)T * B2 + (size_t)(hasL ? t : 0) * B2;
+      R dcol[NB], lcol[NB];
 #pragma unroll
-    for (int k = 0; k < NB; ++k) dcol[k] = (valid && act) ? __ldg(Dt + k * NB + c) : R(0);
+      for (int k = 0; k < NB; ++k) dcol[k] = (valid && act) ? __ldg(Dt + k * NB + c) : R(0);
 #pragma unroll
-    for (int k = 0; k < NB; ++k) lcol[k] = (hasL && act) ? __ldg(Lt + k * NB + c) : R(0);
-    const R* vt = v + (size_t)(valid ? t : 0) * NB;
-    const R* vn = v + (size_t)(hasL ? t + 1 : 0) * NB;
-    R acc = R(0), accT = R(0);
-#pragma unroll
-    for (int k = 0; k < NB; ++k) {
-      acc = fma(dcol[k], vt[k], acc);
-      accT = fma(lcol[k], hasL ? vn[k] : R(0), accT);
+      for (int k = 0; k < NB; ++k) lcol[k] = (hasL && act) ? __ldg(Lt + k * NB + c) : R(0);
+      stream_stage<NB, R, G>(dcol, lcol, v, y, lo, t, c, valid, hasL);
     }
-    // (L_t v_t)[k] = sum over the group's lanes c of L[k][c] v_t[c].
-    const R vc = act ? vt[c] : R(0);
-    R part[G];
+  } else {
+    constexpr int VEC = 16 / (int)sizeof(R);
+    constexpr int CH = B2 / VEC;  // 16-byte chunks per block
+    auto issue = [&](int t0, int slot) {
 #pragma unroll
-    for (int k = 0; k < G; ++k) part[k] = k < NB ? lcol[k] * vc : R(0);
-    // Recursive halving inside the group: after the step with offset o a lane
-    // keeps the half of the current index range selected by its bit o.
-#pragma unroll
-    for (int o = G / 2, len = G / 2; o > 0; o >>= 1, len >>= 1) {
-      const bool up = (c & o) != 0;
-#pragma unroll
-      for (int i = 0; i < len; ++i) {
-        const R send = up ? part[i] : part[i + len];
-        const R keep = up ? part[i + len] : part[i];
-        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o, 32);
+      for (int s2 = 0; s2 < SPW; ++s2) {
+        const int t = t0 + s2;
+        R* dst = wbuf + (size_t)(slot * SPW + s2) * 2 * B2;
+        if (t < T) {
+          const R* Dt = op + (size_t)t * B2;
+          for (int k = lane; k < CH; k += 32) cp_async16(dst + k * VEC, Dt + k * VEC);
+          if (t < N) {
+            const R* Lt = op + (size_t)T * B2 + (size_t)t * B2;
+            for (int k = lane; k < CH; k += 32) cp_async16(dst + B2 + k * VEC, Lt + k * VEC);
+          }
+        }
       }
+      cp_async_commit();
+    };
+    int slot = 0;
+    const int step = nw * SPW;
+    issue(wid * SPW, 0);
+    for (int t0 = wid * SPW; t0 < T; t0 += step) {
+      if (t0 + step < T) {
+        issue(t0 + step, slot ^ 1);
+      } else {
+        cp_async_commit();  // empty group keeps the wait count uniform
+      }
+      cp_async_wait<1>();
+      __syncwarp();
+      const int t = t0 + sub;
+      const bool valid = t < T;
+      const bool hasL = valid && t < N;
+      const R* blk = wbuf + (size_t)(slot * SPW + sub) * 2 * B2;
+      R dcol[NB], lcol[NB];
+#pragma unroll
+      for (int k = 0; k < NB; ++k) dcol[k] = (valid && act) ? blk[k * NB + c] : R(0);
+#pragma unroll
+      for (int k = 0; k < NB; ++k) lcol[k] = (hasL && act) ? blk[B2 + k * NB + c] : R(0);
+      stream_stage<NB, R, G>(dcol, lcol, v, y, lo, t, c, valid, hasL);
+      __syncwarp();  // every lane is done with this slot before it is refilled
+      slot ^= 1;
     }
-    if (valid && act) {
-      y[(size_t)t * NB + c] = acc + accT;
-      if (hasL) lo[(size_t)(t + 1) * NB + c] = part[0];
-    }
+    cp_async_wait<0>();
   }
 }
 
@@ -146,7 +220,7 @@ __device__ __forceinline__ R stream_block_sum(R v, R* slots) {
   return s;
 }
 
-template <int NB, typename R>
+template <int NB, typename R, bool STAGE>
 __global__ void __launch_bounds__(kStreamThreads) pcg_stream_kernel(const R* __restrict__ ops,
                                                                    const R* __restrict__ rhs,
                                                                    const R* __restrict__ x0, R* x_out,
@@ -166,6 +240,7 @@ __global__ void __launch_bounds__(kStreamThreads) pcg_stream_kernel(const R* __r
   R* y = sm + 2 * VS;
   R* lo = sm + 3 * VS;
   R* red = sm + 4 * VS;  // 2 x 32 slots
+  R* wbuf = red + 64 + (size_t)(threadIdx.x >> 5) * stream_wbuf_elems<NB, G>();  // 16-byte aligned
   const int tot = T * n;
   R* x = x_out + (size_t)b * tot;
   const R* g = rhs + (size_t)b * tot;
@@ -179,7 +254,7 @@ __global__ void __launch_bounds__(kStreamThreads) pcg_stream_kernel(const R* __r
   }
   __syncthreads();
   auto matvec = [&](const R* op, const R* v) {
-    stream_matvec<NB, R, G>(op, T, v, y, lo);
+    stream_matvec<NB, R, G, STAGE>(op, T, v, y, lo, wbuf);
     __syncthreads();
   };
   auto idx = [&](int e) { return (e / n) * NB + (e % n); };
@@ -242,16 +317,27 @@ __global__ void __launch_bounds__(kStreamThreads) pcg_stream_kernel(const R* __r
 }
 
 template <int NB, typename R>
-size_t stream_smem_bytes(int T) {
-  return (4 * (size_t)T * NB + 64) * sizeof(R);
+size_t stream_smem_bytes(int T, bool stage) {
+  constexpr int G = NB <= 16 ? 16 : 32;
+  // 4 T NB is a multiple of 4 elements, so the staging buffers start 16-byte aligned.
+  const size_t wb = stage ? (size_t)(kStreamThreads / 32) * stream_wbuf_elems<NB, G>() : 0;
+  return (4 * (size_t)T * NB + 64 + wb) * sizeof(R);
 }
 
 template <int NB, typename R>
 int launch_pcg_stream(const TmpcDims* d, const R* o, const R* rhs, const R* x0, R* xo, uint32_t* it, R eps,
                       int max_iter, cudaStream_t st) {
-  const size_t smem = stream_smem_bytes<NB, R>(d->T);
-  if ((long)smem > max_dyn_smem()) return TMPC_ERR_SMEM;
-  auto k = pcg_stream_kernel<NB, R>;
+  const long smax = max_dyn_smem();
+  const size_t s_stage = stream_smem_bytes<NB, R>(d->T, true);
+  const bool aligned = (reinterpret_cast<uintptr_t>(o) & 15) == 0;
+  // Measured on B200: staging pays for the large blocks (NB >= 24: 93 % of
+  // the measured HBM copy bandwidth at n = 32, T = 129, fp32, against 47 %
+  // with register loads); for NB <= 16 the register path keeps more CTAs per
+  // SM and is faster.
+  const bool stage = NB >= 24 && aligned && (long)s_stage <= smax;
+  const size_t smem = stage ? s_stage : stream_smem_bytes<NB, R>(d->T, false);
+  if ((long)smem > smax) return TMPC_ERR_SMEM;
+  auto k = stage ? pcg_stream_kernel<NB, R, true> : pcg_stream_kernel<NB, R, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   k<<<d->Nb, kStreamThreads, smem, st>>>(o, rhs, x0, xo, it, eps, max_iter, d->Nb, d->T, d->n);
