@@ -83,3 +83,28 @@ def test_solver_builds_qp_on_cpu():
     guess = s.initial_guess(p)
     qp = s._build_qp_data(guess.states, guess.controls, p)
     assert (qp.Nb, qp.T, qp.n, qp.nx, qp.n0, qp.m) == (2, 6, 16, 12, 12, 4)
+
+
+def test_learned_cost_quadratisation_matches_autograd():
+    """Config 5 cost: D and q of the MLP-augmented stage cost equal the
+    autograd Hessian / gradient-minus-Hessian-times-point of cost()."""
+    import torch
+    from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    prog, params = make_learned_cost_problem(2, N=4, hidden=8, seed=1, dtype=torch.float64, device="cpu")
+    g = torch.Generator().manual_seed(0)
+    xs = torch.randn(2, 5, 6, generator=g, dtype=torch.float64)
+    us = 0.05 * torch.randn(2, 5, 3, generator=g, dtype=torch.float64)
+    D, E, q = prog.get_cost_linearized_blocks(xs, us, params)
+    z = torch.cat([xs, us], -1).reshape(-1).requires_grad_(True)
+    f = lambda zz: prog.cost(zz.view(2, 5, 9)[..., :6], zz.view(2, 5, 9)[..., 6:], params).sum()
+    Hf = torch.autograd.functional.hessian(f, z).view(2, 5, 9, 2, 5, 9)
+    grad = torch.autograd.grad(f(z), z)[0].view(2, 5, 9)
+    for b in range(2):
+        for t in range(5):
+            assert torch.allclose(D[b, t], Hf[b, t, :, b, t, :], atol=1e-10)
+    zz = z.detach().view(2, 5, 9)
+    Pz = torch.einsum("btij,btj->bti", D, zz)
+    Pz[:, 1:] += torch.einsum("btij,btj->bti", E, zz[:, :-1])
+    Pz[:, :-1] += torch.einsum("btji,btj->bti", E, zz[:, 1:])
+    assert torch.allclose(q, grad - Pz, atol=1e-9)
+    assert (torch.linalg.eigvalsh(D) > 0).all()
