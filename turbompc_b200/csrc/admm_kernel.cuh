@@ -49,7 +49,7 @@ struct AdmmSmem {
     ct = a4(o); o = ct + n0 + (size_t)N * nx;
     gt = a4(o); o = gt + (size_t)T * m;
     red = a4(o); o = red + kRedSize;
-    fm = a4(o); o = fm + (nvec == 4 ? (size_t)NB * (NB + 1) : 0);  // Cholesky scratch (direct)
+    fm = a4(o); o = fm + (nvec == 4 ? (size_t)riccati_scratch_elems<NB>() : 0);  // Cholesky scratch (direct)
     nelem = a4(o);
   }
 };

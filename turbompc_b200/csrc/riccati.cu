@@ -7,6 +7,13 @@
 namespace tmpc {
 
 constexpr int kRicWarps = 4;
+// Warps (= problems) per block: up to 4 within 40 KB of static shared memory.
+template <int NB, typename R>
+constexpr int ric_warps() {
+  constexpr int per = riccati_scratch_elems<NB>() * (int)sizeof(R);
+  constexpr int w = 40960 / per;
+  return w < 1 ? 1 : (w > kRicWarps ? kRicWarps : w);
+}
 
 // Copy Theta_t / Phi_t out of the reference-layout S into the packed factor
 // slots, then factor.  One warp per problem.
@@ -14,23 +21,21 @@ template <int NB, typename R>
 __global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R* __restrict__ S, R* factor,
                                                                         int32_t* status, int Nb, int T, int n) {
   using Gm = Geo<NB, R>;
-  __shared__ R Msh[kRicWarps][NB * (NB + 1)];
+  constexpr int WPB = ric_warps<NB, R>();
+  __shared__ R Msh[WPB][riccati_scratch_elems<NB>()];
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x * kRicWarps + wid;
+  const int b = blockIdx.x * WPB + wid;
   if (b >= Nb) return;
   const size_t opn = Gm::op_elems(T);
   const FactorView<NB, R> F{factor + (size_t)b * opn, T};
   const R* Sb = S + (size_t)b * T * n * 3 * n;
   for (int t = 0; t < T; ++t) {
     R* th = F.lt(t);
-    for (int e = lane; e < Gm::DSTR; e += 32) {
-      R v = R(0);
-      if (e < Gm::TRI) {
-        const int i = tri_row(e, NB), j = tri_col(e, NB);
-        if (i < n && j < n) v = Sb[((size_t)t * n + i) * 3 * n + n + j];
-      }
-      th[e] = v;
+    for (int e = lane; e < NB * NB; e += 32) {  // (i, j), i <= j, into the packed slot
+      const int i = e / NB, j = e - i * NB;
+      if (i <= j) th[tri_index(i, j, NB)] = (i < n && j < n) ? Sb[((size_t)t * n + i) * 3 * n + n + j] : R(0);
     }
+    for (int e = Gm::TRI + lane; e < Gm::DSTR; e += 32) th[e] = R(0);
     if (t + 1 < T) {
       R* W = F.w(t);
       for (int e = lane; e < NB * NB; e += 32) {
@@ -80,9 +85,9 @@ int riccati_factor(const TmpcDims* d, const R* S, void* factor, int32_t* status,
   if (!S || !factor) return TMPC_ERR_NULL_ARG;
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    const int grid = (d->Nb + kRicWarps - 1) / kRicWarps;
-    riccati_factor_kernel<NB, R><<<grid, 32 * kRicWarps, 0, st>>>(S, static_cast<R*>(factor), status, d->Nb, d->T,
-                                                                   d->n);
+    constexpr int WPB = ric_warps<NB, R>();  // the kernel indexes its scratch by warp: launch exactly WPB warps
+    const int grid = (d->Nb + WPB - 1) / WPB;
+    riccati_factor_kernel<NB, R><<<grid, 32 * WPB, 0, st>>>(S, static_cast<R*>(factor), status, d->Nb, d->T, d->n);
     return (int)cudaPeekAtLastError();
   });
 }

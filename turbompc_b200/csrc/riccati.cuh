@@ -31,16 +31,26 @@ struct FactorView {
   __device__ R* w(int t) const { return base + (size_t)T * Gm::DSTR + (size_t)t * Gm::OSTR; }
 };
 
+// Per-warp shared scratch of riccati_factor_warp (elements): the working
+// block M (NB x (NB+1)) and a copy of the previous W (NB x NB).
+template <int NB>
+__host__ __device__ constexpr int riccati_scratch_elems() {
+  return NB * (NB + 1) + NB * NB;
+}
+
 // Factor one problem in place.  On entry slot t holds Theta_t (packed upper,
 // as written by assemble_theta_phi) and sub-diagonal slot t holds Phi_t; on
-// exit they hold L_t^T and W_t.  M is per-warp shared scratch of NB*(NB+1)
-// elements.  Called by all 32 lanes of one warp; returns false (all lanes)
-// when a pivot is not positive and finite.
+// exit they hold L_t^T and W_t.  M is per-warp shared scratch of
+// riccati_scratch_elems<NB>() elements (W_{t-1} is kept there for the Schur
+// update, so it is not re-read from global memory).  Called by all 32 lanes
+// of one warp; returns false (all lanes) when a pivot is not positive and
+// finite.
 template <int NB, typename R>
 __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
   constexpr int LD = NB + 1;
   const int lane = threadIdx.x & 31;
   const int T = F.T;
+  R* Wsh = M + NB * LD;  // W_{t-1}, row-major
   bool ok = true;
   for (int t = 0; t < T; ++t) {
     const R* th = F.lt(t);
@@ -50,10 +60,9 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
       if (r < n && c < n) {
         v = r <= c ? th[tri_index(r, c, NB)] : th[tri_index(c, r, NB)];
         if (t > 0) {
-          const R* Wp = F.w(t - 1);
           R s = R(0);
-#pragma unroll 4
-          for (int k = 0; k < NB; ++k) s = fma(Wp[r * NB + k], Wp[c * NB + k], s);
+#pragma unroll 8
+          for (int k = 0; k < NB; ++k) s = fma(Wsh[r * NB + k], Wsh[c * NB + k], s);
           v -= s;
         }
       } else {
@@ -99,7 +108,10 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
           wv[k] = s / M[k * LD + k];
         }
 #pragma unroll
-        for (int k = 0; k < NB; ++k) W[lane * NB + k] = wv[k];
+        for (int k = 0; k < NB; ++k) {
+          W[lane * NB + k] = wv[k];
+          Wsh[lane * NB + k] = wv[k];
+        }
       }
     }
     __syncwarp();
