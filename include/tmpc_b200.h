@@ -36,7 +36,7 @@ extern "C" {
 #define TMPC_ERR_NULL_ARG (-1)
 #define TMPC_ERR_BAD_DIMS (-2)
 #define TMPC_ERR_UNSUPPORTED (-3)
-#define TMPC_ERR_WORKSPACE (-4)
+#define TMPC_ERR_WORKSPACE (-4) /* workspace / factor buffer missing, too small or not 16-byte aligned */
 #define TMPC_ERR_SMEM (-5)
 #define TMPC_ERR_SCRATCH_LIMIT (-6) /* needs more scratch than the fixed device buffer holds */
 

@@ -492,7 +492,7 @@ size_t admm_smem_bytes(int T, int nx, int n0, int m, bool ops_smem) {
 template <int NB, typename R>
 int launch_admm_direct_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st) {
   const size_t need = (size_t)P.Nb * Geo<NB, R>::op_elems(P.T) * sizeof(R);
-  if (P.ws == nullptr || ws_bytes < need) return TMPC_ERR_WORKSPACE;
+  if (P.ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(P.ws) & 15) != 0) return TMPC_ERR_WORKSPACE;
   const size_t smem = AdmmSmem<NB, R>(P.T, P.nx, P.n0, P.m, false, 4).nelem * sizeof(R);
   if ((long)smem > max_dyn_smem()) return TMPC_ERR_SMEM;
   auto k = admm_fused_kernel<NB, R, false, TMPC_LINSYS_DIRECT>;
@@ -515,7 +515,7 @@ int launch_admm_nb(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st) {
     return (int)cudaPeekAtLastError();
   }
   const size_t need = (size_t)P.Nb * 2 * Geo<NB, R>::op_elems(P.T) * sizeof(R);
-  if (P.ws == nullptr || ws_bytes < need) return TMPC_ERR_WORKSPACE;
+  if (P.ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(P.ws) & 15) != 0) return TMPC_ERR_WORKSPACE;
   const size_t s_str = admm_smem_bytes<NB, R>(P.T, P.nx, P.n0, P.m, false);
   if ((long)s_str > smax) return TMPC_ERR_SMEM;
   auto k = admm_fused_kernel<NB, R, false>;

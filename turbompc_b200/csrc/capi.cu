@@ -31,7 +31,7 @@ const char* tmpc_error_string(int32_t code) {
     case TMPC_ERR_NULL_ARG: return "null pointer argument";
     case TMPC_ERR_BAD_DIMS: return "invalid dimensions";
     case TMPC_ERR_UNSUPPORTED: return "unsupported configuration (block size n > 32 or unknown option)";
-    case TMPC_ERR_WORKSPACE: return "workspace missing or too small";
+    case TMPC_ERR_WORKSPACE: return "workspace or factor buffer missing, too small or not 16-byte aligned";
     case TMPC_ERR_SMEM: return "problem does not fit the shared-memory budget of one CTA";
     case TMPC_ERR_SCRATCH_LIMIT:
       return "batch needs more scratch than the fixed device buffer of tmpc_admm_solve_fixed_scratch_f64 holds "

@@ -22,7 +22,7 @@ __global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R*
                                                                         int32_t* status, int Nb, int T, int n) {
   using Gm = Geo<NB, R>;
   constexpr int WPB = ric_warps<NB, R>();
-  __shared__ R Msh[WPB][riccati_scratch_elems<NB>()];
+  __shared__ __align__(16) R Msh[WPB][riccati_scratch_elems<NB>()];
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x * WPB + wid;
   if (b >= Nb) return;
@@ -83,6 +83,7 @@ int riccati_factor(const TmpcDims* d, const R* S, void* factor, int32_t* status,
   if (d->Nb < 0 || d->T < 2 || d->n < 1) return TMPC_ERR_BAD_DIMS;
   if (d->Nb == 0) return TMPC_OK;
   if (!S || !factor) return TMPC_ERR_NULL_ARG;
+  if ((reinterpret_cast<uintptr_t>(factor) & 15) != 0) return TMPC_ERR_WORKSPACE;  // 128-bit stores of W
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
     constexpr int WPB = ric_warps<NB, R>();  // the kernel indexes its scratch by warp: launch exactly WPB warps

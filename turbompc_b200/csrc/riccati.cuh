@@ -31,86 +31,127 @@ struct FactorView {
   __device__ R* w(int t) const { return base + (size_t)T * Gm::DSTR + (size_t)t * Gm::OSTR; }
 };
 
-// Per-warp shared scratch of riccati_factor_warp (elements): the working
-// block M (NB x (NB+1)) and a copy of the previous W (NB x NB).
+// Per-warp shared scratch of riccati_factor_warp (elements): W_{t-1}
+// (row-major) and L_t (column-major), NB x NB each.
 template <int NB>
 __host__ __device__ constexpr int riccati_scratch_elems() {
-  return NB * (NB + 1) + NB * NB;
+  return 2 * NB * NB;
 }
 
 // Factor one problem in place.  On entry slot t holds Theta_t (packed upper,
 // as written by assemble_theta_phi) and sub-diagonal slot t holds Phi_t; on
 // exit they hold L_t^T and W_t.  M is per-warp shared scratch of
-// riccati_scratch_elems<NB>() elements (W_{t-1} is kept there for the Schur
-// update, so it is not re-read from global memory).  Called by all 32 lanes
-// of one warp; returns false (all lanes) when a pivot is not positive and
-// finite.
+// riccati_scratch_elems<NB>() elements, 16-byte aligned.  Called by all 32
+// lanes of one warp; returns false (all lanes) when a pivot is not positive
+// and finite.
+//
+// Lane j keeps column j of the stage's working matrix in registers:
+//   M_t = Theta_t - W_{t-1} W_{t-1}^T     (rows of W_{t-1} broadcast from shared memory)
+//   right-looking Cholesky: at step k lane k scales its column and publishes
+//   it (column k of L_t) in shared memory; lanes j > k update their columns
+//   W_t = Phi_t L_t^-T: lane i runs the forward substitution L w = Phi_t[i, :]^T
+//   column by column (column m of L broadcast from shared memory).
 template <int NB, typename R>
 __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
-  constexpr int LD = NB + 1;
+  static_assert(NB % 4 == 0, "128-bit shared-memory broadcasts");
+  constexpr int VEC = 16 / (int)sizeof(R);  // elements per 128-bit access
   const int lane = threadIdx.x & 31;
   const int T = F.T;
-  R* Wsh = M + NB * LD;  // W_{t-1}, row-major
+  R* Wsh = M;            // W_{t-1}: Wsh[r * NB + k]
+  R* Lsh = M + NB * NB;  // L_t:     Lsh[k * NB + r] = L[r][k]
+  const bool act = lane < NB;
+  const int j = act ? lane : 0;
   bool ok = true;
   for (int t = 0; t < T; ++t) {
+    R a[NB];
     const R* th = F.lt(t);
-    for (int e = lane; e < NB * NB; e += 32) {
-      const int r = e / NB, c = e - r * NB;
-      R v;
-      if (r < n && c < n) {
-        v = r <= c ? th[tri_index(r, c, NB)] : th[tri_index(c, r, NB)];
-        if (t > 0) {
-          R s = R(0);
-#pragma unroll 8
-          for (int k = 0; k < NB; ++k) s = fma(Wsh[r * NB + k], Wsh[c * NB + k], s);
-          v -= s;
+#pragma unroll
+    for (int r = 0; r < NB; ++r) {
+      R v = (r == j) ? R(1) : R(0);  // identity in the padded rows / columns
+      if (r < n && j < n) v = r <= j ? th[tri_index(r, j, NB)] : th[tri_index(j, r, NB)];
+      a[r] = v;
+    }
+    if (t > 0 && j < n) {
+      R wj[NB];
+#pragma unroll
+      for (int k = 0; k < NB; k += VEC) ld128(&wj[k], Wsh + j * NB + k);
+#pragma unroll
+      for (int r = 0; r < NB; ++r) {
+        R sacc = R(0);
+#pragma unroll
+        for (int k = 0; k < NB; k += VEC) {
+          R wv[VEC];
+          ld128(wv, Wsh + r * NB + k);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) sacc = fma(wv[e], wj[k + e], sacc);
         }
-      } else {
-        v = (r == c) ? R(1) : R(0);
+        if (r < n) a[r] -= sacc;
       }
-      M[r * LD + c] = v;
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      if (lane == k) {
+        const R d = a[k];
+        if (!(d > R(0)) || !isfinite(d)) ok = false;
+        const R sq = sqrt(d);
+        const R inv = R(1) / sq;
+        a[k] = sq;
+#pragma unroll
+        for (int r = k + 1; r < NB; ++r) a[r] *= inv;
+#pragma unroll
+        for (int r = 0; r < NB; r += VEC) {
+          R cv[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) cv[e] = (r + e >= k) ? a[r + e] : R(0);
+          st128(Lsh + k * NB + r, cv);
+        }
+      }
+      __syncwarp();
+      if (act && lane > k) {
+        const R ljk = Lsh[k * NB + j];
+#pragma unroll
+        for (int r0 = ((k + 1) / VEC) * VEC; r0 < NB; r0 += VEC) {
+          R lv[VEC];
+          ld128(lv, Lsh + k * NB + r0);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const int r = r0 + e;
+            if (r > k && r >= j) a[r] = fma(-lv[e], ljk, a[r]);
+          }
+        }
+      }
     }
     __syncwarp();
-    // Right-looking Cholesky on the lower triangle of M.
-    for (int k = 0; k < NB; ++k) {
-      const R d = M[k * LD + k];
-      if (!(d > R(0)) || !isfinite(d)) ok = false;
-      const R s = sqrt(d);
-      __syncwarp();
-      for (int r = k + 1 + lane; r < NB; r += 32) M[r * LD + k] /= s;
-      if (lane == 0) M[k * LD + k] = s;
-      __syncwarp();
-      const int m = NB - 1 - k;  // trailing size
-      for (int e = lane; e < m * m; e += 32) {
-        const int r = k + 1 + e / m, c = k + 1 + e % m;
-        if (c <= r) M[r * LD + c] -= M[r * LD + k] * M[c * LD + k];
-      }
-      __syncwarp();
-    }
-    // Store L_t^T packed (entry (a, b), a <= b, is L[b][a]).
+    // Store L_t^T packed (entry (a, b), a <= b, is L[b][a] = Lsh[a * NB + b]).
     R* lt = F.lt(t);
     for (int e = lane; e < NB * NB; e += 32) {
-      const int b = e / NB, a = e - b * NB;
-      if (a <= b) lt[tri_index(a, b, NB)] = M[b * LD + a];
+      const int bb = e / NB, aa = e - bb * NB;
+      if (aa <= bb) lt[tri_index(aa, bb, NB)] = Lsh[aa * NB + bb];
     }
-    // W_t = Phi_t L_t^-T: lane i solves L w = Phi_t[i, :]^T by forward substitution.
+    // W_t = Phi_t L_t^-T, row i = lane.
     if (t < T - 1) {
       R* W = F.w(t);
-      if (lane < NB) {
-        R wv[NB];
+      R x[NB];
 #pragma unroll
-        for (int k = 0; k < NB; ++k) wv[k] = W[lane * NB + k];
+      for (int k = 0; k < NB; ++k) x[k] = act ? W[j * NB + k] : R(0);
 #pragma unroll
-        for (int k = 0; k < NB; ++k) {
-          R s = wv[k];
+      for (int m = 0; m < NB; ++m) {
+        x[m] = x[m] / Lsh[m * NB + m];
 #pragma unroll
-          for (int m2 = 0; m2 < k; ++m2) s -= M[k * LD + m2] * wv[m2];
-          wv[k] = s / M[k * LD + k];
+        for (int r0 = ((m + 1) / VEC) * VEC; r0 < NB; r0 += VEC) {
+          R lv[VEC];
+          ld128(lv, Lsh + m * NB + r0);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e)
+            if (r0 + e > m) x[r0 + e] = fma(-lv[e], x[m], x[r0 + e]);
         }
+      }
+      __syncwarp();  // every lane is done reading W_{t-1} in this stage
+      if (act) {
 #pragma unroll
-        for (int k = 0; k < NB; ++k) {
-          W[lane * NB + k] = wv[k];
-          Wsh[lane * NB + k] = wv[k];
+        for (int k = 0; k < NB; k += VEC) {
+          st128(W + j * NB + k, &x[k]);
+          st128(Wsh + j * NB + k, &x[k]);
         }
       }
     }
@@ -143,9 +184,10 @@ __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y,
     R lcol[NB];  // L[li][k] = L^T packed (k, li) for k <= li
 #pragma unroll
     for (int k = 0; k < NB; ++k) lcol[k] = (k <= li) ? lt[tri_index(k, li, NB)] : R(0);
+    const R dinv = R(1) / lt[tri_index(li, li, NB)];  // 1 / L[li][li]
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
-      const R yk = __shfl_sync(0xffffffffu, u / lcol[k], k);  // valid in lane k: lcol[k] = L[k][k]
+      const R yk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
       if (li > k) u = fma(-lcol[k], yk, u);
       if (li == k) u = yk;
     }
@@ -167,9 +209,10 @@ __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y,
     R lrow[NB];  // L^T[li][k] = L[k][li] = packed (li, k) for k >= li
 #pragma unroll
     for (int k = 0; k < NB; ++k) lrow[k] = (k >= li) ? lt[tri_index(li, k, NB)] : R(0);
+    const R dinv = R(1) / lt[tri_index(li, li, NB)];
 #pragma unroll
     for (int k = NB - 1; k >= 0; --k) {
-      const R xk = __shfl_sync(0xffffffffu, u / lrow[k], k);  // lane k: lrow[k] = L[k][k]
+      const R xk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
       if (li < k) u = fma(-lrow[k], xk, u);
       if (li == k) u = xk;
     }

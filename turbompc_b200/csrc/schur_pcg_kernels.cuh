@@ -140,6 +140,7 @@ int launch_pcg_packed(const TmpcDims* d, const R* o, const R* rhs, const R* x0, 
   const int smax = max_dyn_smem();
   const size_t vec_bytes = (11 * (size_t)d->T * Gm::VSTR + 64) * sizeof(R);
   const size_t op_bytes = 2 * Gm::op_elems(d->T) * sizeof(R);
+  if ((reinterpret_cast<uintptr_t>(o) & 15) != 0) return TMPC_ERR_WORKSPACE;  // 128-bit / bulk copies of the operators
   if ((long)(vec_bytes + op_bytes) <= smax) {
     auto k = pcg_packed_kernel<NB, R, true>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(vec_bytes + op_bytes));
