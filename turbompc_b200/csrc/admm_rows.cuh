@@ -346,101 +346,213 @@ __device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th
 }
 
 // Operator build for one rho (the math of admm.py:71-154, restated per owner
-// thread): Theta_t into shared memory from the staged QP (D and E from global
-// memory), -Theta_t^-1 by warp Gauss-Jordan in rounds of one block per warp
-// handed over through the warp's slot, and the Phi rows computed directly by
-// the threads that own them.  Every thread's operator rows go to its save
-// area.  Not inlined: the Gauss-Jordan register demand stays out of the ADMM
-// loop's allocation.  Ends with a barrier.
+// thread).  Thread (t, q) computes rows q and q + 8 of every block it owns:
+//   Theta_t rows      D + sigma I + rho G^T G + rho_f (A^T A terms), from the
+//                     staged QP (rows of the A / G blocks broadcast from shared
+//                     memory), stored to shared memory for the S-matvec;
+//   Theta_t^-1 rows   Gauss-Jordan on [Theta_t | I] by the stage's eight
+//                     threads (one warp), pivot rows exchanged through shared
+//                     memory; Theta_t is symmetric positive definite, so the
+//                     elimination runs without row exchanges (the reference
+//                     inverts with pivoting, admm_math.cuh:248-310; the results
+//                     agree to rounding);
+//   Phi_{t-1} rows / Phi_t columns   E + rho_f Ap^T Am, in the reference's
+//                     summation order over the constraint rows.
+// Every thread's rows go to its save area.  Not inlined (its own register
+// allocation).  Ends with a barrier.
 __device__ __noinline__ void rows_build(float* sm, const RowsSmem* Lp, const QPView<float> qg,
                                         const QPView<float> qs, float rho_f, float rho, float sigma, int T, int n,
                                         int nx, int n0, int m, int* flag, RowOpsSave* save) {
   const RowsSmem& L = *Lp;
   float* th = sm + L.th;
   const int N = T - 1;
+  const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
+  const bool act = t < T;
+  const int tt = act ? t : 0;
   TMPC_PROF_INIT
-#pragma unroll 4
-  for (int e = threadIdx.x; e < T * 256; e += blockDim.x) {
-    const int t = e >> 8, i = (e >> 4) & 15, j = e & 15;
-    float val = 0.f;
-    if (i < n && j < n) {
-      val = qg.D[((size_t)t * n + i) * n + j];
-      if (i == j) val += sigma;
-      float gtg = 0.f;
-      for (int k = 0; k < m; ++k) gtg += qs.G[(t * m + k) * n + i] * qs.G[(t * m + k) * n + j];
-      val += rho * gtg;
-      float ata = 0.f;
-      if (t == 0) {
-        for (int k = 0; k < n0; ++k) ata += qs.A0[k * n + i] * qs.A0[k * n + j];
-        if (N > 0)
-          for (int k = 0; k < nx; ++k) ata += qs.Am[k * n + i] * qs.Am[k * n + j];
-      } else {
-        const float* ap = qs.Ap + (t - 1) * nx * n;
-        for (int k = 0; k < nx; ++k) ata += ap[k * n + i] * ap[k * n + j];
-        if (t < N) {
-          const float* am = qs.Am + t * nx * n;
-          for (int k = 0; k < nx; ++k) ata += am[k * n + i] * am[k * n + j];
+  // Row k (n entries, zero padded to 16) of a staged block, broadcast to the stage's threads.
+  auto row16 = [&](float (&r)[16], const float* p) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = j < n ? p[j] : 0.f;
+  };
+  // ---- Theta rows i = q + 8a
+  float a0[16], a1[16];  // [Theta | .] rows, later the Gauss-Jordan rows
+  {
+    float acc0[16], acc1[16], r[16];
+    const int i0 = q, i1 = q + 8;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      a0[j] = (act && i0 < n && j < n) ? qg.D[((size_t)tt * n + i0) * n + j] : 0.f;
+      a1[j] = (act && i1 < n && j < n) ? qg.D[((size_t)tt * n + i1) * n + j] : 0.f;
+      acc0[j] = 0.f;
+      acc1[j] = 0.f;
+    }
+    if (i0 < n) a0[i0] += sigma;
+    if (i1 < n) a1[i1] += sigma;
+    auto gram = [&](const float* A, int rows) {  // acc_i += sum_k A[k][i] A[k][:]
+      for (int k = 0; k < rows; ++k) {
+        row16(r, A + k * n);
+        const float s0 = i0 < n ? A[k * n + i0] : 0.f;
+        const float s1 = i1 < n ? A[k * n + i1] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          acc0[j] = fmaf(s0, r[j], acc0[j]);
+          acc1[j] = fmaf(s1, r[j], acc1[j]);
         }
       }
-      val += rho_f * ata;
+    };
+    if (act && m > 0) gram(qs.G + tt * m * n, m);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      a0[j] = fmaf(rho, acc0[j], a0[j]);
+      a1[j] = fmaf(rho, acc1[j], a1[j]);
+      acc0[j] = 0.f;
+      acc1[j] = 0.f;
     }
-    th[t * RowsGeo::TBLK + i * RowsGeo::TSTR + j] = val;
+    if (act) {
+      if (t == 0) {
+        if (n0 > 0) gram(qs.A0, n0);
+        if (N > 0) gram(qs.Am, nx);
+      } else {
+        gram(qs.Ap + (t - 1) * nx * n, nx);
+        if (t < N) gram(qs.Am + t * nx * n, nx);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      a0[j] = (i0 < n && j < n) ? fmaf(rho_f, acc0[j], a0[j]) : 0.f;
+      a1[j] = (i1 < n && j < n) ? fmaf(rho_f, acc1[j], a1[j]) : 0.f;
+    }
+    if (act) {
+      float* d0 = th + t * RowsGeo::TBLK + i0 * RowsGeo::TSTR;
+      float* d1 = th + t * RowsGeo::TBLK + i1 * RowsGeo::TSTR;
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        st128(d0 + j, &a0[j]);
+        st128(d1 + j, &a1[j]);
+      }
+    }
   }
-  __syncthreads();
   TMPC_PROF(2);
-  const int t_own = threadIdx.x >> 3, q = threadIdx.x & 7;
-  const int nw = blockDim.x >> 5;
-  for (int base = 0; base < T; base += nw) {
-    const RowsInvAcc ia{th, sm + L.tslot, base};
-    invert_thetas<16, float>(ia, T, n, flag, base, base + nw < T ? base + nw : T);
-    __syncthreads();
-    if (t_own >= base && t_own < base + nw && t_own < T) {
-      const float* blk = sm + L.tslot + (t_own - base) * RowsGeo::SQ;
-      for (int a = 0; a < 2; ++a)
-        for (int k = 0; k < 16; ++k) save->v[a * 16 + k] = -blk[(q + 8 * a) * 16 + k];
+  // ---- Theta^-1 rows by Gauss-Jordan without row exchanges
+  {
+    float b0[16], b1[16];  // identity part
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      b0[j] = (j == q && q < n) ? 1.f : 0.f;
+      b1[j] = (j == q + 8 && q + 8 < n) ? 1.f : 0.f;
     }
-    __syncthreads();
+    float* piv = sm + L.tslot + (size_t)(act ? t : 0) * 32;  // the stage's pivot row [Theta part | inverse part]
+    bool bad = false;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      if (c < n) {  // n is uniform: every thread takes the same branch
+        const bool owner = q == (c & 7);
+        if (owner && act) {
+          float* ra = c < 8 ? a0 : a1;
+          float* rb = c < 8 ? b0 : b1;
+          const float p = ra[c];
+          if (!(fabsf(p) > 0.f) || !isfinite(p)) bad = true;
+          const float inv = 1.f / p;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            ra[j] *= inv;
+            rb[j] *= inv;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            st128(piv + j, &ra[j]);
+            st128(piv + 16 + j, &rb[j]);
+          }
+        }
+        __syncwarp();
+        if (act) {
+          float pr[16], pb[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            ld128(&pr[j], piv + j);
+            ld128(&pb[j], piv + 16 + j);
+          }
+          if (!(owner && c < 8)) {
+            const float f = a0[c];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              a0[j] = fmaf(-f, pr[j], a0[j]);
+              b0[j] = fmaf(-f, pb[j], b0[j]);
+            }
+          }
+          if (!(owner && c >= 8)) {
+            const float f = a1[c];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              a1[j] = fmaf(-f, pr[j], a1[j]);
+              b1[j] = fmaf(-f, pb[j], b1[j]);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    if (bad) atomicOr(flag, TMPC_STATUS_SINGULAR_BLOCK);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      save->v[k] = act ? b0[k] : 0.f;
+      save->v[16 + k] = act ? b1[k] : 0.f;
+    }
   }
   TMPC_PROF(3);
-  // E entries first (16 global loads in flight per row), then the sums from
-  // the staged Ap / Am.
-#pragma unroll 1
-  for (int a = 0; a < 2; ++a) {
-    const int j = q + 8 * a;
-    if (t_own >= T)
-      for (int k = 0; k < 16; ++k) save->v[a * 16 + k] = 0.f;
-    // S(t, t-1) = Phi_{t-1}: row j, Phi_{t-1}[j][k] = E[j][k] + rho_f sum_kk Ap[kk][j] Am[kk][k]
-    const bool lo = t_own >= 1 && t_own < T && j < n;
-    float ev[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) ev[k] = (lo && k < n) ? qg.E[((size_t)(t_own - 1) * n + j) * n + k] : 0.f;
+  // ---- Phi rows: S(t, t-1) = Phi_{t-1} rows j, S(t, t+1) = Phi_t^T rows j (columns j of Phi_t)
+  {
+    float acc0[16], acc1[16], r[16];
+    const int j0 = q, j1 = q + 8;
+    const bool lo = act && t >= 1;
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      float v = 0.f;
-      if (lo && k < n) {
-        const float* ap = qs.Ap + (t_own - 1) * nx * n;
-        const float* am = qs.Am + (t_own - 1) * nx * n;
-        float sum = 0.f;
-        for (int kk = 0; kk < nx; ++kk) sum += ap[kk * n + j] * am[kk * n + k];
-        v = ev[k] + rho_f * sum;
-      }
-      save->v[32 + a * 16 + k] = v;
+      acc0[k] = 0.f;
+      acc1[k] = 0.f;
     }
-    // S(t, t+1) = Phi_t^T: row j is column j of Phi_t, Phi_t[k][j] = E[k][j] + rho_f sum_kk Ap[kk][k] Am[kk][j]
-    const bool up = t_own < N && j < n;
+    if (lo) {
+      const float* ap = qs.Ap + (t - 1) * nx * n;
+      const float* am = qs.Am + (t - 1) * nx * n;
+      for (int kk = 0; kk < nx; ++kk) {  // acc_j[k] += Ap[kk][j] Am[kk][k]
+        row16(r, am + kk * n);
+        const float s0 = j0 < n ? ap[kk * n + j0] : 0.f;
+        const float s1 = j1 < n ? ap[kk * n + j1] : 0.f;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) ev[k] = (up && k < n) ? qg.E[((size_t)t_own * n + k) * n + j] : 0.f;
+        for (int k = 0; k < 16; ++k) {
+          acc0[k] = fmaf(s0, r[k], acc0[k]);
+          acc1[k] = fmaf(s1, r[k], acc1[k]);
+        }
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      float v = 0.f;
-      if (up && k < n) {
-        const float* ap = qs.Ap + t_own * nx * n;
-        const float* am = qs.Am + t_own * nx * n;
-        float sum = 0.f;
-        for (int kk = 0; kk < nx; ++kk) sum += ap[kk * n + k] * am[kk * n + j];
-        v = ev[k] + rho_f * sum;
+      const bool in = lo && k < n;
+      save->v[32 + k] = (in && j0 < n) ? qg.E[((size_t)(t - 1) * n + j0) * n + k] + rho_f * acc0[k] : 0.f;
+      save->v[48 + k] = (in && j1 < n) ? qg.E[((size_t)(t - 1) * n + j1) * n + k] + rho_f * acc1[k] : 0.f;
+      acc0[k] = 0.f;
+      acc1[k] = 0.f;
+    }
+    const bool up = act && t < N;
+    if (up) {
+      const float* ap = qs.Ap + t * nx * n;
+      const float* am = qs.Am + t * nx * n;
+      for (int kk = 0; kk < nx; ++kk) {  // acc_j[k] += Ap[kk][k] Am[kk][j]
+        row16(r, ap + kk * n);
+        const float s0 = j0 < n ? am[kk * n + j0] : 0.f;
+        const float s1 = j1 < n ? am[kk * n + j1] : 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          acc0[k] = fmaf(r[k], s0, acc0[k]);
+          acc1[k] = fmaf(r[k], s1, acc1[k]);
+        }
       }
-      save->v[64 + a * 16 + k] = v;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const bool in = up && k < n;
+      save->v[64 + k] = (in && j0 < n) ? qg.E[((size_t)t * n + k) * n + j0] + rho_f * acc0[k] : 0.f;
+      save->v[80 + k] = (in && j1 < n) ? qg.E[((size_t)t * n + k) * n + j1] + rho_f * acc1[k] : 0.f;
     }
   }
   __syncthreads();
