@@ -344,6 +344,7 @@ def main():
     n_lin = [0]
     orig = ops.admm_solve
     orig_lin = ops.linearize_dynamics
+    orig_kkt = ops.first_order_error
 
     def timed_admm(*a, **k):
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
@@ -357,6 +358,10 @@ def main():
         n_lin[0] += 1
         return orig_lin(*a, **k)
 
+    def counted_kkt(*a, **k):
+        n_lin[0] += 1
+        return orig_kkt(*a, **k)
+
     def step():
         return solver.solve(guess, params)
 
@@ -365,6 +370,7 @@ def main():
     torch.cuda.synchronize()
     ops.admm_solve = timed_admm
     ops.linearize_dynamics = counted_lin
+    ops.first_order_error = counted_kkt
     import turbompc_b200.solver as solver_mod
 
     solver_mod.ops.admm_solve = timed_admm
@@ -382,6 +388,7 @@ def main():
         dist.barrier()
     ops.admm_solve = orig
     ops.linearize_dynamics = orig_lin
+    ops.first_order_error = orig_kkt
     solver_mod.ops.admm_solve = orig
     ms = s0.elapsed_time(s1) / args.steps
     kern_ms = [a.elapsed_time(b) for a, b in launch_ms]

@@ -268,6 +268,25 @@ int32_t tmpc_pcg_solve_stream_f64(const TmpcDims* dims, const double* ops, const
                                   tmpc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * First-order (KKT) error of SQP iterates z [Nb][T][n] with multipliers
+ * y_f0 [Nb][n0], y_fdyn [Nb][N][nx], y_g [Nb][T][m] against the QP linearised
+ * there: the "first_order" convergence measure of the SQP loop
+ * (turbompc/solvers/turbompc_solver.py:1158-1225).  Per problem:
+ *   conv = max(stat, eq, ineq [, ||w_s slack + y_g||_inf when use_slack]),
+ *   stat = ||P z + q + C^T y_f + G^T y_g||_inf, eq = ||C z - c||_inf,
+ *   ineq = ||max(l - g, 0, g - u)||_inf with g = G z (+ slack) written to g_out.
+ * slack [Nb][T][m] and slack_weight [Nb] only with use_slack.
+ * ------------------------------------------------------------------------- */
+int32_t tmpc_first_order_error_f32(const TmpcDims* dims, const TmpcQP* qp, const float* z, const float* y_f0,
+                                   const float* y_fdyn, const float* y_g, const float* slack,
+                                   const float* slack_weight, int32_t use_slack, float* conv_out, float* eq_out,
+                                   float* ineq_out, float* g_out, tmpc_stream_t stream);
+int32_t tmpc_first_order_error_f64(const TmpcDims* dims, const TmpcQP* qp, const double* z, const double* y_f0,
+                                   const double* y_fdyn, const double* y_g, const double* slack,
+                                   const double* slack_weight, int32_t use_slack, double* conv_out, double* eq_out,
+                                   double* ineq_out, double* g_out, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Linearised discrete dynamics of a built-in model, batched over (problem,
  * stage t < N): the QP's dynamics rows, as produced in the reference by
  * get_dynamics_linearized_matrices (turbompc/problems/

@@ -92,3 +92,24 @@ def test_qp_reuse_equals_full_build():
     reuse = s._build_qp_data(st, g.controls, params, prev=q0)
     for f, r in zip(full.tensors().values(), reuse.tensors().values()):
         assert torch.equal(f, r)
+
+
+@pytest.mark.parametrize("slack", [False, True])
+def test_first_order_error_kernel_matches_torch(slack):
+    """tmpc_first_order_error_* against the PyTorch form of the SQP first-order
+    check (fp64, dense QP blocks incl. E coupling, n0 rows, slack variables)."""
+    from tests.helpers import dense_blocks
+    from turbompc_b200.problems import synthetic
+    Nb = 5
+    b = dense_blocks(Nb, 6, 3, 9, 4, seed=4)
+    sw = np.full(Nb, 3.0) if slack else None
+    qd = synthetic.to_qpdata(b, dtype=torch.float64, device="cuda", slack_weight=sw, use_slack=slack)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    r = lambda *s: torch.randn(*s, generator=g, device="cuda", dtype=torch.float64)
+    st = ops.ADMMState(r(Nb, 10, 9), r(Nb, 10, 4), r(Nb, 6), r(Nb, 9, 6), r(Nb, 10, 4), r(Nb, 10, 4), r(Nb).abs())
+    states, controls, slacks = r(Nb, 10, 6), r(Nb, 10, 3), r(Nb, 10, 4)
+    s = TurboMPCSolver.__new__(TurboMPCSolver)
+    a = s._first_order_error(qd, states, controls, slacks, st)
+    c = s._first_order_error_torch(qd, states, controls, slacks, st)
+    for x, y in zip(a, c):
+        assert rel_err(x.cpu().numpy(), y.cpu().numpy()) < 1e-12

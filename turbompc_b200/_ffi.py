@@ -66,6 +66,8 @@ for _s in ("f32", "f64"):
                                                              C.c_double, C.c_double, _P, _P, _P])
     _SIGS[f"tmpc_pcg_solve_stream_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P, _P, C.c_double,
                                                         C.c_int32, _P])
+    _SIGS[f"tmpc_first_order_error_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP)] + [_P] * 6 +
+                                                         [C.c_int32] + [_P] * 4 + [_P])
     _SIGS[f"tmpc_riccati_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_adjoint_kkt_solve_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP), _P, _P, _P, _P,
                                                           C.c_size_t, _P])

@@ -309,3 +309,27 @@ def linearize_dynamics(model: int, params, scheme: int, dt: float, states: torch
                                         _ptr(controls, states.dtype, states.device), pa, len(params), _ptr(Am),
                                         _ptr(c), _stream(states.device)))
     return Am, c
+
+
+def first_order_error(qp: QPData, z: torch.Tensor, state: ADMMState, slacks: Optional[torch.Tensor] = None):
+    """First-order (KKT) error of SQP iterates (tmpc_first_order_error_*):
+    returns (conv, eq, ineq, g) with g = G z (+ slacks), shapes (Nb,), (Nb,),
+    (Nb,), (Nb, T, m)."""
+    lib = _ffi.load()
+    dt, dev = qp.dtype, qp.device
+    z = z.contiguous()
+    conv = torch.empty(qp.Nb, dtype=dt, device=dev)
+    eq = torch.empty_like(conv)
+    ineq = torch.empty_like(conv)
+    g = torch.empty(qp.Nb, qp.T, qp.m, dtype=dt, device=dev)
+    use_slack = bool(qp.ineq.use_slack_variables) and qp.m > 0
+    sw = qp.ineq.slack_penalization_weight if use_slack else None
+    name = f"tmpc_first_order_error_{_suffix(dt)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(dims_of(qp)), C.byref(_qp_c(qp)), _ptr(z, dt, dev),
+                                        _ptr(state.y_f_0.contiguous(), dt, dev),
+                                        _ptr(state.y_f_dyn.contiguous(), dt, dev),
+                                        _ptr(state.y_g.contiguous(), dt, dev),
+                                        _ptr(slacks.contiguous() if use_slack else None, dt, dev),
+                                        _ptr(_rho_vec(sw, qp) if sw is not None else None, dt, dev),
+                                        int(use_slack), _ptr(conv), _ptr(eq), _ptr(ineq), _ptr(g), _stream(dev)))
+    return conv, eq, ineq, g

@@ -274,7 +274,15 @@ class TurboMPCSolver:
                       QPInequalityBlocks(c(G), c(l), c(u), sw, prog.use_slack_variables))
 
     def _first_order_error(self, qp: QPData, states, controls, slacks, st: ADMMState):
-        """turbompc_solver.py:1158-1225 (first_order criterion)."""
+        """turbompc_solver.py:1158-1225 (first_order criterion): the fused CUDA
+        kernel on GPU tensors (tmpc_first_order_error_*)."""
+        x = torch.cat([states, controls], -1)
+        if x.is_cuda:
+            return ops.first_order_error(qp, x, st, slacks)
+        return self._first_order_error_torch(qp, states, controls, slacks, st)
+
+    def _first_order_error_torch(self, qp: QPData, states, controls, slacks, st: ADMMState):
+        """The same measure in PyTorch operations (host tensors; the GPU kernel's test reference)."""
         x = torch.cat([states, controls], -1)
         D, E = qp.cost.D, qp.cost.E
         Px = torch.einsum("btij,btj->bti", D, x)
