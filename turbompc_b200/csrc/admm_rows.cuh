@@ -284,6 +284,105 @@ struct __align__(16) RowOpsSave {
   }
 };
 
+// Two block sums with one barrier (same deterministic order as rows_block_sum);
+// slots holds 2 x 16 entries.
+__device__ __forceinline__ void rows_block_sum2(float& a, float& b, float* slots) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if ((threadIdx.x & 31) == 0) {
+    slots[threadIdx.x >> 5] = a;
+    slots[16 + (threadIdx.x >> 5)] = b;
+  }
+  __syncthreads();
+  float sa = slots[threadIdx.x & 15], sb = slots[16 + (threadIdx.x & 15)];
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  }
+  a = sa;
+  b = sb;
+}
+
+// PCG in the single-reduction (Chronopoulos-Gear) arrangement: the same
+// iterates as admm_fused.cu:54-161 in exact arithmetic, with both inner
+// products of an iteration in one reduction.  With u = M r and w = S u,
+//   gamma = r.u, delta = w.u, beta = gamma_new / gamma,
+//   p.Sp = delta - beta gamma_new / alpha  (denominator, clamped at 1e-30 as
+//   the reference's p.Sp), alpha = gamma_new / (p.Sp),
+//   p = u + beta p, s (= S p) = w + beta s, x += alpha p, r -= alpha s.
+// The stopping test |gamma| < 1e-12 + eps |gamma_0| runs before each update,
+// as the reference's |eta| test, so the iteration counts agree.  Three CTA
+// barriers and one reduction per iteration instead of four and two.  xs /
+// gam are [T][VSTR] block vectors in shared memory; x is read from and
+// written back to xs.  Returns the iteration count.
+__device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
+                                           const float* gam, int T, int max_iter, float eps, float* slots) {
+  constexpr int VS = RowsGeo::VSTR;
+  RowOps o;
+  saved.load(o);
+  const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
+  const bool act = t < T;
+  const float* th_row = th + t * RowsGeo::TBLK + q * RowsGeo::TSTR;
+  float* bt = bb + t * RowsGeo::BSTR;
+  float* prow = bt + RowsGeo::BSTR;
+  float x[2], r[2], p[2], sv[2], u[2], w[2];
+  x[0] = act ? xs[t * VS + q] : 0.f;
+  x[1] = act ? xs[t * VS + q + 8] : 0.f;
+  prow[q] = x[0];
+  prow[q + 8] = x[1];
+  __syncthreads();
+  rows_smv(w, o, th_row, bt);
+  r[0] = (act ? gam[t * VS + q] : 0.f) - w[0];
+  r[1] = (act ? gam[t * VS + q + 8] : 0.f) - w[1];
+  rows_prec(u, r, o, bt, q);  // its barrier ends every read of x in the buffer
+  prow[q] = u[0];
+  prow[q + 8] = u[1];
+  __syncthreads();
+  rows_smv(w, o, th_row, bt);
+  float gamma = fmaf(r[1], u[1], r[0] * u[0]);
+  float delta = fmaf(w[1], u[1], w[0] * u[0]);
+  rows_block_sum2(gamma, delta, slots);
+  const float eta0 = fabsf(gamma);
+  float den = fabsf(delta) < 1e-30f ? 1e-30f : delta;
+  float alpha = gamma / den;
+  p[0] = u[0];
+  p[1] = u[1];
+  sv[0] = w[0];
+  sv[1] = w[1];
+  int it = 0;
+  for (; it < max_iter; ++it) {
+    if (fabsf(gamma) < 1e-12f + eps * eta0) break;
+    x[0] = fmaf(alpha, p[0], x[0]);
+    x[1] = fmaf(alpha, p[1], x[1]);
+    r[0] = fmaf(-alpha, sv[0], r[0]);
+    r[1] = fmaf(-alpha, sv[1], r[1]);
+    rows_prec(u, r, o, bt, q);  // its barrier ends every read of the previous u
+    prow[q] = u[0];
+    prow[q + 8] = u[1];
+    __syncthreads();
+    rows_smv(w, o, th_row, bt);
+    float gnew = fmaf(r[1], u[1], r[0] * u[0]);
+    float dl = fmaf(w[1], u[1], w[0] * u[0]);
+    rows_block_sum2(gnew, dl, slots);
+    const float beta = gnew / gamma;
+    float pap = dl - beta * gnew / alpha;
+    if (fabsf(pap) < 1e-30f) pap = 1e-30f;
+    alpha = gnew / pap;
+    gamma = gnew;
+    p[0] = fmaf(beta, p[0], u[0]);
+    p[1] = fmaf(beta, p[1], u[1]);
+    sv[0] = fmaf(beta, sv[0], w[0]);
+    sv[1] = fmaf(beta, sv[1], w[1]);
+  }
+  if (act) {
+    xs[t * VS + q] = x[0];
+    xs[t * VS + q + 8] = x[1];
+  }
+  __syncthreads();
+  return it;
+}
+
 // PCG with the stopping rule and recurrences of admm_fused.cu:54-161 (see
 // pcg_core.cuh).  xs / gam are [T][VSTR] block vectors in shared memory; x is
 // read from and written back to xs.  Returns the iteration count.
@@ -665,7 +764,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
       __syncthreads();
     }
     TMPC_PROF(6);
-    rows_pcg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
+    rows_pcg_cg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
              TMPC_RS(red) + kRedSlots);
     TMPC_PROF(7);
     {
