@@ -383,66 +383,6 @@ __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float*
   return it;
 }
 
-// PCG with the stopping rule and recurrences of admm_fused.cu:54-161 (see
-// pcg_core.cuh).  xs / gam are [T][VSTR] block vectors in shared memory; x is
-// read from and written back to xs.  Returns the iteration count.
-__device__ __forceinline__ int rows_pcg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
-                                        const float* gam, int T, int max_iter, float eps, float* slots) {
-  constexpr int VS = RowsGeo::VSTR;
-  TMPC_PROF_INIT
-  RowOps o;
-  saved.load(o);
-  const int t = threadIdx.x >> 3, q = threadIdx.x & 7;
-  const bool act = t < T;
-  const float* th_row = th + t * RowsGeo::TBLK + q * RowsGeo::TSTR;
-  float* bt = bb + t * RowsGeo::BSTR;
-  float* prow = bt + RowsGeo::BSTR;
-  float x[2], r[2], p[2], z[2], y[2];
-  x[0] = act ? xs[t * VS + q] : 0.f;
-  x[1] = act ? xs[t * VS + q + 8] : 0.f;
-  prow[q] = x[0];
-  prow[q + 8] = x[1];
-  __syncthreads();
-  rows_smv(y, o, th_row, bt);
-  r[0] = (act ? gam[t * VS + q] : 0.f) - y[0];
-  r[1] = (act ? gam[t * VS + q + 8] : 0.f) - y[1];
-  rows_prec(z, r, o, bt, q);
-  p[0] = z[0];
-  p[1] = z[1];
-  float eta = rows_block_sum(fmaf(r[1], z[1], r[0] * z[0]), slots);
-  const float eta0 = fabsf(eta);
-  int it = 0;
-  for (; it < max_iter; ++it) {
-    if (fabsf(eta) < 1e-12f + eps * eta0) break;
-    prow[q] = p[0];
-    prow[q + 8] = p[1];
-    __syncthreads();
-    TMPC_PROF(12);
-    rows_smv(y, o, th_row, bt);
-    TMPC_PROF(13);
-    float den = rows_block_sum(fmaf(p[1], y[1], p[0] * y[0]), slots + 16);
-    TMPC_PROF(14);
-    if (fabsf(den) < 1e-30f) den = 1e-30f;
-    const float alpha = eta / den;
-    x[0] = fmaf(alpha, p[0], x[0]);
-    x[1] = fmaf(alpha, p[1], x[1]);
-    r[0] = fmaf(-alpha, y[0], r[0]);
-    r[1] = fmaf(-alpha, y[1], r[1]);
-    rows_prec(z, r, o, bt, q);
-    TMPC_PROF(15);
-    const float en = rows_block_sum(fmaf(r[1], z[1], r[0] * z[0]), slots);
-    const float beta = en / eta;
-    eta = en;
-    p[0] = fmaf(beta, p[0], z[0]);
-    p[1] = fmaf(beta, p[1], z[1]);
-  }
-  if (act) {
-    xs[t * VS + q] = x[0];
-    xs[t * VS + q + 8] = x[1];
-  }
-  __syncthreads();
-  return it;
-}
 
 // Operator build for one rho (the math of admm.py:71-154, restated per owner
 // thread).  Thread (t, q) computes rows q and q + 8 of every block it owns:
