@@ -598,6 +598,108 @@ __device__ __noinline__ void rows_build(float* sm, const RowsSmem* Lp, const QPV
   TMPC_PROF(4);
 }
 
+// ADMM-level step 1 (per entry (t, j) of the block vectors): the pending
+// over-relaxation of the previous iteration's PCG result (x = alpha x + (1 -
+// alpha) x_old, admm.py:893) when `relax`, then x_old = x and
+//   gamma = sigma x - q + C^T(rho_f c - y_f) + G^T(rho z - y_g)
+// with the targets rho_f c - y_f, rho z - y_g formed inline (the same
+// operations and rounding as admm_targets + compute_gamma, without their
+// buffers and barrier).  Caller syncs after.
+__device__ __forceinline__ void rows_relax_gamma(float* xs, float* xold, float* gam, const QPView<float>& qp,
+                                                 const float* yf0, const float* yfd, const float* zg,
+                                                 const float* yg, float rho, float rho_f, float sigma, float al,
+                                                 bool relax, int T, int n, int nx, int n0, int m) {
+  const int N = T - 1;
+  TMPC_FOR_ENTRIES(e, o, T, 16, RowsGeo::VSTR) {
+    const int t = e >> 4, j = e & 15;
+    float xv = xs[o];
+    if (relax) {
+      xv = al * xv + (1.f - al) * xold[o];
+      xs[o] = xv;
+    }
+    xold[o] = xv;
+    float val = 0.f;
+    if (j < n) {
+      val = sigma * xv - qp.q[t * n + j];
+      float eq = 0.f;
+      if (t == 0) {
+#pragma unroll 4
+        for (int k = 0; k < n0; ++k) eq += qp.A0[k * n + j] * (rho_f * qp.c0[k] - yf0[k]);
+        if (N > 0) {
+#pragma unroll 4
+          for (int k = 0; k < nx; ++k) eq += qp.Am[k * n + j] * (rho_f * qp.c[k] - yfd[k]);
+        }
+      } else {
+        const float* ap = qp.Ap + (t - 1) * nx * n;
+        const int r0 = (t - 1) * nx;
+#pragma unroll 4
+        for (int k = 0; k < nx; ++k) eq += ap[k * n + j] * (rho_f * qp.c[r0 + k] - yfd[r0 + k]);
+        if (t < N) {
+          const float* am = qp.Am + t * nx * n;
+          const int r1 = t * nx;
+#pragma unroll 4
+          for (int k = 0; k < nx; ++k) eq += am[k * n + j] * (rho_f * qp.c[r1 + k] - yfd[r1 + k]);
+        }
+      }
+      val += eq;
+      float iq = 0.f;
+#pragma unroll 4
+      for (int k = 0; k < m; ++k) iq += qp.G[(t * m + k) * n + j] * (rho * zg[t * m + k] - yg[t * m + k]);
+      val += iq;
+    }
+    gam[o] = val;
+  }
+}
+
+// ADMM-level step 2 (per constraint row): the row of C x / G x on the PCG
+// result (before relaxation, admm.py:884-887), then that row's dual update
+// and, for inequality rows, the slack / projection update (admm.py:896-931):
+// apply_constraints and admm_relax_duals fused row by row (same operations,
+// no cx / gx buffers).  The x relaxation is applied by the next step 1 (or
+// rows_relax).  Caller syncs after.
+__device__ __forceinline__ void rows_constraints_duals(const float* xs, const QPView<float>& qp, float* yf0,
+                                                       float* yfd, float* zg, float* yg, float* xig, float rho,
+                                                       float rho_f, float al, float sw, bool use_slack, int T,
+                                                       int n, int nx, int n0, int m) {
+  const int N = T - 1;
+  const int tot = n0 + N * nx + T * m;
+  for (int e = threadIdx.x; e < tot; e += blockDim.x) {
+    if (e < n0) {
+      const float cx0 = row_dot(qp.A0 + e * n, xs, n);
+      yf0[e] += rho_f * al * (cx0 - qp.c0[e]);
+    } else if (e < n0 + N * nx) {
+      const int k = e - n0, t = k / nx, i = k - t * nx;
+      const float cx = row_dot(qp.Am + (t * nx + i) * n, xs + t * RowsGeo::VSTR, n) +
+                       row_dot(qp.Ap + (t * nx + i) * n, xs + (t + 1) * RowsGeo::VSTR, n);
+      yfd[k] += rho_f * al * (cx - qp.c[k]);
+    } else {
+      const int k = e - n0 - N * nx, t = k / m, i = k - t * m;
+      const float gx = row_dot(qp.G + (t * m + i) * n, xs + t * RowsGeo::VSTR, n);
+      const float zold = zg[k];
+      const float zt = al * gx + (1.f - al) * zold + yg[k] / rho;
+      float cl = zt;
+      const float lb = qp.l[k], ub = qp.u[k];
+      if (cl < lb) cl = lb;
+      if (cl > ub) cl = ub;
+      float znew;
+      if (use_slack) {
+        const float f = sw / (sw + rho);
+        znew = (1.f - f) * zt + f * cl;
+        xig[k] = (rho / (sw + rho)) * (cl - zt);
+      } else {
+        znew = cl;
+      }
+      zg[k] = znew;
+      yg[k] += rho * (al * gx + (1.f - al) * zold - znew);
+    }
+  }
+}
+
+// The pending over-relaxation alone (before a residual check and at exit).
+__device__ __forceinline__ void rows_relax(float* xs, const float* xold, float al, int T) {
+  TMPC_FOR_ENTRIES(e, o, T, 16, RowsGeo::VSTR) { xs[o] = al * xs[o] + (1.f - al) * xold[o]; }
+}
+
 // Staged QP view rebuilt at each use from the offsets in shared memory (kept
 // out of registers across the PCG loop).
 __device__ __forceinline__ QPView<float> rows_qp_view(float* sm, const RowsSmem& L, const TmpcQP& g, int b, int T,
@@ -686,43 +788,33 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   TMPC_PROF(5);  // (phases 2-4 timed inside the build; this is the call overhead)
 
   uint32_t iters = (uint32_t)P.max_iter;
+  bool pending = false;  // xs holds a PCG result whose over-relaxation is still to be applied
   for (int it = 0; it < P.max_iter; ++it) {
     const int T = P.T, n = P.n, nx = P.nx, n0 = P.n0, m = P.m;
     const R rho_f = rho * P.rho_f_factor;
     {
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
-      admm_targets(TMPC_RS(ct), TMPC_RS(gt), qp, TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg), TMPC_RS(yg), rho, rho_f,
-                   T, nx, n0, m);
-      __syncthreads();
-    }
-    {
-      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
-      compute_gamma<NB>(TMPC_RS(gam), TMPC_RS(x), qp, TMPC_RS(ct), TMPC_RS(gt), P.sigma, T, n, nx, n0, m);
-      R* xs = TMPC_RS(x);
-      R* xold = TMPC_RS(xold);
-      TMPC_FOR_ENTRIES(e, o, T, NB, RowsGeo::VSTR) { xold[o] = xs[o]; }
+      rows_relax_gamma(TMPC_RS(x), TMPC_RS(xold), TMPC_RS(gam), qp, TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg),
+                       TMPC_RS(yg), rho, rho_f, P.sigma, P.alpha, pending, T, n, nx, n0, m);
       __syncthreads();
     }
     TMPC_PROF(6);
     rows_pcg_cg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
-             TMPC_RS(red) + kRedSlots);
+                TMPC_RS(red) + kRedSlots);
+    pending = true;
     TMPC_PROF(7);
     {
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
-      apply_constraints<NB>(TMPC_RS(cx0), TMPC_RS(cx), TMPC_RS(gx), TMPC_RS(x), qp, T, n, nx, n0, m);
+      const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
+      rows_constraints_duals(TMPC_RS(x), qp, TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg), TMPC_RS(yg), TMPC_RS(xig),
+                             rho, rho_f, P.alpha, sw, P.use_slack != 0, T, n, nx, n0, m);
       __syncthreads();
     }
     TMPC_PROF(8);
-    {
-      const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
-      const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
-      admm_relax_duals<NB>(TMPC_RS(x), TMPC_RS(xold), TMPC_RS(yf0), TMPC_RS(yfd), TMPC_RS(zg), TMPC_RS(yg),
-                           TMPC_RS(xig), TMPC_RS(cx0), TMPC_RS(cx), TMPC_RS(gx), qp, rho, rho_f, P.alpha, sw,
-                           P.use_slack != 0, T, nx, n0, m);
-      __syncthreads();
-    }
-    TMPC_PROF(9);
     if (P.check_every > 0 && (it % P.check_every) == 0) {
+      rows_relax(TMPC_RS(x), TMPC_RS(xold), P.alpha, T);
+      pending = false;
+      __syncthreads();
       const QPView<R> qp = rows_qp_view(sm, Ls, P.qp, b, T, n, nx, n0, m);
       const R sw = P.slack_weight ? P.slack_weight[b] : R(0);
       R rho_new;
@@ -740,6 +832,11 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
       __syncthreads();
     }
   }
+  if (pending) {
+    rows_relax(TMPC_RS(x), TMPC_RS(xold), P.alpha, P.T);
+    __syncthreads();
+  }
+  TMPC_PROF(9);
 
   // ---- store
   TMPC_PROF(10);
