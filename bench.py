@@ -273,6 +273,86 @@ def pcg_sweep(points, reps=3, pcg_iters=PCG):
         del Sb, fac
 
 
+def run_config(name, steps=3, warmup=2):
+    """Configs 4 and 5 on one GPU (one JSON line each; the default run above is
+    config 3).  obstacles: quadrotor N=40 with 8 spheres per problem, batch
+    8192, 10 SQP x 50 ADMM x 30 PCG, each step warm-started from the previous
+    solution (states, controls and ADMM state).  cw_mlp: Clohessy-Wiltshire
+    with the learned MLP stage cost, N=60, batch 16384, 3 SQP x 50 ADMM x 30
+    PCG forward plus the VJP w.r.t. x0, the MLP parameters and A, B (adjoint
+    KKT on the GPU).  Device time with CUDA events."""
+    import torch
+
+    from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    from turbompc_b200.problems.quadrotor import make_obstacle_problem
+    from turbompc_b200.solver import TurboMPCSolver
+
+    def fixed(sqp, admm, pcg):
+        return {"num_sqp_iteration_max": sqp, "tol_convergence": 0.0,
+                "admm": {"max_iter": admm, "check_termination_every": 0, "adapt_rho_every": 0, "eps_abs": 0.0,
+                         "eps_rel": 0.0, "pcg": {"max_iter": pcg, "tol_epsilon": 0.0}}}
+
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    if name == "obstacles":
+        batch = 8192
+        prog, params = make_obstacle_problem(batch, N=40, seed=4, dtype=torch.float32, device="cuda")
+        solver = TurboMPCSolver(prog, fixed(10, 50, 30))
+        guess = solver.initial_guess(params)
+        for _ in range(warmup):
+            guess = solver.solve(guess, params)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            guess = solver.solve(guess, params)  # warm start from the previous solve
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        line = {"config": "obstacles (config 4)", "metric": "MPC solves/sec", "value": batch / (ms / 1e3),
+                "unit": "solves/s", "ms_per_step": ms, "batch": batch, "horizon": 40, "m": 12,
+                "iterations": "10 SQP x 50 ADMM x 30 PCG, warm-started", "dtype": "f32", "n_gpus": 1}
+    else:
+        batch = 16384
+        prog, params = make_learned_cost_problem(batch, N=60, seed=0, dtype=torch.float32, device="cuda")
+        solver = TurboMPCSolver(prog, fixed(3, 50, 30), use_full_hessian=True)
+        guess = solver.initial_guess(params)
+        leaves = {"mlp_W1": params["mlp_W1"], "mlp_b1": params["mlp_b1"], "mlp_w2": params["mlp_w2"],
+                  "dynamics_state_dot_params": dict(params["dynamics_state_dot_params"]),
+                  "initial_state": params["initial_state"]}
+
+        def fwd_bwd():
+            w = {k: (v.detach().clone().requires_grad_(True) if isinstance(v, torch.Tensor) else
+                     {kk: vv.detach().clone().requires_grad_(True) for kk, vv in v.items()})
+                 for k, v in leaves.items()}
+            sol = solver.solve(guess, params, w)
+            loss = (sol.states ** 2).sum() + (sol.controls ** 2).sum()
+            flat = [w["mlp_W1"], w["mlp_b1"], w["mlp_w2"], w["initial_state"],
+                    w["dynamics_state_dot_params"]["A"], w["dynamics_state_dot_params"]["B"]]
+            return torch.autograd.grad(loss, flat)
+
+        for _ in range(warmup):
+            fwd_bwd()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            with torch.no_grad():
+                solver.solve(guess, params)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_f = e0.elapsed_time(e1) / steps
+        e0.record()
+        for _ in range(steps):
+            fwd_bwd()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_fb = e0.elapsed_time(e1) / steps
+        line = {"config": "cw_mlp (config 5)", "metric": "MPC solves/sec", "value": batch / (ms_f / 1e3),
+                "unit": "solves/s", "forward_ms": ms_f, "forward_plus_vjp_ms": ms_fb,
+                "forward_plus_vjp_solves_per_s": batch / (ms_fb / 1e3), "batch": batch, "horizon": 60,
+                "iterations": "3 SQP x 50 ADMM x 30 PCG; VJP w.r.t. x0, MLP W1 b1 w2, A, B", "dtype": "f32",
+                "n_gpus": 1}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -288,10 +368,14 @@ def main():
                     help="with --admm-only: auto (register-resident kernel where it applies) or the packed kernel")
     ap.add_argument("--admm-pcg", type=int, default=PCG, help="with --admm-only: PCG iterations per ADMM iteration")
     ap.add_argument("--admm-iters", type=int, default=ADMM, help="with --admm-only: ADMM iterations per launch")
+    ap.add_argument("--config", default="", choices=["", "obstacles", "cw_mlp"],
+                    help="time config 4 (obstacles) or config 5 (cw_mlp) on one GPU instead of the default run")
     ap.add_argument("--pcg-sweep", default="", metavar="POINTS",
                     help="config-2 linear-system sweep: ';'-separated nx,nu,N,batch,dtype points "
                          "(e.g. '24,8,128,4096,f32'); 'default' runs a representative set")
     args = ap.parse_args()
+    if args.config:
+        return run_config(args.config)
     if args.pcg_sweep:
         spec = args.pcg_sweep
         if spec == "default":
