@@ -118,3 +118,19 @@ def test_rows_kernel_pcg_early_stop():
     so, _ = _oracle(b, kw)
     assert (_np(status) == 0).all()
     assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+
+
+@pytest.mark.parametrize("linsys", [_ffi.LINSYS_PCG, _ffi.LINSYS_PCG_PACKED])
+def test_initial_control_constraint_rows(linsys):
+    """n0 = n (constrain_initial_control: A0 = I over states and controls):
+    both fp32 kernels against the oracle."""
+    b = dense_blocks(4, 10, 4, 20, 3, seed=21)
+    n = 14
+    b = dict(b)
+    b["A0"] = np.repeat(np.eye(n)[None], 4, 0)
+    b["c0"] = np.random.default_rng(0).normal(size=(4, n))
+    out, iters, status = _solve(b, FIXED, linsys=linsys)
+    so, _ = _oracle(b, FIXED)
+    assert (_np(status) == 0).all()
+    assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+    assert rel_err(_np(out.y_f_0), so.y_f0) < 1e-3

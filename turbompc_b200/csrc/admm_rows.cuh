@@ -74,8 +74,8 @@ struct RowsSmem {
   // stage: a copy of the QP data the assembly and the ADMM-level steps read
   // (q, A0, Am, Ap, G, c0, c, l, u); tslot: one 16 x 16 block per warp for
   // handing -Theta_t^-1 from the Gauss-Jordan warp to the block's owners.
-  size_t th, stage, sq, sa0, sam, sap, sg, sc0, sc, sl, su, tslot, bb, x, gam, xold, yf0, yfd, zg, yg, xig, cx0,
-      cx, gx, ct, gt, red, nelem;
+  size_t th, stage, sq, sa0, sam, sap, sg, sc0, sc, sl, su, tslot, bb, x, gam, xold, yf0, yfd, zg, yg, xig, red,
+      nelem;
   RowsSmem() = default;
   __host__ __device__ RowsSmem(int T, int n, int nx, int n0, int m) {
     using G = RowsGeo;
@@ -103,11 +103,6 @@ struct RowsSmem {
     zg = a4(o); o = zg + (size_t)T * m;
     yg = a4(o); o = yg + (size_t)T * m;
     xig = a4(o); o = xig + (size_t)T * m;
-    cx0 = a4(o); o = cx0 + n0;
-    cx = a4(o); o = cx + (size_t)N * nx;
-    gx = a4(o); o = gx + (size_t)T * m;
-    ct = a4(o); o = ct + n0 + (size_t)N * nx;
-    gt = a4(o); o = gt + (size_t)T * m;
     red = a4(o); o = red + kRedSize;  // residual table and scalars, 2 x 16 dot slots
     nelem = a4(o);
   }
