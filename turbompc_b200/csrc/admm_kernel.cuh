@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
     if constexpr (DIRECT) {
       assemble_theta_phi<NB>(acc, qp, rho_now * P.rho_f_factor, rho_now, P.sigma, T, n, nx, n0, m);
       __syncthreads();
-      if (!riccati_factor_warp<NB>(F, sm + L.fm, n) && threadIdx.x == 0)
+      if (!riccati_factor_warp<NB>(F, sm + L.fm, n, PackedSrc<NB, R>{F}) && threadIdx.x == 0)
         flag |= TMPC_STATUS_SINGULAR_BLOCK;
       __syncthreads();
     } else {

@@ -15,8 +15,8 @@ constexpr int ric_warps() {
   return w < 1 ? 1 : (w > kRicWarps ? kRicWarps : w);
 }
 
-// Copy Theta_t / Phi_t out of the reference-layout S into the packed factor
-// slots, then factor.  One warp per problem.
+// Factor straight from the reference-layout S (no copy into the factor
+// slots first).  One warp per problem.
 template <int NB, typename R>
 __global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R* __restrict__ S, R* factor,
                                                                         int32_t* status, int Nb, int T, int n) {
@@ -28,24 +28,8 @@ __global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R*
   if (b >= Nb) return;
   const size_t opn = Gm::op_elems(T);
   const FactorView<NB, R> F{factor + (size_t)b * opn, T};
-  const R* Sb = S + (size_t)b * T * n * 3 * n;
-  for (int t = 0; t < T; ++t) {
-    R* th = F.lt(t);
-    for (int e = lane; e < NB * NB; e += 32) {  // (i, j), i <= j, into the packed slot
-      const int i = e / NB, j = e - i * NB;
-      if (i <= j) th[tri_index(i, j, NB)] = (i < n && j < n) ? Sb[((size_t)t * n + i) * 3 * n + n + j] : R(0);
-    }
-    for (int e = Gm::TRI + lane; e < Gm::DSTR; e += 32) th[e] = R(0);
-    if (t + 1 < T) {
-      R* W = F.w(t);
-      for (int e = lane; e < NB * NB; e += 32) {
-        const int i = e / NB, j = e - i * NB;
-        W[e] = (i < n && j < n) ? Sb[((size_t)(t + 1) * n + i) * 3 * n + j] : R(0);  // S(t+1, t) = Phi_t
-      }
-    }
-  }
-  __syncwarp();
-  const bool ok = riccati_factor_warp<NB>(F, Msh[wid], n);
+  const RefSrc<R> src{S + (size_t)b * T * n * 3 * n, n};  // Theta / Phi read straight from S
+  const bool ok = riccati_factor_warp<NB>(F, Msh[wid], n, src);
   if (lane == 0 && status) status[b] = ok ? 0 : TMPC_STATUS_SINGULAR_BLOCK;
 }
 

@@ -31,6 +31,28 @@ struct FactorView {
   __device__ R* w(int t) const { return base + (size_t)T * Gm::DSTR + (size_t)t * Gm::OSTR; }
 };
 
+// Where the factor reads Theta_t and Phi_t (indices inside the n x n blocks).
+//   PackedSrc: the factor's own slots (Theta_t packed upper in slot t, Phi_t in
+//              sub-diagonal slot t), as written by assemble_theta_phi.
+//   RefSrc:    the reference-layout S [T][n][3n] directly (no copy-in pass):
+//              Theta_t[r][j] = S[t][r][n + j], Phi_t[i][k] = S[t+1][i][k].
+template <int NB, typename R>
+struct PackedSrc {
+  FactorView<NB, R> F;
+  __device__ R theta(int t, int r, int j) const {
+    const R* th = F.lt(t);
+    return r <= j ? th[tri_index(r, j, NB)] : th[tri_index(j, r, NB)];
+  }
+  __device__ R phi(int t, int i, int k) const { return F.w(t)[i * NB + k]; }
+};
+template <typename R>
+struct RefSrc {
+  const R* S;
+  int n;
+  __device__ R theta(int t, int r, int j) const { return __ldg(S + ((size_t)t * n + r) * 3 * n + n + j); }
+  __device__ R phi(int t, int i, int k) const { return __ldg(S + ((size_t)(t + 1) * n + i) * 3 * n + k); }
+};
+
 // Per-warp shared scratch of riccati_factor_warp (elements): W_{t-1}
 // (row-major) and L_t (column-major), NB x NB each.
 template <int NB>
@@ -38,9 +60,9 @@ __host__ __device__ constexpr int riccati_scratch_elems() {
   return 2 * NB * NB;
 }
 
-// Factor one problem in place.  On entry slot t holds Theta_t (packed upper,
-// as written by assemble_theta_phi) and sub-diagonal slot t holds Phi_t; on
-// exit they hold L_t^T and W_t.  M is per-warp shared scratch of
+// Factor one problem.  Theta_t and Phi_t come from `src` (the factor's own
+// slots, filled by assemble_theta_phi, or the reference-layout S); on exit
+// diagonal slot t holds L_t^T and sub-diagonal slot t holds W_t.  M is per-warp shared scratch of
 // riccati_scratch_elems<NB>() elements, 16-byte aligned.  Called by all 32
 // lanes of one warp; returns false (all lanes) when a pivot is not positive
 // and finite.
@@ -51,8 +73,8 @@ __host__ __device__ constexpr int riccati_scratch_elems() {
 //   it (column k of L_t) in shared memory; lanes j > k update their columns
 //   W_t = Phi_t L_t^-T: lane i runs the forward substitution L w = Phi_t[i, :]^T
 //   column by column (column m of L broadcast from shared memory).
-template <int NB, typename R>
-__device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
+template <int NB, typename R, class Src>
+__device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, const Src& src) {
   static_assert(NB % 4 == 0, "128-bit shared-memory broadcasts");
   constexpr int VEC = 16 / (int)sizeof(R);  // elements per 128-bit access
   const int lane = threadIdx.x & 31;
@@ -64,11 +86,10 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
   bool ok = true;
   for (int t = 0; t < T; ++t) {
     R a[NB];
-    const R* th = F.lt(t);
 #pragma unroll
     for (int r = 0; r < NB; ++r) {
       R v = (r == j) ? R(1) : R(0);  // identity in the padded rows / columns
-      if (r < n && j < n) v = r <= j ? th[tri_index(r, j, NB)] : th[tri_index(j, r, NB)];
+      if (r < n && j < n) v = src.theta(t, r, j);
       a[r] = v;
     }
     if (t > 0 && j < n) {
@@ -133,7 +154,7 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n) {
       R* W = F.w(t);
       R x[NB];
 #pragma unroll
-      for (int k = 0; k < NB; ++k) x[k] = act ? W[j * NB + k] : R(0);
+      for (int k = 0; k < NB; ++k) x[k] = (act && j < n && k < n) ? src.phi(t, j, k) : R(0);
 #pragma unroll
       for (int m = 0; m < NB; ++m) {
         x[m] = x[m] / Lsh[m * NB + m];
