@@ -32,6 +32,29 @@ def test_riccati_solve_matches_dense(dt, nx, nu, N):
     assert rel_err(x.cpu().numpy(), xd) < TOL[dt]
 
 
+def test_riccati_reuses_caller_buffers():
+    """Factor / solve into caller-provided buffers, twice with different
+    systems: the second result does not depend on the first one's contents."""
+    Nb, nx, nu, N = 4, 12, 4, 30
+    c = lambda a: torch.tensor(a, dtype=torch.float64, device="cuda")
+    rng = np.random.default_rng(11)
+    fac = st = x = None
+    for seed in (5, 6):
+        b = synthetic.random_lti(Nb, nx, nu, N, seed=seed)
+        S, _ = ref.compute_S_Phiinv(oracle_qp(b), np.full(Nb, 50.0), 1e-6, np.full(Nb, 0.1))
+        rhs = rng.normal(size=(Nb, N + 1, nx + nu))
+        if fac is None:
+            fac, st = ops.riccati_factor(c(S))
+            x = torch.empty(Nb, N + 1, nx + nu, dtype=torch.float64, device="cuda")
+        else:
+            f2, s2 = ops.riccati_factor(c(S), fac, st)
+            assert f2.data_ptr() == fac.data_ptr() and s2.data_ptr() == st.data_ptr()
+        out = ops.riccati_solve(fac, c(rhs), x)
+        assert out.data_ptr() == x.data_ptr()
+        assert int(st.abs().sum()) == 0
+        assert rel_err(x.cpu().numpy(), ref.solve_block_tridi_dense(S, rhs)) < TOL[torch.float64]
+
+
 def test_riccati_reports_indefinite():
     b = synthetic.random_lti(3, 4, 2, 5, seed=1)
     S, _ = ref.compute_S_Phiinv(oracle_qp(b), np.full(3, 10.0), 1e-6, np.full(3, 0.1))

@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) admm_fused_kernel(const A
     TMPC_FOR_ENTRIES(e, o, T, NB, Gm::VSTR) { xold[o] = w.x[o]; }
     __syncthreads();
     if constexpr (DIRECT) {
-      riccati_solve_warp<NB>(F, gam, ysolve, w.x);
+      riccati_solve_warp<NB, R, false>(F, gam, ysolve, w.x);
       __syncthreads();
     } else {
       pcg_solve<NB, OPS_SMEM>(opS, opP, T, gam, w, red, P.pcg_max_iter, P.pcg_eps);

@@ -83,15 +83,31 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
   R* Lsh = M + NB * NB;  // L_t:     Lsh[k * NB + r] = L[r][k]
   const bool act = lane < NB;
   const int j = act ? lane : 0;
-  bool ok = true;
-  for (int t = 0; t < T; ++t) {
-    R a[NB];
+  auto load_theta = [&](int t, R(&dst)[NB]) {
 #pragma unroll
     for (int r = 0; r < NB; ++r) {
       R v = (r == j) ? R(1) : R(0);  // identity in the padded rows / columns
       if (r < n && j < n) v = src.theta(t, r, j);
-      a[r] = v;
+      dst[r] = v;
     }
+  };
+  auto load_phi = [&](int t, R(&dst)[NB]) {
+#pragma unroll
+    for (int k = 0; k < NB; ++k) dst[k] = (act && j < n && k < n) ? src.phi(t, j, k) : R(0);
+  };
+  // Where Theta_{t+1} is loaded: right after stage t's stores (EARLY_THETA: early
+  // issue) or at the top of stage t + 1.  Measured per block size (B200,
+  // factor of reference-layout S): the early issue is 19 % faster for NB * w = 256
+  // bytes and 7 % for 48 bytes, 4-20 % slower for 64-128 bytes.  (Issuing
+  // Phi_t and Theta_{t+1} at the start of stage t, to overlap the Cholesky,
+  // measured no faster at any size.)
+  constexpr int BW = NB * (int)sizeof(R);
+  constexpr bool EARLY_THETA = BW >= 256 || BW <= 48;
+  bool ok = true;
+  R a[NB];
+  if constexpr (EARLY_THETA) load_theta(0, a);
+  for (int t = 0; t < T; ++t) {
+    if constexpr (!EARLY_THETA) load_theta(t, a);
     if (t > 0 && j < n) {
       R wj[NB];
 #pragma unroll
@@ -153,8 +169,7 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
     if (t < T - 1) {
       R* W = F.w(t);
       R x[NB];
-#pragma unroll
-      for (int k = 0; k < NB; ++k) x[k] = (act && j < n && k < n) ? src.phi(t, j, k) : R(0);
+      load_phi(t, x);
 #pragma unroll
       for (int m = 0; m < NB; ++m) {
         x[m] = x[m] / Lsh[m * NB + m];
@@ -177,68 +192,123 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
       }
     }
     __syncwarp();
+    if constexpr (EARLY_THETA) {
+      if (t < T - 1) load_theta(t + 1, a);
+    }
   }
   return __all_sync(0xffffffffu, ok);
 }
 
 // Solve S x = b with the factor; b, x, y are this problem's [T][VSTR] vectors
 // (shared or global, padded entries of b must be zero).  All 32 lanes.
-template <int NB, typename R>
+// The factor blocks a stage needs (a row / column of W and of L) do not
+// depend on the vectors, so with PF the next stage's blocks are loaded while
+// the current stage's substitution runs (the substitution chain is
+// sequential in t, and a warp-synchronous step would otherwise wait a full
+// memory latency per stage).  PIPE = false keeps the register footprint of
+// the unpipelined solve (for register-capped callers).
+template <int NB, typename R, bool PIPE = true>
 __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y, R* x) {
   using Gm = Geo<NB, R>;
+  constexpr bool PF = PIPE && NB * (int)sizeof(R) <= 128;
   const int lane = threadIdx.x & 31;
   const int T = F.T;
   const bool act = lane < NB;
   const int li = act ? lane : 0;
+  // forward stage t reads W_{t-1} row li and L_t row li (packed (k, li), k <= li)
+  auto load_fwd = [&](int t, R(&w)[NB], R(&l)[NB], R& dv) {
+    const R* W = F.w(t > 0 ? t - 1 : 0) + li * NB;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) w[k] = t > 0 ? W[k] : R(0);
+    const R* lt = F.lt(t);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) l[k] = (k <= li) ? lt[tri_index(k, li, NB)] : R(0);
+    dv = lt[tri_index(li, li, NB)];
+  };
+  // backward stage t reads W_t column li and L_t^T row li (packed (li, k), k >= li)
+  auto load_bwd = [&](int t, R(&w)[NB], R(&l)[NB], R& dv) {
+    const R* W = F.w(t < T - 1 ? t : 0);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) w[k] = t < T - 1 ? W[k * NB + li] : R(0);
+    const R* lt = F.lt(t);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) l[k] = (k >= li) ? lt[tri_index(li, k, NB)] : R(0);
+    dv = lt[tri_index(li, li, NB)];
+  };
+  R wv[NB], lv[NB], dv;
   // forward: y_t = L_t^-1 (b_t - W_{t-1} y_{t-1})
+  load_fwd(0, wv, lv, dv);
   for (int t = 0; t < T; ++t) {
+    R wn[NB], ln[NB], dn = R(1);
+    if constexpr (PF) {
+      if (t + 1 < T) load_fwd(t + 1, wn, ln, dn);
+    }
     R u = act ? b[t * Gm::VSTR + li] : R(0);
     if (t > 0) {
-      const R* W = F.w(t - 1) + li * NB;
       const R* yp = y + (t - 1) * Gm::VSTR;
       R s = R(0);
 #pragma unroll
-      for (int k = 0; k < NB; ++k) s = fma(W[k], yp[k], s);
+      for (int k = 0; k < NB; ++k) s = fma(wv[k], yp[k], s);
       u -= s;
     }
-    const R* lt = F.lt(t);
-    R lcol[NB];  // L[li][k] = L^T packed (k, li) for k <= li
-#pragma unroll
-    for (int k = 0; k < NB; ++k) lcol[k] = (k <= li) ? lt[tri_index(k, li, NB)] : R(0);
-    const R dinv = R(1) / lt[tri_index(li, li, NB)];  // 1 / L[li][li]
+    const R dinv = R(1) / dv;  // 1 / L[li][li]
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
       const R yk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
-      if (li > k) u = fma(-lcol[k], yk, u);
+      if (li > k) u = fma(-lv[k], yk, u);
       if (li == k) u = yk;
     }
     if (act) y[t * Gm::VSTR + li] = u;
     __syncwarp();
+    if (t + 1 < T) {
+      if constexpr (PF) {
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+          wv[k] = wn[k];
+          lv[k] = ln[k];
+        }
+        dv = dn;
+      } else {
+        load_fwd(t + 1, wv, lv, dv);
+      }
+    }
   }
   // backward: x_t = L_t^-T (y_t - W_t^T x_{t+1})
+  load_bwd(T - 1, wv, lv, dv);
   for (int t = T - 1; t >= 0; --t) {
+    R wn[NB], ln[NB], dn = R(1);
+    if constexpr (PF) {
+      if (t > 0) load_bwd(t - 1, wn, ln, dn);
+    }
     R u = act ? y[t * Gm::VSTR + li] : R(0);
     if (t < T - 1) {
-      const R* W = F.w(t);
       const R* xn = x + (t + 1) * Gm::VSTR;
       R s = R(0);
 #pragma unroll
-      for (int k = 0; k < NB; ++k) s = fma(W[k * NB + li], xn[k], s);
+      for (int k = 0; k < NB; ++k) s = fma(wv[k], xn[k], s);
       u -= s;
     }
-    const R* lt = F.lt(t);
-    R lrow[NB];  // L^T[li][k] = L[k][li] = packed (li, k) for k >= li
-#pragma unroll
-    for (int k = 0; k < NB; ++k) lrow[k] = (k >= li) ? lt[tri_index(li, k, NB)] : R(0);
-    const R dinv = R(1) / lt[tri_index(li, li, NB)];
+    const R dinv = R(1) / dv;
 #pragma unroll
     for (int k = NB - 1; k >= 0; --k) {
       const R xk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
-      if (li < k) u = fma(-lrow[k], xk, u);
+      if (li < k) u = fma(-lv[k], xk, u);
       if (li == k) u = xk;
     }
     if (act) x[t * Gm::VSTR + li] = u;
     __syncwarp();
+    if (t > 0) {
+      if constexpr (PF) {
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+          wv[k] = wn[k];
+          lv[k] = ln[k];
+        }
+        dv = dn;
+      } else {
+        load_bwd(t - 1, wv, lv, dv);
+      }
+    }
   }
 }
 

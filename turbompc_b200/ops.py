@@ -246,28 +246,42 @@ def admm_initial_state(qp: QPData, rho_bar, x0: Optional[torch.Tensor] = None) -
                      z.contiguous(), torch.zeros_like(z), _rho_vec(rho_bar, qp).clone())
 
 
-def riccati_factor(S: torch.Tensor):
+def riccati_factor(S: torch.Tensor, factor: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None):
     """Block Cholesky of reference-layout S (Nb, T, n, 3n).  Returns
-    (factor uint8 tensor, status int32 (Nb,))."""
+    (factor uint8 tensor, status int32 (Nb,)); ``factor`` / ``status`` reuse
+    caller buffers (uint8 of at least the factor size, int32 (Nb,))."""
     lib = _ffi.load()
     B, T, n = S.shape[:3]
     d = _ffi.TmpcDims(B, T, n, n, 0, 0)
     nbytes = lib.tmpc_riccati_factor_bytes(C.byref(d), S.dtype.itemsize)
     if nbytes == 0 and B > 0:
         raise ValueError(f"unsupported dimensions for the block Cholesky (n={n})")
-    fac = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=S.device)
-    st = torch.zeros(B, dtype=torch.int32, device=S.device)
+    if factor is not None:
+        if factor.dtype != torch.uint8 or factor.numel() < nbytes or not factor.is_contiguous():
+            raise ValueError(f"factor buffer must be contiguous uint8 with at least {nbytes} bytes")
+        fac = factor
+    else:
+        fac = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=S.device)
+    if status is not None:
+        if status.dtype != torch.int32 or status.numel() != B:
+            raise ValueError("status buffer must be int32 with one entry per problem")
+        st = status
+    else:
+        st = torch.zeros(B, dtype=torch.int32, device=S.device)
     name = f"tmpc_riccati_factor_{_suffix(S.dtype)}"
     _ffi.check(name, getattr(lib, name)(C.byref(d), _ptr(S), fac.data_ptr(), _ptr(st), _stream(S.device)))
     return fac, st
 
 
-def riccati_solve(factor: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
-    """Solve S x = rhs (rhs (Nb, T, n)) with a factor from riccati_factor."""
+def riccati_solve(factor: torch.Tensor, rhs: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Solve S x = rhs (rhs (Nb, T, n)) with a factor from riccati_factor
+    (into ``out`` when given: same shape / dtype as rhs, contiguous)."""
     lib = _ffi.load()
     B, T, n = rhs.shape
     d = _ffi.TmpcDims(B, T, n, n, 0, 0)
-    x = torch.empty_like(rhs)
+    if out is not None and (out.shape != rhs.shape or out.dtype != rhs.dtype or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous tensor shaped like rhs")
+    x = torch.empty_like(rhs) if out is None else out
     name = f"tmpc_riccati_solve_{_suffix(rhs.dtype)}"
     _ffi.check(name, getattr(lib, name)(C.byref(d), factor.data_ptr(), _ptr(rhs), _ptr(x), _stream(rhs.device)))
     return x
