@@ -521,6 +521,10 @@ def main():
         achieved = b_launch / (kms / 1e3) / 1e9
         kernel = "admm_rows_kernel" if (T <= 52 and 8 < n <= 16) else "admm_fused_kernel"
         peak, pk_kind = peaks()
+        # QP data one fused ADMM launch reads (one SQP iteration's D, E, q,
+        # A_minus, A_plus, c, G, l, u for this GPU's shard, fp32).
+        qp_gb = shard * 4 * (T * n * n * 2 + T * n + 2 * (T - 1) * nx * n + (T - 1) * nx
+                                               + T * m * (n + 2)) / 1e9
         cb = None
         if world == 1 and not args.no_cpu_baseline:
             try:
@@ -531,9 +535,12 @@ def main():
             "metric": METRIC, "value": value, "unit": "solves/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "quadrotor-12 N=50 batch 65536, 5 SQP x 30 ADMM x 30 PCG (fixed counts)",
+            "config": {"workload": f"quadrotor-12 N={N_HORIZON} batch {args.batch}, 5 SQP x 30 ADMM x 30 PCG "
+                                   "(fixed counts)",
                        "global_batch": args.batch, "per_gpu_batch": shard, "horizon": N_HORIZON,
-                       "parallelism": f"batch-shard x{world}", "l2": "inputs > L2 (QP data ~13 GB per step)"},
+                       "parallelism": f"batch-shard x{world}",
+                       "l2": f"inputs > L2 (QP data ~{qp_gb:.1f} GB per SQP iteration)" if qp_gb > 0.126
+                             else f"QP data {qp_gb:.3f} GB per SQP iteration (fits L2)"},
             "e2e": {"value": args.batch / (e2e_ms / 1e3), "unit": "solves/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

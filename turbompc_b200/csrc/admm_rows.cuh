@@ -214,10 +214,28 @@ __device__ __forceinline__ void rows_smv(float (&y)[2], const RowOps& o, const f
   y[1] = (l1 + d1) + u1;
 }
 
+// y = (S z) at the owned rows for z = Phiinv r, without Theta: with
+// w = Theta^-1 r and f = F w (F: the off-diagonal blocks of S), z = Theta^-1 f - w,
+// so Theta z = f - r and S z = (f - r) + F z.  f comes from rows_prec; only
+// the two off-diagonal block products of z remain (Theta's rows are not
+// read).  The identity holds up to the rounding of Theta^-1 (Theta Theta^-1 =
+// I): with the quadrotor QPs (cond(Theta) ~ 1e3) the fp32 PCG iterate after
+// 30 iterations differs from the fp64 one by 2e-5 relative with it and by
+// 7e-6 with the explicit Theta product.
+__device__ __forceinline__ void rows_smv_prec(float (&y)[2], const RowOps& o, const float* vt, const float (&fw)[2],
+                                              const float (&r)[2]) {
+  float l0 = 0.f, l1 = 0.f, u0 = 0.f, u1 = 0.f;
+  rows_bdot(l0, l1, o.lr[0], o.lr[1], vt);
+  rows_bdot(u0, u1, o.lc[0], o.lc[1], vt + 2 * RowsGeo::BSTR);
+  y[0] = (l0 + (fw[0] - r[0])) + u0;
+  y[1] = (l1 + (fw[1] - r[1])) + u1;
+}
+
 // z = Phiinv r in factored form.  bt points at row t (stage t - 1) of the p
 // buffer; the r, w, u buffers follow at constant offsets.  Contains one
 // __syncthreads (all threads call it).
-__device__ __forceinline__ void rows_prec(float (&z)[2], const float (&r)[2], const RowOps& o, float* bt, int q) {
+__device__ __forceinline__ void rows_prec(float (&z)[2], float (&fw)[2], const float (&r)[2], const RowOps& o, float* bt,
+                                          int q) {
   constexpr int VS = RowsGeo::BSTR;
   float* wb = bt + RowsGeo::BUF;      // row t of the w buffer
   float* rrow = bt + 2 * RowsGeo::BUF + VS;
@@ -234,8 +252,10 @@ __device__ __forceinline__ void rows_prec(float (&z)[2], const float (&r)[2], co
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
   rows_bdot(a0, a1, o.lr[0], o.lr[1], wb);
   rows_bdot(b0, b1, o.lc[0], o.lc[1], wb + 2 * VS);
-  urow[q] = a0 + b0;
-  urow[q + 8] = a1 + b1;
+  fw[0] = a0 + b0;
+  fw[1] = a1 + b1;
+  urow[q] = fw[0];
+  urow[q + 8] = fw[1];
   __syncwarp();
   float v0, v1;
   rows_bdot_split(v0, v1, o.ti[0], o.ti[1], urow);
@@ -308,7 +328,9 @@ __device__ __forceinline__ void rows_block_sum2(float& a, float& b, float* slots
 //   p = u + beta p, s (= S p) = w + beta s, x += alpha p, r -= alpha s.
 // The stopping test |gamma| < 1e-12 + eps |gamma_0| runs before each update,
 // as the reference's |eta| test, so the iteration counts agree.  Three CTA
-// barriers and one reduction per iteration instead of four and two.  xs /
+// barriers and one reduction per iteration instead of four and two.  w = S u
+// is formed without Theta (rows_smv_prec); the initial residual uses the
+// explicit S x.  xs /
 // gam are [T][VSTR] block vectors in shared memory; x is read from and
 // written back to xs.  Returns the iteration count.
 __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
@@ -330,11 +352,12 @@ __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float*
   rows_smv(w, o, th_row, bt);
   r[0] = (act ? gam[t * VS + q] : 0.f) - w[0];
   r[1] = (act ? gam[t * VS + q + 8] : 0.f) - w[1];
-  rows_prec(u, r, o, bt, q);  // its barrier ends every read of x in the buffer
+  float fw[2];
+  rows_prec(u, fw, r, o, bt, q);  // its barrier ends every read of x in the buffer
   prow[q] = u[0];
   prow[q + 8] = u[1];
   __syncthreads();
-  rows_smv(w, o, th_row, bt);
+  rows_smv_prec(w, o, bt, fw, r);
   float gamma = fmaf(r[1], u[1], r[0] * u[0]);
   float delta = fmaf(w[1], u[1], w[0] * u[0]);
   rows_block_sum2(gamma, delta, slots);
@@ -352,11 +375,11 @@ __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float*
     x[1] = fmaf(alpha, p[1], x[1]);
     r[0] = fmaf(-alpha, sv[0], r[0]);
     r[1] = fmaf(-alpha, sv[1], r[1]);
-    rows_prec(u, r, o, bt, q);  // its barrier ends every read of the previous u
+    rows_prec(u, fw, r, o, bt, q);  // its barrier ends every read of the previous u
     prow[q] = u[0];
     prow[q + 8] = u[1];
     __syncthreads();
-    rows_smv(w, o, th_row, bt);
+    rows_smv_prec(w, o, bt, fw, r);
     float gnew = fmaf(r[1], u[1], r[0] * u[0]);
     float dl = fmaf(w[1], u[1], w[0] * u[0]);
     rows_block_sum2(gnew, dl, slots);
