@@ -111,13 +111,24 @@ def test_rows_kernel_convergence_stop():
 
 
 def test_rows_kernel_pcg_early_stop():
-    """PCG tolerance > 0: the per-solve stop test |eta| < 1e-12 + eps |eta0|."""
+    """PCG tolerance > 0: the per-solve stop test |eta| < 1e-12 + eps |eta0|.
+    eta = r.z is a squared norm, so eps = 1e-4 stops at about 1e-2 of the
+    initial residual, and an fp32 stop decision near the threshold can fall
+    one iteration from the fp64 oracle's.  The early stops move the oracle's
+    solution by `shift` (5e-3 relative here) away from the full-count one; the
+    kernel must follow the stopped iterates: within shift / 2 of the oracle's
+    stopped solution (measured 1.1e-3) and farther from the full-count one."""
     b = dense_blocks(4, 12, 4, 20, 4, seed=9)
     kw = dict(FIXED, max_iter=10, pcg_max_iter=50, pcg_eps=1e-4)
     out, _, status = _solve(b, kw)
     so, _ = _oracle(b, kw)
+    so_full, _ = _oracle(b, dict(kw, pcg_eps=0.0))
     assert (_np(status) == 0).all()
-    assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+    shift = rel_err(so.x, so_full.x)
+    assert shift > 1e-3, "the stop test must change the result for this check to mean anything"
+    x = _np(out.x_blocks)
+    assert rel_err(x, so.x) < 0.5 * shift
+    assert rel_err(x, so_full.x) > rel_err(x, so.x)
 
 
 @pytest.mark.parametrize("linsys", [_ffi.LINSYS_PCG, _ffi.LINSYS_PCG_PACKED])
