@@ -379,7 +379,8 @@ def main():
     if args.pcg_sweep:
         spec = args.pcg_sweep
         if spec == "default":
-            spec = "6,3,32,65536,f32;12,4,64,16384,f32;24,8,128,4096,f32;24,8,128,2048,f64"
+            spec = ("6,3,32,65536,f32;12,4,64,16384,f32;24,8,128,4096,f32;"
+                    "6,3,32,65536,f64;12,4,64,16384,f64;24,8,128,2048,f64")
         pts = []
         for item in spec.split(";"):
             a = item.split(",")

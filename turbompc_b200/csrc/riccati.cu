@@ -7,55 +7,71 @@
 namespace tmpc {
 
 constexpr int kRicWarps = 4;
-// Warps (= problems) per block: up to 4 within 40 KB of static shared memory.
+// Lanes per problem: NB <= 16 runs two problems per warp (16-lane groups);
+// one problem per warp would leave at least half of every warp idle.
+template <int NB>
+constexpr int ric_group() {
+  return NB <= 16 ? 16 : 32;
+}
+// Warps per block: up to 4 within 40 KB of static shared memory (one
+// scratch area per group).
 template <int NB, typename R>
 constexpr int ric_warps() {
-  constexpr int per = riccati_scratch_elems<NB>() * (int)sizeof(R);
+  constexpr int per = riccati_scratch_elems<NB>() * (int)sizeof(R) * (32 / ric_group<NB>());
   constexpr int w = 40960 / per;
   return w < 1 ? 1 : (w > kRicWarps ? kRicWarps : w);
 }
 
 // Factor straight from the reference-layout S (no copy into the factor
-// slots first).  One warp per problem.
+// slots first).  One group of ric_group<NB>() lanes per problem.
 template <int NB, typename R>
 __global__ void __launch_bounds__(32 * kRicWarps) riccati_factor_kernel(const R* __restrict__ S, R* factor,
                                                                         int32_t* status, int Nb, int T, int n) {
   using Gm = Geo<NB, R>;
-  constexpr int WPB = ric_warps<NB, R>();
-  __shared__ __align__(16) R Msh[WPB][riccati_scratch_elems<NB>()];
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x * WPB + wid;
-  if (b >= Nb) return;
+  constexpr int G = ric_group<NB>();
+  constexpr int GPB = ric_warps<NB, R>() * (32 / G);  // groups (problems) per block
+  __shared__ __align__(16) R Msh[GPB][riccati_scratch_elems<NB>()];
+  const int grp = threadIdx.x / G, gl = threadIdx.x & (G - 1);
+  const int first_in_warp = blockIdx.x * GPB + (threadIdx.x >> 5) * (32 / G);
+  if (first_in_warp >= Nb) return;  // the whole warp is past the batch
+  int b = blockIdx.x * GPB + grp;
+  const bool valid = b < Nb;  // a spare half-warp repeats the last problem without storing
+  if (!valid) b = Nb - 1;
   const size_t opn = Gm::op_elems(T);
   const FactorView<NB, R> F{factor + (size_t)b * opn, T};
   const RefSrc<R> src{S + (size_t)b * T * n * 3 * n, n};  // Theta / Phi read straight from S
-  const bool ok = riccati_factor_warp<NB>(F, Msh[wid], n, src);
-  if (lane == 0 && status) status[b] = ok ? 0 : TMPC_STATUS_SINGULAR_BLOCK;
+  const bool ok = riccati_factor_warp<NB, R, RefSrc<R>, G>(F, Msh[grp], n, src, valid);
+  if (gl == 0 && status && valid) status[b] = ok ? 0 : TMPC_STATUS_SINGULAR_BLOCK;
 }
 
-// One warp per problem; b / y / x staged in shared memory as [T][VSTR].
+// One group of ric_group<NB>() lanes per problem (32 / G problems per
+// one-warp block); each group stages its b / y / x in shared memory as [T][VSTR].
 template <int NB, typename R>
 __global__ void __launch_bounds__(32) riccati_solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs,
                                                            R* x_out, int Nb, int T, int n) {
   using Gm = Geo<NB, R>;
+  constexpr int G = ric_group<NB>();
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  R* sm = reinterpret_cast<R*>(smem_raw);
-  const int b = blockIdx.x;
-  if (b >= Nb) return;
+  const int grp = threadIdx.x / G, gl = threadIdx.x & (G - 1);
+  int b = blockIdx.x * (32 / G) + grp;
+  const bool valid = b < Nb;  // a spare half-warp solves the last problem again and stores nothing
+  if (!valid) b = Nb - 1;
   const size_t VS = (size_t)T * Gm::VSTR;
+  R* sm = reinterpret_cast<R*>(smem_raw) + grp * 3 * VS;
   R* bb = sm;
   R* y = sm + VS;
   R* x = sm + 2 * VS;
-  for (size_t e = threadIdx.x; e < 3 * VS; e += 32) sm[e] = R(0);
+  for (size_t e = gl; e < 3 * VS; e += G) sm[e] = R(0);
   __syncwarp();
-  for (int e = threadIdx.x; e < T * n; e += 32) {
+  for (int e = gl; e < T * n; e += G) {
     const int t = e / n, j = e - t * n;
     bb[t * Gm::VSTR + j] = rhs[(size_t)b * T * n + e];
   }
   __syncwarp();
   const FactorView<NB, R> F{const_cast<R*>(factor) + (size_t)b * Gm::op_elems(T), T};
-  riccati_solve_warp<NB>(F, bb, y, x);
-  for (int e = threadIdx.x; e < T * n; e += 32) {
+  riccati_solve_warp<NB, R, true, G>(F, bb, y, x);
+  if (!valid) return;
+  for (int e = gl; e < T * n; e += G) {
     const int t = e / n, j = e - t * n;
     x_out[(size_t)b * T * n + e] = x[t * Gm::VSTR + j];
   }
@@ -70,8 +86,9 @@ int riccati_factor(const TmpcDims* d, const R* S, void* factor, int32_t* status,
   if ((reinterpret_cast<uintptr_t>(factor) & 15) != 0) return TMPC_ERR_WORKSPACE;  // 128-bit stores of W
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    constexpr int WPB = ric_warps<NB, R>();  // the kernel indexes its scratch by warp: launch exactly WPB warps
-    const int grid = (d->Nb + WPB - 1) / WPB;
+    constexpr int WPB = ric_warps<NB, R>();  // the kernel indexes its scratch by group: launch exactly WPB warps
+    constexpr int GPB = WPB * (32 / ric_group<NB>());
+    const int grid = (d->Nb + GPB - 1) / GPB;
     riccati_factor_kernel<NB, R><<<grid, 32 * WPB, 0, st>>>(S, static_cast<R*>(factor), status, d->Nb, d->T, d->n);
     return (int)cudaPeekAtLastError();
   });
@@ -85,12 +102,13 @@ int riccati_solve(const TmpcDims* d, const void* factor, const R* rhs, R* x, cud
   if (!factor || !rhs || !x) return TMPC_ERR_NULL_ARG;
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    const size_t smem = 3 * (size_t)d->T * Geo<NB, R>::VSTR * sizeof(R);
+    constexpr int GPB = 32 / ric_group<NB>();  // problems per one-warp block
+    const size_t smem = GPB * 3 * (size_t)d->T * Geo<NB, R>::VSTR * sizeof(R);
     if ((long)smem > max_dyn_smem()) return (int)TMPC_ERR_SMEM;
     auto k = riccati_solve_kernel<NB, R>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    k<<<d->Nb, 32, smem, st>>>(static_cast<const R*>(factor), rhs, x, d->Nb, d->T, d->n);
+    k<<<(d->Nb + GPB - 1) / GPB, 32, smem, st>>>(static_cast<const R*>(factor), rhs, x, d->Nb, d->T, d->n);
     return (int)cudaPeekAtLastError();
   });
 }

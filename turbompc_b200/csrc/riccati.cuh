@@ -73,11 +73,18 @@ __host__ __device__ constexpr int riccati_scratch_elems() {
 //   it (column k of L_t) in shared memory; lanes j > k update their columns
 //   W_t = Phi_t L_t^-T: lane i runs the forward substitution L w = Phi_t[i, :]^T
 //   column by column (column m of L broadcast from shared memory).
-template <int NB, typename R, class Src>
-__device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, const Src& src) {
+//
+// G = 32: the whole warp works on one problem.  G = 16 (NB <= 16): each
+// half-warp factors its own problem (two problems per warp; both halves run
+// the same T and n, so they stay in step through the warp-wide __syncwarp);
+// `store` = false runs a half without writing the factor (the spare half of
+// the last warp).
+template <int NB, typename R, class Src, int G = 32>
+__device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, const Src& src, bool store = true) {
   static_assert(NB % 4 == 0, "128-bit shared-memory broadcasts");
+  static_assert(G == 32 || (G == 16 && NB <= 16), "half-warp groups need NB <= 16");
   constexpr int VEC = 16 / (int)sizeof(R);  // elements per 128-bit access
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & (G - 1);
   const int T = F.T;
   R* Wsh = M;            // W_{t-1}: Wsh[r * NB + k]
   R* Lsh = M + NB * NB;  // L_t:     Lsh[k * NB + r] = L[r][k]
@@ -161,9 +168,9 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
     __syncwarp();
     // Store L_t^T packed (entry (a, b), a <= b, is L[b][a] = Lsh[a * NB + b]).
     R* lt = F.lt(t);
-    for (int e = lane; e < NB * NB; e += 32) {
+    for (int e = lane; e < NB * NB; e += G) {
       const int bb = e / NB, aa = e - bb * NB;
-      if (aa <= bb) lt[tri_index(aa, bb, NB)] = Lsh[aa * NB + bb];
+      if (aa <= bb && store) lt[tri_index(aa, bb, NB)] = Lsh[aa * NB + bb];
     }
     // W_t = Phi_t L_t^-T, row i = lane.
     if (t < T - 1) {
@@ -186,7 +193,7 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
       if (act) {
 #pragma unroll
         for (int k = 0; k < NB; k += VEC) {
-          st128(W + j * NB + k, &x[k]);
+          if (store) st128(W + j * NB + k, &x[k]);
           st128(Wsh + j * NB + k, &x[k]);
         }
       }
@@ -196,7 +203,12 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
       if (t < T - 1) load_theta(t + 1, a);
     }
   }
-  return __all_sync(0xffffffffu, ok);
+  if constexpr (G == 32) {
+    return __all_sync(0xffffffffu, ok);
+  } else {
+    const unsigned bad = __ballot_sync(0xffffffffu, !ok);
+    return ((bad >> (threadIdx.x & 16)) & 0xffffu) == 0;  // this half's lanes only
+  }
 }
 
 // Solve S x = b with the factor; b, x, y are this problem's [T][VSTR] vectors
@@ -207,11 +219,14 @@ __device__ bool riccati_factor_warp(const FactorView<NB, R>& F, R* M, int n, con
 // sequential in t, and a warp-synchronous step would otherwise wait a full
 // memory latency per stage).  PIPE = false keeps the register footprint of
 // the unpipelined solve (for register-capped callers).
-template <int NB, typename R, bool PIPE = true>
+// G = 16 (NB <= 16): one problem per half-warp, as in riccati_factor_warp
+// (shuffles stay inside the half; b, y, x are the half's own vectors).
+template <int NB, typename R, bool PIPE = true, int G = 32>
 __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y, R* x) {
   using Gm = Geo<NB, R>;
+  static_assert(G == 32 || (G == 16 && NB <= 16), "half-warp groups need NB <= 16");
   constexpr bool PF = PIPE && NB * (int)sizeof(R) <= 128;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & (G - 1);
   const int T = F.T;
   const bool act = lane < NB;
   const int li = act ? lane : 0;
@@ -254,7 +269,7 @@ __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y,
     const R dinv = R(1) / dv;  // 1 / L[li][li]
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
-      const R yk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
+      const R yk = __shfl_sync(0xffffffffu, u * dinv, k, G);  // lane k's scaled value
       if (li > k) u = fma(-lv[k], yk, u);
       if (li == k) u = yk;
     }
@@ -291,7 +306,7 @@ __device__ void riccati_solve_warp(const FactorView<NB, R>& F, const R* b, R* y,
     const R dinv = R(1) / dv;
 #pragma unroll
     for (int k = NB - 1; k >= 0; --k) {
-      const R xk = __shfl_sync(0xffffffffu, u * dinv, k);  // lane k's scaled value
+      const R xk = __shfl_sync(0xffffffffu, u * dinv, k, G);  // lane k's scaled value
       if (li < k) u = fma(-lv[k], xk, u);
       if (li == k) u = xk;
     }
