@@ -520,7 +520,7 @@ def main():
         T, n, nx, m, n0 = qp.T, qp.n, qp.nx, qp.m, qp.n0
         b_launch = algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, 4) * shard
         achieved = b_launch / (kms / 1e3) / 1e9
-        kernel = "admm_rows_kernel" if (T <= 52 and 8 < n <= 16) else "admm_fused_kernel"
+        kernel = "admm_rows_kernel" if (T <= 64 and 8 < n <= 16) else "admm_fused_kernel"
         peak, pk_kind = peaks()
         # QP data one fused ADMM launch reads (one SQP iteration's D, E, q,
         # A_minus, A_plus, c, G, l, u for this GPU's shard, fp32).

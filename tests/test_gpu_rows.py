@@ -57,6 +57,24 @@ def test_rows_kernel_matches_oracle(nx, nu, N, m):
         assert rel_err(_np(out.y_g), so.y_g) < 1e-3
 
 
+@pytest.mark.parametrize("nx,nu,N,m", [(6, 3, 60, 3),    # T = 61, n = 9: the config-5 shape
+                                       (10, 2, 58, 2)])  # T = 59, n = 12
+def test_rows_kernel_64_stage_instance(nx, nu, N, m):
+    """Horizons with 52 < T <= 64 run the 64-stage instance (512 threads).
+    It must match the oracle, and it must be the kernel that ran: its
+    rounding differs from the packed kernel's on the same problems."""
+    b = dense_blocks(4, nx, nu, N, m, seed=7 + N)
+    out, iters, status = _solve(b, FIXED)
+    packed, _, _ = _solve(b, FIXED, linsys=_ffi.LINSYS_PCG_PACKED)
+    so, _ = _oracle(b, FIXED)
+    assert (_np(status) == 0).all()
+    assert (_np(iters) == FIXED["max_iter"]).all()
+    assert rel_err(_np(out.x_blocks), so.x) < 1e-3
+    assert rel_err(_np(out.y_f_dyn), so.y_fdyn) < 1e-3
+    assert rel_err(_np(out.z_g), so.z_g) < 1e-3
+    assert not torch.equal(out.x_blocks, packed.x_blocks)
+
+
 def test_rows_kernel_lti_config_matches_packed_kernel():
     """Quadrotor-sized LTI batch: register-resident and packed kernels agree to
     fp32 rounding (and are different code paths: not bit-identical)."""

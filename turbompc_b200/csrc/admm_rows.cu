@@ -7,20 +7,20 @@ bool admm_rows_ok(int T, int n, int nx, int n0, int m) {
   if (!admm_rows_applicable(T, n, nx, n0, m)) return false;
   // The kernel must fit on one SM (registers of rows_threads(T) threads + shared memory).
   const size_t smem = admm_rows_smem_bytes(T, n, nx, n0, m);
-  if (cudaFuncSetAttribute(admm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return false;
+  auto k = rows_cap(T) == 52 ? admm_rows_kernel<52> : admm_rows_kernel<64>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, admm_rows_kernel, rows_threads(T), smem) != cudaSuccess)
-    return false;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, rows_threads(T), smem) != cudaSuccess) return false;
   return blocks >= 1;
 }
 
 int launch_admm_rows(const AdmmParams<float>& P, cudaStream_t st) {
   if (!admm_rows_applicable(P.T, P.n, P.nx, P.n0, P.m)) return TMPC_ERR_UNSUPPORTED;
   const size_t smem = admm_rows_smem_bytes(P.T, P.n, P.nx, P.n0, P.m);
-  cudaError_t e = cudaFuncSetAttribute(admm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto k = rows_cap(P.T) == 52 ? admm_rows_kernel<52> : admm_rows_kernel<64>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
-  admm_rows_kernel<<<P.Nb, rows_threads(P.T), smem, st>>>(P);
+  k<<<P.Nb, rows_threads(P.T), smem, st>>>(P);
   return (int)cudaPeekAtLastError();
 }
 

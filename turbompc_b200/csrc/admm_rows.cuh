@@ -57,10 +57,15 @@ struct RowsGeo {
   static constexpr int TSTR = 20;         // row stride of a Theta block in shared memory
   static constexpr int TBLK = 16 * TSTR;  // Theta block stride
   static constexpr int SQ = 256;          // dense 16 x 16 scratch block
-  static constexpr int TMAX = 52;
-  static constexpr int MAX_THREADS = TPB * TMAX;  // 416
-  static constexpr int BUF = (TMAX + 3) * BSTR;   // one broadcast buffer (zero rows around the stages)
+  static constexpr int TMAX = 64;  // largest horizon + 1 (two instances: 52 and 64 stages)
 };
+// Stage capacity of the kernel instance that runs T stages: 52 (the quadrotor
+// size, 416 threads) or 64 (512 threads; 128 registers per thread either way).
+// The broadcast buffers are sized by the capacity, and the 64-stage instance's
+// larger buffers would push the 52-stage problems past the shared-memory limit.
+__host__ __device__ constexpr int rows_cap(int T) { return T <= 52 ? 52 : 64; }
+// One broadcast buffer (zero rows around the stages) for capacity TM.
+__host__ __device__ constexpr int rows_buf(int TM) { return (TM + 3) * RowsGeo::BSTR; }
 static_assert(Geo<16, float>::VSTR == RowsGeo::VSTR, "block-vector stride shared with the ADMM helpers");
 
 __host__ __device__ constexpr int rows_threads(int T) { return (T * RowsGeo::TPB + 31) / 32 * 32; }
@@ -77,7 +82,7 @@ struct RowsSmem {
   size_t th, stage, sq, sa0, sam, sap, sg, sc0, sc, sl, su, tslot, bb, x, gam, xold, yf0, yfd, zg, yg, xig, red,
       nelem;
   RowsSmem() = default;
-  __host__ __device__ RowsSmem(int T, int n, int nx, int n0, int m) {
+  __host__ __device__ RowsSmem(int T, int n, int nx, int n0, int m, int buf) {
     using G = RowsGeo;
     const int N = T - 1, TP = rows_tpad(T);
     auto a4 = [](size_t v) { return (v + 3) & ~size_t(3); };
@@ -94,7 +99,7 @@ struct RowsSmem {
     sl = o; o = a4(o + (size_t)T * m);
     su = o; o = a4(o + (size_t)T * m);
     tslot = o; o += (size_t)(rows_threads(T) / 32) * G::SQ;
-    bb = o; o += 4 * (size_t)G::BUF;  // p, w, r, u broadcast buffers at constant offsets
+    bb = o; o += 4 * (size_t)buf;  // p, w, r, u broadcast buffers at constant offsets
     x = o; o += (size_t)T * G::VSTR;
     gam = o; o += (size_t)T * G::VSTR;
     xold = o; o += (size_t)T * G::VSTR;
@@ -235,12 +240,13 @@ __device__ __forceinline__ void rows_smv_prec(float (&y)[2], const RowOps& o, co
 // z = Phiinv r in factored form.  bt points at row t (stage t - 1) of the p
 // buffer; the r, w, u buffers follow at constant offsets.  Contains one
 // __syncthreads (all threads call it).
+template <int BUF>
 __device__ __forceinline__ void rows_prec(float (&z)[2], float (&fw)[2], const float (&r)[2], const RowOps& o, float* bt,
                                           int q) {
   constexpr int VS = RowsGeo::BSTR;
-  float* wb = bt + RowsGeo::BUF;      // row t of the w buffer
-  float* rrow = bt + 2 * RowsGeo::BUF + VS;
-  float* urow = bt + 3 * RowsGeo::BUF + VS;
+  float* wb = bt + BUF;      // row t of the w buffer
+  float* rrow = bt + 2 * BUF + VS;
+  float* urow = bt + 3 * BUF + VS;
   rrow[q] = r[0];
   rrow[q + 8] = r[1];
   __syncwarp();  // the eight threads of a stage block share a warp
@@ -334,6 +340,7 @@ __device__ __forceinline__ void rows_block_sum2(float& a, float& b, float* slots
 // explicit S x.  xs /
 // gam are [T][VSTR] block vectors in shared memory; x is read from and
 // written back to xs.  Returns the iteration count.
+template <int BUF>
 __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float* th, float* bb, float* xs,
                                            const float* gam, int T, int max_iter, float eps, float* slots) {
   constexpr int VS = RowsGeo::VSTR;
@@ -354,7 +361,7 @@ __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float*
   r[0] = (act ? gam[t * VS + q] : 0.f) - w[0];
   r[1] = (act ? gam[t * VS + q + 8] : 0.f) - w[1];
   float fw[2];
-  rows_prec(u, fw, r, o, bt, q);  // its barrier ends every read of x in the buffer
+  rows_prec<BUF>(u, fw, r, o, bt, q);  // its barrier ends every read of x in the buffer
   prow[q] = u[0];
   prow[q + 8] = u[1];
   __syncthreads();
@@ -381,7 +388,7 @@ __device__ __forceinline__ int rows_pcg_cg(const RowOpsSave& saved, const float*
     x[1] = fmaf(alpha, p[1], x[1]);
     r[0] = fmaf(-alpha, sv[0], r[0]);
     r[1] = fmaf(-alpha, sv[1], r[1]);
-    rows_prec(u, fw, r, o, bt, q);  // its barrier ends every read of the previous u
+    rows_prec<BUF>(u, fw, r, o, bt, q);  // its barrier ends every read of the previous u
     prow[q] = u[0];
     prow[q + 8] = u[1];
     __syncthreads();
@@ -746,7 +753,8 @@ __device__ __forceinline__ QPView<float> rows_qp_view(float* sm, const RowsSmem&
 // Register budget: the operator rows (96 registers) are live inside the PCG
 // loop only; state that lives across the loop is kept in shared memory (arena
 // offsets) or re-read from the kernel parameters.
-__global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(const AdmmParams<float> P) {
+template <int TM>
+__global__ void __launch_bounds__(RowsGeo::TPB * TM, 1) admm_rows_kernel(const AdmmParams<float> P) {
   using R = float;
   constexpr int NB = 16;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -758,7 +766,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
   TMPC_PROF_INIT
 #define TMPC_RS(f) (sm + Ls.f)
   if (threadIdx.x == 0) {
-    Ls = RowsSmem(P.T, P.n, P.nx, P.n0, P.m);
+    Ls = RowsSmem(P.T, P.n, P.nx, P.n0, P.m, rows_buf(TM));
     flag = 0;
   }
   __syncthreads();
@@ -825,7 +833,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
       __syncthreads();
     }
     TMPC_PROF(6);
-    rows_pcg_cg(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
+    rows_pcg_cg<rows_buf(TM)>(ops, TMPC_RS(th), TMPC_RS(bb), TMPC_RS(x), TMPC_RS(gam), P.T, P.pcg_max_iter, P.pcg_eps,
                 TMPC_RS(red) + kRedSlots);
     pending = true;
     TMPC_PROF(7);
@@ -907,7 +915,7 @@ __global__ void __launch_bounds__(RowsGeo::MAX_THREADS, 1) admm_rows_kernel(cons
 }
 
 inline size_t admm_rows_smem_bytes(int T, int n, int nx, int n0, int m) {
-  return RowsSmem(T, n, nx, n0, m).nelem * sizeof(float);
+  return RowsSmem(T, n, nx, n0, m, rows_buf(rows_cap(T))).nelem * sizeof(float);
 }
 
 // True when the register-resident kernel handles these dimensions.
