@@ -1,6 +1,6 @@
 // Fused ADMM solve with register-resident operators: stage blocks of width 16
-// (n <= 16), fp32, horizons up to T = 52 (the quadrotor configuration has
-// n = 16, T = 51).
+// (n <= 16), fp32, horizons up to T = 64 (the quadrotor configuration has
+// n = 16, T = 51; the Clohessy-Wiltshire one n = 9, T = 61).
 //
 // Same algorithm and iteration order as admm_fused_kernel (admm_kernel.cuh);
 // only the linear-system layer differs.  Eight threads own one stage block t,

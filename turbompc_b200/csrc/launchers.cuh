@@ -26,7 +26,7 @@ template <int NB, typename R>
 int launch_pcg_packed(const TmpcDims* d, const R* o, const R* rhs, const R* x0, R* xo, uint32_t* it, R eps,
                       int max_iter, cudaStream_t st);
 
-// Register-resident kernel for 8 < n <= 16, T <= 52, fp32 (admm_rows.cu).
+// Register-resident kernel for 8 < n <= 16, T <= 64, fp32 (admm_rows.cu).
 bool admm_rows_ok(int T, int n, int nx, int n0, int m);
 int launch_admm_rows(const AdmmParams<float>& P, cudaStream_t st);
 
