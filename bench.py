@@ -1,4 +1,4 @@
-"""Benchmark: MPC solves/sec, quadrotor N=50, batch 65536.
+"""Benchmark: MPC solves/sec, quadrotor N=50, batch 65536 (benchmark configuration 3).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 

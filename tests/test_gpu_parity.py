@@ -96,7 +96,7 @@ FIXED = dict(max_iter=50, pcg_max_iter=20, check_every=0, adapt_rho_every=0, eps
 
 @pytest.mark.parametrize("prec", ["f64", "f32"])
 def test_admm_config1_double_integrator(prec):
-    """nx=4, nu=2, N=20, batch 64, 1 x 50 ADMM x 20 PCG."""
+    """Benchmark configuration 1: nx=4, nu=2, N=20, batch 64, 1 x 50 ADMM x 20 PCG."""
     b = synthetic.double_integrator(batch=64, N=20)
     out, iters, status, so, io, tol = _run_admm(b, prec, FIXED)
     assert (_np(status) == 0).all()

@@ -1,4 +1,4 @@
-"""Whole SQP solves of BASELINE configs 4 (quadrotor with spherical obstacles,
+"""Whole SQP solves of benchmark configurations 4 (quadrotor with spherical obstacles,
 warm-started re-solve) and 5 (Clohessy-Wiltshire with a learned MLP stage
 cost, forward + VJP) on the GPU, against the same SQP loop whose ADMM solves
 run in the NumPy oracle (fp64, fixed SQP/ADMM/PCG counts; tolerance 1e-6

@@ -1,4 +1,4 @@
-"""12-state rigid-body quadrotor with four rotor thrusts.
+"""12-state rigid-body quadrotor with four rotor thrusts (benchmark configuration 3).
 
 State  x = [p (3, world), Euler angles (roll phi, pitch theta, yaw psi),
             v (3, world-frame velocity), omega (3, body rates)]

@@ -1,4 +1,4 @@
-"""Clohessy-Wiltshire relative motion.
+"""Clohessy-Wiltshire relative motion (benchmark configuration 5).
 
 State [x, y, z, vx, vy, vz] in the Hill frame, control = acceleration (3,).
     x_dd = 3 n^2 x + 2 n y_d + ux ;  y_d d = -2 n x_d + uy ;  z_dd = -n^2 z + uz

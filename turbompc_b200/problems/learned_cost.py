@@ -1,4 +1,4 @@
-"""differentiable MPC with a learned stage cost on the
+"""Benchmark configuration 5: differentiable MPC with a learned stage cost on the
 Clohessy-Wiltshire relative-motion model.
 
 Stage cost (every stage t, z_t = [x_t, u_t]):

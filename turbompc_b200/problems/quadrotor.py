@@ -1,7 +1,7 @@
-"""BASELINE.json config 3 (and the config-4 obstacle variant): batched
+"""Benchmark configuration 3 (and the config-4 obstacle variant): batched
 quadrotor tracking MPC with seeded synthetic initial states and set-points.
 
-Choices the configuration leaves open (recorded here and in DESIGN.md):
+Choices the configuration leaves open (recorded here):
 tracking weights w_x = [10]*3 (position) + [1]*3 (angles) + [1]*3 (velocity)
 + [0.1]*3 (rates); terminal extra weight 10 w_x; thrust weight 0.1 around
 hover thrust m g / 4 (penalize_control_reference); no rate penalty; thrust

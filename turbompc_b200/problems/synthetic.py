@@ -1,4 +1,4 @@
-"""Seeded synthetic QPs for the BASELINE.json configurations that are linear.
+"""Seeded synthetic QPs for the benchmark configurations that are linear.
 
 The QPs are what TurboMPC's OptimalControlProblem linearisation
 (turbompc/problems/optimal_control_problem.py:1068-1332) produces for linear
