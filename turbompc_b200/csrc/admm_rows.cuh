@@ -316,14 +316,22 @@ __device__ __forceinline__ void rows_block_sum2(float& a, float& b, float* slots
     slots[16 + (threadIdx.x >> 5)] = b;
   }
   __syncthreads();
-  float sa = slots[threadIdx.x & 15], sb = slots[16 + (threadIdx.x & 15)];
+  // Every thread reads all 16 slots of each sum (broadcast 128-bit loads) and
+  // adds them in the same fixed tree order: deterministic and identical in
+  // all threads, without the shuffle round trips on the iteration's chain.
+  const float4* sl = reinterpret_cast<const float4*>(slots);
+  float4 v[8];
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) {
-    sa += __shfl_xor_sync(0xffffffffu, sa, o);
-    sb += __shfl_xor_sync(0xffffffffu, sb, o);
-  }
-  a = sa;
-  b = sb;
+  for (int c = 0; c < 8; ++c) v[c] = sl[c];
+  auto tree16 = [](const float4* w) {
+    const float q0 = (w[0].x + w[0].y) + (w[0].z + w[0].w);
+    const float q1 = (w[1].x + w[1].y) + (w[1].z + w[1].w);
+    const float q2 = (w[2].x + w[2].y) + (w[2].z + w[2].w);
+    const float q3 = (w[3].x + w[3].y) + (w[3].z + w[3].w);
+    return (q0 + q1) + (q2 + q3);
+  };
+  a = tree16(v);
+  b = tree16(v + 4);
 }
 
 // PCG in the single-reduction (Chronopoulos-Gear) arrangement: the same
