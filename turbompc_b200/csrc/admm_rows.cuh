@@ -270,20 +270,6 @@ __device__ __forceinline__ void rows_prec(float (&z)[2], float (&fw)[2], const f
   z[1] = v1 - w1;
 }
 
-// Deterministic block sum: warp sums into 16 slots (unused slots stay zero),
-// then lane i of every warp reads slot i & 15 and the warp adds them with the
-// same shuffle tree, so every thread gets the same value.  Each lane reads 4
-// bytes instead of the 64-byte slot table.
-__device__ __forceinline__ float rows_block_sum(float v, float* slots) {
-  v = warp_sum(v);
-  if ((threadIdx.x & 31) == 0) slots[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float s = slots[threadIdx.x & 15];
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  return s;
-}
-
 // The operator rows of a thread are written by rows_build (a call that
 // receives the area's address, so the area lives in per-thread local memory,
 // L1/L2 backed) and loaded at the start of every PCG solve with 128-bit
@@ -306,8 +292,8 @@ struct __align__(16) RowOpsSave {
   }
 };
 
-// Two block sums with one barrier (same deterministic order as rows_block_sum);
-// slots holds 2 x 16 entries.
+// Two deterministic block sums with one barrier: each warp's sums go to 16
+// slots per sum (unused slots stay zero); slots holds 2 x 16 entries.
 __device__ __forceinline__ void rows_block_sum2(float& a, float& b, float* slots) {
   a = warp_sum(a);
   b = warp_sum(b);
