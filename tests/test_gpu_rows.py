@@ -58,7 +58,9 @@ def test_rows_kernel_matches_oracle(nx, nu, N, m):
 
 
 @pytest.mark.parametrize("nx,nu,N,m", [(6, 3, 60, 3),    # T = 61, n = 9: the config-5 shape
-                                       (10, 2, 58, 2)])  # T = 59, n = 12
+                                       (10, 2, 58, 2),   # T = 59, n = 12
+                                       (10, 2, 52, 2),   # T = 53: the first horizon of this instance
+                                       (6, 3, 63, 3)])   # T = 64: the largest
 def test_rows_kernel_64_stage_instance(nx, nu, N, m):
     """Horizons with 52 < T <= 64 run the 64-stage instance (512 threads).
     It must match the oracle, and it must be the kernel that ran: its
