@@ -85,7 +85,7 @@ typedef struct TmpcAdmmState {
 #define TMPC_LINSYS_PCG 0    /* preconditioned CG on the Schur system (admm_fused_pcg) */
 #define TMPC_LINSYS_DIRECT 1 /* block-tridiagonal Cholesky (replaces admm_fused_cudss) */
 /* PCG as TMPC_LINSYS_PCG, but always on the shared-memory packed-operator kernel
- * (TMPC_LINSYS_PCG picks the register-resident kernel for fp32, 8 < n <= 16, T <= 52). */
+ * (TMPC_LINSYS_PCG picks the register-resident kernel for fp32, 8 < n <= 16, T <= 64). */
 #define TMPC_LINSYS_PCG_PACKED 2
 
 /* Mirrors ADMMConfig (turbompc/solvers/admm/csrc/admm_fused.cuh:6-22). */
@@ -110,6 +110,16 @@ typedef struct TmpcAdmmConfig {
 /* Library version (major*10000 + minor*100 + patch) and error strings. */
 int32_t tmpc_version(void);
 const char* tmpc_error_string(int32_t code);
+
+/* Diagnostics hook, no counterpart in the reference.  Kernels that stage
+ * their operators into shared memory with TMA bulk copies wait for them with
+ * a bounded poll loop; if it runs out, the problem's iters_out is set to
+ * 0xffffffff (a transfer time-out), the copies still in flight are drained,
+ * and the CTA returns without hanging the GPU.  This sets that loop's poll
+ * limit for subsequent launches (default 2^26) and returns the previous one;
+ * a limit of 0 makes every such wait report a time-out, which lets a test
+ * exercise the status path on copies that do complete. */
+uint32_t tmpc_set_transfer_poll_limit(uint32_t polls);
 
 /* ---------------------------------------------------------------------------
  * Schur complement + preconditioner assembly.
@@ -236,7 +246,8 @@ int32_t tmpc_adjoint_kkt_solve_f64(const TmpcDims* dims, const TmpcQP* qp, doubl
  * loading the library holds until process exit.  Batches needing more
  * return TMPC_ERR_SCRATCH_LIMIT without launching.  The first call on a
  * device looks up the buffer's device address (make it before any stream
- * capture).  All calls share the buffer: calls that can overlap on the GPU
+ * capture); the address is kept for the life of the device's primary
+ * context, so no call may follow a cudaDeviceReset of that device.  All calls share the buffer: calls that can overlap on the GPU
  * (different streams, or different host threads, on one device) race and
  * must be serialised by the caller.
  * ------------------------------------------------------------------------- */

@@ -6,7 +6,7 @@
 # oracle/_ref/ (git-ignored) only.
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-REF="${TMPC_REFERENCE_ROOT:-/root/reference}/turbompc/solvers"
+REF="${TMPC_REFERENCE_ROOT:-$(dirname "$HERE")/../reference}/turbompc/solvers"
 OUT="$HERE/_ref"
 if [ ! -d "$REF" ]; then echo "reference tree not found at $REF; skipping"; exit 0; fi
 mkdir -p "$OUT"

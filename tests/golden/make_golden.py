@@ -3,8 +3,9 @@
 reference tree by oracle/build_ref.sh) on seeded inputs.  Needs a GPU and
 oracle/_ref/libtmpc_refcuda.so:
 
-    bash oracle/build_ref.sh && python tests/golden/make_golden.py
+    bash oracle/build_ref.sh && python tests/golden/make_golden.py [case ...]
 
+(no case names: regenerate every fixture).
 S and Phiinv (computed in JAX by the reference before it calls the kernel,
 admm.py:719-724) come from the NumPy restatement; the fixtures therefore pin
 the kernels' ADMM/PCG semantics, and test_golden.py pins compute_S_Phiinv
@@ -85,7 +86,28 @@ CFG = dict(max_iter=50, pcg_max_iter=20, check_every=0, adapt_rho_every=0, eps_a
            sigma=1e-6, rho_f_factor=1000.0, alpha=1.6, adaptive_rho_tolerance=5.0, rho_min=1e-6, rho_max=1e6)
 
 
+def _problem_qp(kind, batch):
+    """First-SQP-iteration QP blocks (float64 NumPy, reference layout) of the
+    benchmark problems: the config-3 quadrotor (n = 16, T = 51) or the config-5
+    Clohessy-Wiltshire problem with the learned stage cost (n = 9, T = 61)."""
+    from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    from turbompc_b200.problems.quadrotor import make_quadrotor_problem
+    from turbompc_b200.solver import TurboMPCSolver
+
+    if kind == "quadrotor":
+        ocp, p = make_quadrotor_problem(batch, N=50, seed=11, dtype=torch.float64, device="cpu")
+    else:
+        # thrust box tightened to |u| <= 0.01 so that it is active (non-zero y_g)
+        ocp, p = make_learned_cost_problem(batch, N=60, seed=12, dtype=torch.float64, device="cpu", u_max=0.01)
+    s = TurboMPCSolver(ocp, {"num_sqp_iteration_max": 1})
+    g = s.initial_guess(p)
+    t = {k: v.numpy() for k, v in s._build_qp_data(g.states, g.controls, p).tensors().items()}
+    return dict(D=t["D"], E=t["E"], q=t["q"], A0=t["A0"], Am=t["A_minus"], Ap=t["A_plus"], c0=t["c0"], c=t["c"],
+                G=t["G"], l=t["l"], u=t["u"])
+
+
 def main():
+    only = set(sys.argv[1:])
     lib = C.CDLL(LIB)
     cases = {
         "admm_config1_f64": (synthetic.double_integrator(batch=8, N=20), np.float64, dict(CFG), None),
@@ -95,8 +117,17 @@ def main():
         "admm_slack_adapt_f64": (synthetic.random_dense(4, 4, 2, 10, 3, seed=3), np.float64,
                                  dict(CFG, max_iter=60, pcg_max_iter=6, check_every=5, adapt_rho_every=10,
                                       eps_abs=1e-3, eps_rel=1e-3, rho_f_factor=100.0), 10.0),
+        # The benchmark shapes in fp32 (30 ADMM x 30 PCG, fixed counts): the
+        # register-resident b200 kernel's 52- and 64-stage instances.
+        "admm_quadrotor16_f32": (lambda: _problem_qp("quadrotor", 16), np.float32,
+                                 dict(CFG, max_iter=30, pcg_max_iter=30), None),
+        "admm_cw9_f32": (lambda: _problem_qp("cw", 16), np.float32, dict(CFG, max_iter=30, pcg_max_iter=30), None),
     }
     for name, (blocks, dt, cfg, slack) in cases.items():
+        if only and name not in only:
+            continue
+        if callable(blocks):
+            blocks = blocks()
         out = run_ref_admm(lib, blocks, dt, cfg, slack=slack)
         np.savez_compressed(os.path.join(HERE, name + ".npz"),
                             **{"in_" + k: np.asarray(v) for k, v in blocks.items()},
@@ -106,6 +137,8 @@ def main():
         print(name, "iters", out["iters_out"][:4])
     # PCG (pcgBlkTridiSingleBlock) on random LTI Schur systems
     for dt in (np.float64, np.float32):
+        if only and ("pcg_lti9_" + ("f64" if dt == np.float64 else "f32")) not in only:
+            continue
         b = synthetic.random_lti(6, 6, 3, 32, seed=32)
         qo = ref.QP(**b)
         S, P = ref.compute_S_Phiinv(qo, np.full(6, 100.0), 1e-6, np.full(6, 0.1))

@@ -12,7 +12,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 def declared_functions():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int32_t|size_t|const char\*)\s+(tmpc_\w+)\s*\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int32_t|uint32_t|size_t|const char\*)\s+(tmpc_\w+)\s*\(", src, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -36,3 +36,10 @@ def test_error_codes_without_gpu():
     assert lib.tmpc_packed_operator_bytes(C.byref(_ffi.TmpcDims(1, 3, 40, 20, 20, 0)), 4) == 0  # n > 32
     d = _ffi.TmpcDims(2, 5, 16, 12, 12, 4)
     assert lib.tmpc_packed_operator_bytes(C.byref(d), 4) > 0
+
+
+def test_transfer_poll_limit_hook_round_trips():
+    lib = _ffi.load()
+    prev = lib.tmpc_set_transfer_poll_limit(1234)
+    assert prev == 1 << 26
+    assert lib.tmpc_set_transfer_poll_limit(prev) == 1234

@@ -1,5 +1,5 @@
 """GPU parity of the register-resident fused ADMM kernel (fp32, 8 < n <= 16,
-T <= 52; chosen automatically for TMPC_LINSYS_PCG) against the NumPy oracle,
+T <= 64; chosen automatically for TMPC_LINSYS_PCG) against the NumPy oracle,
 and against the shared-memory packed kernel (TMPC_LINSYS_PCG_PACKED).
 Tolerance: 1e-3 relative (||a-b||_inf / ||b||_inf), the fp32 bar."""
 import numpy as np

@@ -21,9 +21,18 @@ def test_shard_range_covers_batch_exactly(nb, world):
 def test_shard_params_slices_batched_only():
     p = {"initial_state": torch.arange(10.0)[:, None].repeat(1, 3), "w": torch.ones(3), "horizon": 5,
          "dyn": {"A": torch.zeros(10, 2, 2), "c": torch.zeros(2, 2)}}
-    s = shard_params(p, 10, 3, 7)
+    s = shard_params(p, 10, 3, 7, batched={"initial_state", "dyn.A"})
     assert s["initial_state"].shape == (4, 3) and s["initial_state"][0, 0] == 3
     assert s["w"].shape == (3,) and s["dyn"]["A"].shape == (4, 2, 2) and s["dyn"]["c"].shape == (2, 2)
+
+
+def test_shard_params_leaves_shared_tensors_whose_size_matches_the_batch():
+    # a weight matrix with nb rows is shared, not a batch axis
+    p = {"initial_state": torch.zeros(6, 6), "mlp_W1": torch.ones(6, 9),
+         "dynamics_state_dot_params": {"A": torch.eye(6)}}
+    s = shard_params(p, 6, 2, 4)
+    assert s["initial_state"].shape == (2, 6)
+    assert s["mlp_W1"].shape == (6, 9) and s["dynamics_state_dot_params"]["A"].shape == (6, 6)
 
 
 def _worker(rank, world, port, nb, q):

@@ -52,6 +52,25 @@ def test_fixed_scratch_matches_workspace_entry_point_twice():
             assert rel_err(g.cpu().numpy(), w.cpu().numpy()) < 1e-6
 
 
+def test_fixed_scratch_direct_linsys_matches_workspace_entry_point_twice():
+    # The direct (block-Cholesky) solve keeps its whole factor in the scratch
+    # buffer; compared with the same solve given a caller workspace.
+    b = dense_blocks(16, 20, 6, 8, 6, seed=7)
+    qd = synthetic.to_qpdata(b, dtype=torch.float64, device="cuda")
+    cfg = ops.AdmmConfig(**CFG, linsys=_ffi.LINSYS_DIRECT)
+    assert ops.admm_workspace_bytes(qd, cfg) > 0
+    s0 = ops.admm_initial_state(qd, 0.1)
+    want, want_it, _ = ops.admm_solve(qd, s0, cfg)
+    for _ in range(2):
+        rc, got, it, st = _call_fixed(qd, s0, cfg)
+        torch.cuda.synchronize()
+        assert rc == 0, _ffi.load().tmpc_error_string(rc)
+        assert int(st.abs().sum()) == 0
+        assert (it.cpu().numpy() == want_it.cpu().numpy()).all()
+        for g, w in zip(got, want):
+            assert rel_err(g.cpu().numpy(), w.cpu().numpy()) < 1e-6
+
+
 def test_fixed_scratch_rejects_batches_beyond_its_buffer():
     b = dense_blocks(400, 20, 6, 8, 6, seed=6)  # ~400 x 207 KB of operators > 64 MiB
     qd = synthetic.to_qpdata(b, dtype=torch.float64, device="cuda")

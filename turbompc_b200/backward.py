@@ -14,6 +14,9 @@ Forward: the SQP solve.  Backward (turbompc_solver.py:1052-1093):
      with y_eq* / y_ineq* the forward multipliers (y_ineq* = -(lower - upper) y_g),
      g the equality constraints and h = lower (g - l) + upper (u - g) the active
      inequalities, evaluated by PyTorch autograd at the solution.
+With soft (slack) constraints the active rows are folded into the adjoint QP
+(turbompc_solver.py:587-605) and their multipliers, and the cotangent of
+slack_penalization_weight, are recovered after the solve (:620-640).
 theta ranges over the tensors in ``weights`` (and ``initial_state``) that
 require grad; the initial-state cotangent equals the x0-row multipliers.
 """
@@ -65,8 +68,11 @@ def _detach_params(params):
     return out
 
 
-def backward_qp(solver, sol, params, dl_dstates, dl_dcontrols) -> QPData:
-    """turbompc_solver.py:544-618 (hard inequalities)."""
+def backward_qp(solver, sol, params, dl_dstates, dl_dcontrols, dl_dslack=None):
+    """turbompc_solver.py:544-618.  Returns (the QP the adjoint KKT solve
+    takes, G_active = sign * G).  With soft (slack) constraints the active
+    rows leave the KKT system: D += gamma G_act^T G_act and
+    q = -(dL/dz - G_act^T dL/dslack) (turbompc_solver.py:587-605)."""
     prog = solver.program
     kkt = sol.kkt_state
     qp = solver._build_qp_data(kkt.states, kkt.controls, params)
@@ -79,12 +85,23 @@ def backward_qp(solver, sol, params, dl_dstates, dl_dcontrols) -> QPData:
                                                            active * sol.admm_state.y_g)
     sign = kkt.ineq_active_lower_idx.to(D.dtype) - kkt.ineq_active_upper_idx.to(D.dtype)
     G = (qp.ineq.G * sign[..., None]).contiguous()
-    q = -torch.cat([dl_dstates, dl_dcontrols], -1).to(D.dtype).contiguous()
-    return QPData(QPCostBlocks(D.contiguous(), qp.cost.E, q),
-                  QPEqualityBlocks(qp.eq.A0, qp.eq.A_minus, qp.eq.A_plus, torch.zeros_like(qp.eq.c0),
-                                   torch.zeros_like(qp.eq.c)),
+    dl = torch.cat([dl_dstates, dl_dcontrols], -1).to(D.dtype)
+    eq = QPEqualityBlocks(qp.eq.A0, qp.eq.A_minus, qp.eq.A_plus, torch.zeros_like(qp.eq.c0),
+                          torch.zeros_like(qp.eq.c))
+    if qp.ineq.use_slack_variables and qp.m > 0:
+        gamma = qp.ineq.slack_penalization_weight.to(D.dtype)
+        if dl_dslack is None:
+            dl_dslack = torch.zeros_like(sol.slack)
+        D = D + gamma[:, None, None, None] * torch.einsum("btki,btkj->btij", G, G)
+        q = -(dl - torch.einsum("btki,btk->bti", G, dl_dslack.to(D.dtype)))
+        Nb, T, n = q.shape
+        empty = torch.zeros(Nb, T, 0, dtype=D.dtype, device=D.device)
+        ineq = QPInequalityBlocks(torch.zeros(Nb, T, 0, n, dtype=D.dtype, device=D.device), empty, empty.clone(),
+                                  qp.ineq.slack_penalization_weight, False)
+        return QPData(QPCostBlocks(D.contiguous(), qp.cost.E, q.contiguous()), eq, ineq), G
+    return QPData(QPCostBlocks(D.contiguous(), qp.cost.E, (-dl).contiguous()), eq,
                   QPInequalityBlocks(G, torch.zeros_like(qp.ineq.l), torch.zeros_like(qp.ineq.u),
-                                     qp.ineq.slack_penalization_weight, False))
+                                     qp.ineq.slack_penalization_weight, False)), G
 
 
 class _SolveFn(torch.autograd.Function):
@@ -98,27 +115,39 @@ class _SolveFn(torch.autograd.Function):
     def backward(ctx, g_states, g_controls, g_slack):
         solver, sol, params, paths = ctx.solver, ctx.sol, ctx.params, ctx.paths
         prog = solver.program
-        if prog.use_slack_variables:
-            raise NotImplementedError("gradients through soft (slack) constraints are not on the b200 path yet")
         kkt = sol.kkt_state
         dt = sol.states.dtype
         if g_states is None:
             g_states = torch.zeros_like(sol.states)
         if g_controls is None:
             g_controls = torch.zeros_like(sol.controls)
+        m = sol.slack.shape[-1]
+        soft = prog.use_slack_variables and m > 0
+        if g_slack is None:
+            g_slack = torch.zeros_like(sol.slack)
         with torch.no_grad():
-            bq = backward_qp(solver, sol, params, g_states.to(dt), g_controls.to(dt))
+            bq, G_act = backward_qp(solver, sol, params, g_states.to(dt), g_controls.to(dt), g_slack.to(dt))
             dz, mult, status = ops.adjoint_kkt_solve(bq)
         nx = prog.num_state_variables
-        Nb, T, m = sol.states.shape[0], sol.states.shape[1], bq.m
+        Nb, T = sol.states.shape[0], sol.states.shape[1]
         n_eq = bq.n0 + (T - 1) * nx
         y_eq_lin = mult[:, :n_eq]
-        y_ineq_lin = mult[:, n_eq:].reshape(Nb, T, m)
         st = sol.admm_state
-        y_eq_star = torch.cat([st.y_f_0, st.y_f_dyn.reshape(Nb, -1)], 1)
-        sign = kkt.ineq_active_lower_idx.to(dt) - kkt.ineq_active_upper_idx.to(dt)
-        y_ineq_star = -sign * st.y_g
         lo_m, up_m = kkt.ineq_active_lower_idx.to(dt), kkt.ineq_active_upper_idx.to(dt)
+        sign = lo_m - up_m
+        dL_dgamma = None
+        if soft:
+            # turbompc_solver.py:620-640: the active-row multipliers and the
+            # slack-weight cotangent from the adjoint step.
+            act = torch.maximum(lo_m, up_m)
+            g_dx = torch.einsum("btki,bti->btk", G_act, dz)
+            gamma = sol_gamma(solver, params, Nb, dt, dz.device)
+            y_ineq_lin = g_slack.to(dt) * act + gamma[:, None, None] * g_dx
+            dL_dgamma = (sign * st.xi_g * act * g_dx).sum((-1, -2))
+        else:
+            y_ineq_lin = mult[:, n_eq:].reshape(Nb, T, m)
+        y_eq_star = torch.cat([st.y_f_0, st.y_f_dyn.reshape(Nb, -1)], 1)
+        y_ineq_star = -sign * st.y_g
 
         with torch.enable_grad():
             leaves = [torch.nn.Parameter(v.detach().clone()) for v in ctx.saved_leaf_values]
@@ -142,7 +171,17 @@ class _SolveFn(torch.autograd.Function):
                 phi = phi + (h_fn(xs, us) * y_ineq_lin).sum()
             grads = torch.autograd.grad(phi, leaves, allow_unused=True)
         out = [None if g is None else -g for g in grads]
+        for i, path in enumerate(paths):
+            if path == ("slack_penalization_weight",) and dL_dgamma is not None:
+                leaf = ctx.saved_leaf_values[i]
+                out[i] = (dL_dgamma.sum() if leaf.numel() == 1 else dL_dgamma).reshape(leaf.shape).to(leaf.dtype)
         return (None, None, None, None, *out)
+
+
+def sol_gamma(solver, params, Nb, dtype, device):
+    """The slack penalty weight per problem (Nb,), as the QP carries it."""
+    sw = params.get("slack_penalization_weight", 0.0)
+    return torch.as_tensor(sw, dtype=dtype, device=device).expand(Nb)
 
 
 def make_differentiable_solve(solver):

@@ -12,7 +12,10 @@
 // library holds its kTmpcFixedScratchBytes until the process exits.  In host
 // code its name is only a host-side stand-in, never a device address, so the
 // address is looked up with cudaGetSymbolAddress once per device (with that
-// device current) on the first call made on that device, and cached.
+// device current) on the first call made on that device, and cached.  The
+// cached address belongs to the device's primary context: after
+// cudaDeviceReset (or anything else that destroys that context) it is stale,
+// and the process must not call this entry point on that device again.
 #include <mutex>
 
 #include "launchers.cuh"

@@ -1,6 +1,7 @@
 // Library-level C ABI entry points (version, error strings) and host helpers.
 #include <cuda_runtime.h>
 
+#include "tma.cuh"
 #include "tmpc_common.cuh"
 
 namespace tmpc {
@@ -24,6 +25,8 @@ int max_dyn_smem() {
 extern "C" {
 
 int32_t tmpc_version(void) { return 100; }
+
+uint32_t tmpc_set_transfer_poll_limit(uint32_t polls) { return tmpc::transfer_poll_limit().exchange(polls); }
 
 const char* tmpc_error_string(int32_t code) {
   switch (code) {

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(max_threads_for(NB)) pcg_packed_kernel(const R
                                                                  const R* __restrict__ rhs,
                                                                  const R* __restrict__ x0, R* x_out,
                                                                  uint32_t* iters_out, R eps, int max_iter, int Nb,
-                                                                 int T, int n) {
+                                                                 int T, int n, uint32_t max_polls) {
   using Gm = Geo<NB, R>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   R* sm = reinterpret_cast<R*>(smem_raw);
@@ -97,7 +97,12 @@ __global__ void __launch_bounds__(max_threads_for(NB)) pcg_packed_kernel(const R
   }
   if constexpr (OPS_SMEM) {
     if (threadIdx.x == 0) {
-      if (!mbar_wait_bounded(&bar, 0, 1u << 26)) tma_ok = 0;
+      if (!mbar_wait_bounded(&bar, 0, max_polls)) {
+        tma_ok = 0;
+        // The CTA must not retire with bulk copies into its shared memory
+        // still in flight: drain them (again with a bounded wait) first.
+        mbar_wait_bounded(&bar, 0, kTransferDrainPolls);
+      }
     }
   }
   __syncthreads();
@@ -145,13 +150,14 @@ int launch_pcg_packed(const TmpcDims* d, const R* o, const R* rhs, const R* x0, 
     auto k = pcg_packed_kernel<NB, R, true>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(vec_bytes + op_bytes));
     if (e != cudaSuccess) return (int)e;
-    k<<<d->Nb, th, vec_bytes + op_bytes, st>>>(o, rhs, x0, xo, it, eps, max_iter, d->Nb, d->T, d->n);
+    k<<<d->Nb, th, vec_bytes + op_bytes, st>>>(o, rhs, x0, xo, it, eps, max_iter, d->Nb, d->T, d->n,
+                                                transfer_poll_limit().load());
   } else {
     if ((long)vec_bytes > smax) return (int)TMPC_ERR_SMEM;
     auto k = pcg_packed_kernel<NB, R, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vec_bytes);
     if (e != cudaSuccess) return (int)e;
-    k<<<d->Nb, th, vec_bytes, st>>>(o, rhs, x0, xo, it, eps, max_iter, d->Nb, d->T, d->n);
+    k<<<d->Nb, th, vec_bytes, st>>>(o, rhs, x0, xo, it, eps, max_iter, d->Nb, d->T, d->n, 0u);
   }
   return (int)cudaPeekAtLastError();
 }

@@ -6,7 +6,23 @@
 
 #include <stdint.h>
 
+#include <atomic>
+
 namespace tmpc {
+
+// Polls a kernel spends waiting for its operators' bulk copies before it
+// reports a transfer time-out (far longer than any copy takes), and the polls
+// it then spends draining the copies still in flight before it returns.
+constexpr uint32_t kTransferPolls = 1u << 26;
+constexpr uint32_t kTransferDrainPolls = 1u << 26;
+
+// Host-side poll limit passed to the kernels; tmpc_set_transfer_poll_limit
+// changes it (a diagnostics hook: a limit of 0 makes every wait report a
+// time-out after its copies have landed, which exercises the status path).
+inline std::atomic<uint32_t>& transfer_poll_limit() {
+  static std::atomic<uint32_t> v{kTransferPolls};
+  return v;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -7,7 +7,7 @@ on GPUs; gloo in CPU tests).  There is no collective on the solve path.
 """
 from __future__ import annotations
 
-from typing import Any, Dict, Sequence, Tuple
+from typing import Any, Dict, Iterable, Sequence, Tuple
 
 import torch
 
@@ -21,26 +21,44 @@ def shard_range(nb: int, world: int, rank: int) -> Tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
-def shard_params(params: Dict[str, Any], nb: int, lo: int, hi: int) -> Dict[str, Any]:
-    """Slice every tensor whose leading dimension is the batch (nb); others are shared."""
-    out = {}
-    for k, v in params.items():
-        if isinstance(v, dict):
-            out[k] = shard_params(v, nb, lo, hi)
-        elif isinstance(v, torch.Tensor) and v.dim() > 0 and v.shape[0] == nb:
-            out[k] = v[lo:hi]
-        else:
-            out[k] = v
-    return out
+# Problem parameters that carry one entry per problem (leading batch axis)
+# in the batched API; every other entry is shared by the whole batch.
+BATCHED_KEYS = frozenset({
+    "initial_state", "initial_guess_final_state", "initial_control", "reference_state_trajectory",
+    "reference_control_trajectory", "obstacles_centers", "obstacles_radii", "slack_penalization_weight",
+})
 
 
-def gather_batch(local: torch.Tensor, nb: int, group=None, dst: int = 0):
+def shard_params(params: Dict[str, Any], nb: int, lo: int, hi: int,
+                 batched: Iterable[str] = BATCHED_KEYS) -> Dict[str, Any]:
+    """Slice the per-problem entries named in ``batched`` (top-level keys, or
+    'outer.inner' for entries of nested dicts such as dynamics parameters)
+    whose leading dimension is the batch size nb; everything else (weights,
+    dynamics matrices, scalars) is shared and passed through unsliced, even
+    when a dimension of it happens to equal nb."""
+    batched = frozenset(batched)
+
+    def walk(d, prefix):
+        out = {}
+        for k, v in d.items():
+            name = prefix + k
+            if isinstance(v, dict):
+                out[k] = walk(v, name + ".")
+            elif (name in batched and isinstance(v, torch.Tensor) and v.dim() > 0 and v.shape[0] == nb):
+                out[k] = v[lo:hi]
+            else:
+                out[k] = v
+        return out
+
+    return walk(params, "")
+
+
+def gather_batch(local: torch.Tensor, nb: int, group=None):
     """Gather per-rank slices (leading dim = the rank's shard) into the full
     (nb, ...) tensor on every rank (all_gather of equally padded slices)."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
     sizes = [shard_range(nb, world, r) for r in range(world)]
     cap = max(h - l for l, h in sizes)
     pad = torch.zeros((cap,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
@@ -49,7 +67,6 @@ def gather_batch(local: torch.Tensor, nb: int, group=None, dst: int = 0):
     dist.all_gather_into_tensor(out, pad, group=group) if hasattr(dist, "all_gather_into_tensor") and \
         local.is_cuda else _gather_list(out, pad, world, group)
     parts = [out[r * cap: r * cap + (h - l)] for r, (l, h) in enumerate(sizes)]
-    del rank, dst
     return torch.cat(parts, 0)
 
 

@@ -113,6 +113,11 @@ class SolverStats(NamedTuple):
     eq_constraints_violations: torch.Tensor
     ineq_constraints_violations: torch.Tensor
     convergence_errors: torch.Tensor
+    # Per-problem OR of the fused kernel's status words over the SQP
+    # iterations (TMPC_STATUS_SINGULAR_BLOCK = 1, TMPC_STATUS_NONFINITE = 2;
+    # 0 = clean).  The reference reports no such field (its top-level status
+    # is always STATUS_SUCCESS, turbompc_solver.py:1752); it is an addition.
+    kernel_status: Optional[torch.Tensor] = None  # (Nb,) int32
 
 
 class TurboMPCSolution(NamedTuple):
@@ -352,10 +357,12 @@ class TurboMPCSolver:
         nx = self._program.num_state_variables
         kkt = None
         sw = qp.ineq.slack_penalization_weight
+        kstatus = torch.zeros(Nb, dtype=torch.int32, device=dev)
         for k in range(max_iter):
             if k > 0 and tol > 0 and not bool(active.any()):
                 break
             st_new, iters, status = ops.admm_solve(qp, st, cfg, slack_weight=sw, workspace=self._workspace)
+            kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
             xb = st_new.x_blocks
             s_new, c_new = xb[..., :nx], xb[..., nx:]
             sl_new = st_new.xi_g
@@ -400,4 +407,4 @@ class TurboMPCSolver:
             del a3
         return TurboMPCSolution(states=states, controls=controls, slack=st.xi_g, status=self.STATUS_SUCCESS,
                                 num_iter=it_count, convergence_error=conv, admm_iters=admm_iters, admm_state=st,
-                                solver_stats=SolverStats(admm_iters, eqv, inv, cerr), kkt_state=kkt)
+                                solver_stats=SolverStats(admm_iters, eqv, inv, cerr, kstatus), kkt_state=kkt)
