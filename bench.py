@@ -46,6 +46,46 @@ def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG)
     return admm * (pcg * b_pcg + b_admm) + b_sqp
 
 
+def rows_kernel_flops_per_problem(T, n, nx, m, n0, admm=ADMM, pcg=PCG):
+    """Floating-point operations one problem costs the fused register-resident
+    ADMM kernel in one launch (one SQP iteration), counted from its code at
+    the problem's true block size n (padding excluded):
+      per PCG iteration   six n x n block-row products per stage (Theta^-1 r,
+                          the two off-diagonal blocks of S on w, Theta^-1 u,
+                          the two off-diagonal blocks on z) = 12 T n^2, plus
+                          the two inner products and the x, r, p, s updates;
+      per ADMM iteration  the PCG set-up (S x, one preconditioner application,
+                          one S z: 9 block products = 18 T n^2), gamma
+                          (C^T and G^T products), the constraint products
+                          C x and G x, relaxation and dual updates;
+      per launch          the operator build: Theta (G^T G and A^T A terms),
+                          Theta^-1 (Gauss-Jordan, 2 n^3 per stage), Phi."""
+    N = T - 1
+    f_pcg = 12 * T * n * n + 16 * T * n
+    f_setup = 18 * T * n * n + 8 * T * n
+    f_admm = 8 * N * nx * n + 4 * T * m * n + 4 * n0 * n + 20 * T * n + 12 * T * m + 6 * N * nx
+    f_build = T * (2 * m * n * n + 2 * n ** 3) + 6 * N * nx * n * n + 2 * n0 * n * n
+    return admm * (pcg * f_pcg + f_setup + f_admm) + f_build
+
+
+def fp32_peak_tflops():
+    """FP32 CUDA-core peak of one B200 (148 SMs x 128 FP32 lanes x 2 flop per
+    FMA x the maximum SM clock); MEASURED_PEAKS.json holds no FP32 figure, so
+    this is the nominal number at its measured maximum clock."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f)["sm_max_mhz"])
+    except (OSError, KeyError, ValueError):
+        mhz = 1965.0
+    return 148 * 128 * 2 * mhz * 1e6 / 1e12
+
+
+# Shared-memory pipe share (l1tex data-pipe wavefronts, % of peak) of the
+# fused kernel on this workload, from the ncu capture summarised in
+# profiles/admm_rows_quadrotor_b592_fp32.txt.
+NCU_SMEM_PIPE_SHARE = 0.484
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -109,14 +149,14 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def cpu_baseline(target_s=12.0, seed=0):
+def cpu_baseline(target_s=8.0, seed=0, runs=3):
     """CPU baseline: the C restatement of the reference's ADMM/PCG (oracle/c,
     the reference's own JAX CPU install is unavailable) on all host cores, on
     the QPs of the first SQP iteration of this workload (fp32, 30 ADMM x 30
     PCG), scaled by the 5 SQP iterations of a solve.  Linearisation is not
-    timed on the CPU side, which flatters the CPU.  The sample is sized so the
-    timed run takes about ``target_s`` seconds."""
-    import numpy as np
+    timed on the CPU side, which flatters the CPU.  The sample is sized so one
+    timed run takes about ``target_s`` seconds; the value is the median of
+    ``runs`` timed runs on the same sample."""
     import torch
 
     from oracle import admm_ref as ref
@@ -134,30 +174,40 @@ def cpu_baseline(target_s=12.0, seed=0):
         return ref.QP(D=t["D"], E=t["E"], q=t["q"], A0=t["A0"], Am=t["A_minus"], Ap=t["A_plus"], c0=t["c0"],
                       c=t["c"], G=t["G"], l=t["l"], u=t["u"])
 
-    def timed(k):
-        q = qp_sample(k)
+    def timed(q):
         t0 = time.perf_counter()
         c_oracle.admm_fixed(q, 0.1, ADMM, PCG, threads=threads)
         return time.perf_counter() - t0
 
     k = threads
-    dt = timed(k)
+    dt = timed(qp_sample(k))
     k = int(min(8192, max(k, k * target_s / max(dt, 1e-3))))
-    dt = timed(k)
+    q = qp_sample(k)
+    times = [timed(q) for _ in range(runs)]
+    dt = statistics.median(times)
     return {"value": k / (dt * SQP), "unit": "solves/s", "cores": threads, "kind": "port",
             "sample": f"{k} quadrotor QPs x 1 SQP iteration (30 ADMM x 30 PCG, fp32, C restatement in oracle/c, "
-                      f"{threads} host threads), scaled x{SQP} SQP iterations; {dt:.1f} s"}
+                      f"{threads} host threads), scaled x{SQP} SQP iterations; median of {runs} runs "
+                      f"({', '.join(f'{t:.1f}' for t in times)} s)"}
+
+
+def workload_config(batch, world, shard):
+    """The `config` object of both arms' JSON lines."""
+    return {"workload": f"quadrotor-12 N={N_HORIZON} batch {batch}, {SQP} SQP x {ADMM} ADMM x {PCG} PCG "
+                        "(fixed counts)",
+            "global_batch": batch, "per_gpu_batch": shard, "horizon": N_HORIZON, "parallelism": f"batch-shard x{world}"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_baseline()
+    cb = cpu_baseline(runs=max(3, args.steps))
+    cfg = workload_config(args.batch, 1, args.batch)
+    cfg["l2"] = "CPU run (no GPU); sample in cpu_baseline.sample"
     line = {"metric": METRIC, "value": cb["value"], "unit": "solves/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": BATCH / cb["value"] * 1e3, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": args.batch / cb["value"] * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "quadrotor-12 N=50 batch 65536, 5 SQP x 30 ADMM x 30 PCG"},
-            "impl": "reference", "cpu_baseline": cb,
+            "config": cfg, "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "solves/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -189,7 +239,7 @@ def admm_only(nb, linsys="auto", reps=3, pcg=PCG, admm=ADMM):
                       "us_per_problem": round(1e3 * ms / nb, 3), "status_nonzero": int((st != 0).sum())}))
 
 
-def pcg_sweep(points, reps=5, pcg_iters=PCG):
+def pcg_sweep(points, reps=5, pcg_iters=PCG, emit=None):
     """Config 2 (linear-system kernel sweep): standalone PCG (fixed iterations,
     tol 0) on assembled packed operators and the direct block-Cholesky solve,
     timed with CUDA events and reported against the HBM roofline with the
@@ -201,6 +251,7 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG):
     from turbompc_b200 import _ffi, ops
     from turbompc_b200.problems import synthetic
 
+    emit = emit or (lambda d: print(json.dumps(d), flush=True))
     peak, pk_kind = peaks()
     for (nx, nu, N, batch, dt) in points:
         tdt = torch.float32 if dt == "f32" else torch.float64
@@ -226,8 +277,8 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG):
             try:
                 x, it = solve(opsb, dims, rhs, x0, 0.0, pcg_iters)
             except Exception as exc:  # e.g. the packed kernel's vectors exceed shared memory
-                print(json.dumps({"sweep": "pcg_" + kind, "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
-                                  "unavailable": str(exc)}), flush=True)
+                emit(({"sweep": "pcg_" + kind, "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+                                  "unavailable": str(exc)}))
                 del opsb
                 continue
             torch.cuda.synchronize()
@@ -242,7 +293,7 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG):
                     "pcg_iters": pcg_iters, "iters_ok": bool((it == pcg_iters).all()), "ms": round(ms, 3),
                     "solves_per_s": round(batch / (ms / 1e3), 1), "model_GBps": round(gbs, 1),
                     "frac_of_peak": round(gbs / peak, 3), "peak": peak, "peak_source": pk_kind}
-            print(json.dumps(line), flush=True)
+            emit(line)
             del opsb
         # direct solve on reference-layout S
         S, P, _ = ops.schur_assemble(small, 0.1, 1e-6, 1000.0)
@@ -265,15 +316,15 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG):
         ms_s = e0.elapsed_time(e1) / reps
         b_f = (T * n * 3 * n + (2 * T - 1) * n * n) * w  # read S (reference layout) + write the factor
         b_s = (2 * T - 1) * n * n * w + 2 * T * n * w
-        print(json.dumps({"sweep": "riccati", "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+        emit(({"sweep": "riccati", "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
                           "factor_ms": round(ms_f, 3), "solve_ms": round(ms_s, 3),
                           "factor_model_GBps": round(batch * b_f / (ms_f / 1e3) / 1e9, 1),
                           "solve_model_GBps": round(batch * b_s / (ms_s / 1e3) / 1e9, 1),
-                          "status_nonzero": int((fst != 0).sum())}), flush=True)
+                          "status_nonzero": int((fst != 0).sum())}))
         del Sb, fac
 
 
-def run_config(name, steps=3, warmup=2):
+def run_config(name, steps=3, warmup=2, emit=True):
     """Configs 4 and 5 on one GPU (one JSON line each; the default run above is
     config 3).  obstacles: quadrotor N=40 with 8 spheres per problem, batch
     8192, 10 SQP x 50 ADMM x 30 PCG, each step warm-started from the previous
@@ -350,7 +401,28 @@ def run_config(name, steps=3, warmup=2):
                 "forward_plus_vjp_solves_per_s": batch / (ms_fb / 1e3), "batch": batch, "horizon": 60,
                 "iterations": "3 SQP x 50 ADMM x 30 PCG; VJP w.r.t. x0, MLP W1 b1 w2, A, B", "dtype": "f32",
                 "n_gpus": 1}
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
+
+
+def other_configs():
+    """Configurations 4 and 5 and a short configuration-2 sweep on one GPU,
+    reported inside the headline line (one JSON line per run)."""
+    out = {}
+    for name in ("obstacles", "cw_mlp"):
+        try:
+            out[name] = run_config(name, emit=False)
+        except Exception as exc:  # reported, not fatal
+            out[name] = {"error": repr(exc)}
+    sweep = []
+    try:
+        pcg_sweep([(6, 3, 32, 65536, "f32"), (12, 4, 64, 16384, "f32"), (24, 8, 128, 4096, "f32"),
+                   (24, 8, 128, 2048, "f64")], reps=3, emit=sweep.append)
+    except Exception as exc:
+        sweep.append({"error": repr(exc)})
+    out["lti_sweep"] = sweep
+    return out
 
 
 def main():
@@ -361,6 +433,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="skip the one-GPU runs of configurations 2, 4 and 5 that the default run adds to its line")
     ap.add_argument("--admm-only", type=int, default=0, metavar="NB",
                     help="profiling aid: one fused ADMM launch (30 ADMM x 30 PCG, fp32) on NB quadrotor-shaped "
                          "synthetic QPs, then exit")
@@ -518,10 +592,13 @@ def main():
     if rank == 0:
         qp = solver._build_qp_data(guess.states, guess.controls, params)
         T, n, nx, m, n0 = qp.T, qp.n, qp.nx, qp.m, qp.n0
-        b_launch = algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, 4) * shard
-        achieved = b_launch / (kms / 1e3) / 1e9
         kernel = "admm_rows_kernel" if (T <= 64 and 8 < n <= 16) else "admm_fused_kernel"
-        peak, pk_kind = peaks()
+        flops = rows_kernel_flops_per_problem(T, n, nx, m, n0) * shard
+        achieved = flops / (kms / 1e3) / 1e12
+        fpk = fp32_peak_tflops()
+        hbm, pk_kind = peaks()
+        model_gbs = algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, 4) * shard / (kms / 1e3) / 1e9
+        dram = NCU_DRAM_BYTES_PER_PROBLEM * shard
         # QP data one fused ADMM launch reads (one SQP iteration's D, E, q,
         # A_minus, A_plus, c, G, l, u for this GPU's shard, fp32).
         qp_gb = shard * 4 * (T * n * n * 2 + T * n + 2 * (T - 1) * nx * n + (T - 1) * nx
@@ -532,28 +609,37 @@ def main():
                 cb = cpu_baseline()
             except Exception as exc:  # reported, not fatal
                 cb = {"error": repr(exc)}
+        cfg = workload_config(args.batch, world, shard)
+        cfg["l2"] = (f"inputs > L2 (QP data ~{qp_gb:.1f} GB per SQP iteration)" if qp_gb > 0.126
+                     else f"QP data {qp_gb:.3f} GB per SQP iteration (fits L2)")
         line = {
             "metric": METRIC, "value": value, "unit": "solves/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"quadrotor-12 N={N_HORIZON} batch {args.batch}, 5 SQP x 30 ADMM x 30 PCG "
-                                   "(fixed counts)",
-                       "global_batch": args.batch, "per_gpu_batch": shard, "horizon": N_HORIZON,
-                       "parallelism": f"batch-shard x{world}",
-                       "l2": f"inputs > L2 (QP data ~{qp_gb:.1f} GB per SQP iteration)" if qp_gb > 0.126
-                             else f"QP data {qp_gb:.3f} GB per SQP iteration (fits L2)"},
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
             "e2e": {"value": args.batch / (e2e_ms / 1e3), "unit": "solves/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": NCU_DRAM_BYTES_PER_PROBLEM * shard,
-                         "peak_source": pk_kind, "kernel": kernel, "kernel_ms_per_launch": kms,
-                         "note": "achieved = streaming-model bytes / launch time; the operators stay on chip, so "
-                                 "frac > 1 means the kernel moves far less than the model (traffic = ncu DRAM "
-                                 "bytes per launch, scaled per problem); the kernel is bound on chip"},
+            "roofline": {
+                "bound": "fp32", "achieved": achieved, "peak": fpk, "unit": "TFLOP/s", "frac": achieved / fpk,
+                "peak_source": "nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2 x max SM clock); "
+                               "MEASURED_PEAKS.json has no FP32 figure",
+                "traffic": dram, "kernel": kernel, "kernel_ms_per_launch": kms,
+                "flops_per_problem_launch": flops / shard,
+                "smem_pipe_share": NCU_SMEM_PIPE_SHARE,
+                "dram_frac": dram / (kms / 1e3) / 1e9 / hbm,
+                "model_frac": model_gbs / hbm,
+                "note": "the operators stay on chip (registers and shared memory), so the kernel is bound on "
+                        "chip, not by HBM: frac = its own FP32 flops (counted from the code at the true block "
+                        "size) per launch time over the FP32 peak; smem_pipe_share = shared-memory pipe share "
+                        "from ncu; traffic = measured DRAM bytes per launch (ncu, scaled per problem), dram_frac "
+                        "= that traffic over the launch time as a share of the measured HBM copy peak; "
+                        "model_frac = the streaming model's bytes (S and Phiinv re-read every PCG iteration) "
+                        "per launch time over that peak, > 1 because the model's bytes are never moved"},
             "gpu_launches": len(launch_ms) + n_lin[0],
             "clocks": clk.summary(),
             "cpu_baseline": cb,
         }
+        if world == 1 and not args.headline_only:
+            line["configs"] = other_configs()
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

@@ -32,8 +32,8 @@ def test_transfer_timeout_sets_status_and_context_stays_usable():
         assert lib.tmpc_set_transfer_poll_limit(prev) == 0
     assert (it.cpu().numpy() == 0xFFFFFFFF).all()
     x, it2 = ops.pcg_solve_packed(o, ops.dims_of(qd), rhs, x0, 0.0, 20)
-    assert (it2.cpu().numpy() == 20).all()
     q = ref.QP(**{k: np.asarray(v) for k, v in b.items()})
     S, P = ref.compute_S_Phiinv(q, np.full(8, 10.0), 1e-6, np.full(8, 0.1))
-    xr, _ = ref.pcg(S, P, rhs.cpu().numpy(), x0.cpu().numpy(), 20, 0.0)
+    xr, itr = ref.pcg(S, P, rhs.cpu().numpy(), x0.cpu().numpy(), 20, 0.0)
+    assert (it2.cpu().numpy() == itr).all()  # the 1e-12 floor may stop some problems early
     assert rel_err(x.cpu().numpy(), xr) < 1e-6

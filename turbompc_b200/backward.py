@@ -127,7 +127,14 @@ class _SolveFn(torch.autograd.Function):
             g_slack = torch.zeros_like(sol.slack)
         with torch.no_grad():
             bq, G_act = backward_qp(solver, sol, params, g_states.to(dt), g_controls.to(dt), g_slack.to(dt))
-            dz, mult, status = ops.adjoint_kkt_solve(bq)
+            # The adjoint KKT system is solved in float64 whatever the solve's
+            # precision: its condition number amplifies float32 rounding into
+            # ~1e-3 relative errors in the multipliers (the x0 cotangent among
+            # them), while the float32 forward solution itself is good to
+            # ~1e-4.  One factorisation per problem, so the cost is small.
+            dz, mult, status = ops.adjoint_kkt_solve(bq.map(
+                lambda a: a.to(torch.float64) if a.is_floating_point() else a))
+            dz, mult = dz.to(dt), mult.to(dt)
         nx = prog.num_state_variables
         Nb, T = sol.states.shape[0], sol.states.shape[1]
         n_eq = bq.n0 + (T - 1) * nx
