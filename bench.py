@@ -321,6 +321,42 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG, emit=None):
                           "factor_model_GBps": round(batch * b_f / (ms_f / 1e3) / 1e9, 1),
                           "solve_model_GBps": round(batch * b_s / (ms_s / 1e3) / 1e9, 1),
                           "status_nonzero": int((fst != 0).sum())}))
+        if n <= (16 if dt == "f32" else 12):
+            # the same factor / solve on the batch-interleaved layout (one
+            # problem per thread, coalesced across problems)
+            ops_il = ops.schur_interleave(Sb)
+            rhs_il = ops.interleave(rhs)
+            fil, sil = ops.riccati_factor_il(ops_il, dims)
+            xil = ops.riccati_solve_il(fil, dims, rhs_il)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                ops.riccati_factor_il(ops_il, dims, fil, sil)
+            e1.record()
+            torch.cuda.synchronize()
+            ms_fi = e0.elapsed_time(e1) / reps
+            e0.record()
+            for _ in range(reps):
+                ops.riccati_solve_il(fil, dims, rhs_il, xil)
+            e1.record()
+            torch.cuda.synchronize()
+            ms_si = e0.elapsed_time(e1) / reps
+            eop = T * n * (n + 1) // 2 + N * n * n  # elements per problem of the operator and of the factor
+            bf = 2 * eop * w  # read Theta / Phi, write L / W (W_{t-1} re-read from L2)
+            bs = (2 * eop + 4 * T * n) * w  # factor read in both sweeps; rhs, y write + read, x write
+            xd = ops.deinterleave(xil, (batch, T, n))
+            emit(({"sweep": "riccati_interleaved", "nx": nx, "nu": nu, "N": N, "batch": batch, "dtype": dt,
+                   "factor_ms": round(ms_fi, 3), "solve_ms": round(ms_si, 3),
+                   "factor_GBps": round(batch * bf / (ms_fi / 1e3) / 1e9, 1),
+                   "factor_frac_of_peak": round(batch * bf / (ms_fi / 1e3) / 1e9 / peak, 3),
+                   "solve_GBps": round(batch * bs / (ms_si / 1e3) / 1e9, 1),
+                   "solve_frac_of_peak": round(batch * bs / (ms_si / 1e3) / 1e9 / peak, 3),
+                   "speedup_vs_reference_layout": [round(ms_f / ms_fi, 2), round(ms_s / ms_si, 2)],
+                   "max_rel_diff_vs_reference_layout":
+                       float(((xd - xr).abs().max() / xr.abs().max()).item()),
+                   "status_nonzero": int((sil != 0).sum()),
+                   "bytes": "factor 2 E w (E = T n(n+1)/2 + N n^2 per problem), solve (2 E + 4 T n) w"}))
+            del ops_il, rhs_il, fil, xil, xd
         del Sb, fac
 
 

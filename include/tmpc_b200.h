@@ -323,6 +323,50 @@ int32_t tmpc_linearize_dynamics_f64(const TmpcDims* dims, int32_t model, int32_t
                                     const double* states, const double* controls, const double* params,
                                     int32_t n_params, double* A_minus, double* c, tmpc_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Batch-interleaved layout and the direct solve on it.
+ *
+ * TMPC_LAYOUT_REFERENCE is the problem-major layout every entry point above
+ * takes (what the reference's FFI handlers receive).  TMPC_LAYOUT_INTERLEAVED
+ * groups problems by 32 and stores each group element-major, problem-minor:
+ *     element e of problem b  at  ((b / 32) * E + e) * 32 + b % 32
+ * (E = elements per problem), so the 32 lanes of a warp, one problem each,
+ * read and write every element with one coalesced transaction.  Interleaved
+ * arrays hold tmpc_interleaved_elems(Nb, E) elements (ceil(Nb / 32) * 32
+ * problem slots; the slots past Nb are padding the kernels may write).
+ *
+ * Interleaved operator / factor format, E = tmpc_riccati_il_elems_per_problem:
+ *   T blocks Theta_t (factor: L_t), lower triangle packed row-major
+ *     ((i, j <= i) at t n(n+1)/2 + i(i+1)/2 + j), then
+ *   N blocks Phi_t = S(t+1, t) (factor: W_t = Phi_t L_t^-T), row-major n x n.
+ * Vectors (rhs, x) are [T][n] per problem, interleaved.
+ * The factor and solve replace the cuDSS direct solve `cudss_blktridi_cuda`
+ * (linear_systems_solvers/csrc/cudss_ffi.cc:76-98) like tmpc_riccati_*, one
+ * problem per thread; n <= 16 in fp32, n <= 12 in fp64 (TMPC_ERR_UNSUPPORTED
+ * beyond: use tmpc_riccati_* on the reference layout).
+ * ------------------------------------------------------------------------- */
+#define TMPC_LAYOUT_REFERENCE 0
+#define TMPC_LAYOUT_INTERLEAVED 1
+size_t tmpc_interleaved_elems(int32_t Nb, int64_t elems_per_problem);
+int64_t tmpc_riccati_il_elems_per_problem(const TmpcDims* dims);
+/* [Nb][elems] problem-major <-> interleaved (any per-problem array). */
+int32_t tmpc_interleave_f32(int32_t Nb, int64_t elems, const float* src, float* dst, tmpc_stream_t stream);
+int32_t tmpc_interleave_f64(int32_t Nb, int64_t elems, const double* src, double* dst, tmpc_stream_t stream);
+int32_t tmpc_deinterleave_f32(int32_t Nb, int64_t elems, const float* src, float* dst, tmpc_stream_t stream);
+int32_t tmpc_deinterleave_f64(int32_t Nb, int64_t elems, const double* src, double* dst, tmpc_stream_t stream);
+/* Reference-layout S [Nb, T, n, 3n] -> interleaved operator (Theta, Phi). */
+int32_t tmpc_schur_interleave_f32(const TmpcDims* dims, const float* S, float* ops, tmpc_stream_t stream);
+int32_t tmpc_schur_interleave_f64(const TmpcDims* dims, const double* S, double* ops, tmpc_stream_t stream);
+/* status_out [Nb] (problem-major) as tmpc_riccati_factor_*. */
+int32_t tmpc_riccati_factor_il_f32(const TmpcDims* dims, const float* ops, float* factor, int32_t* status_out,
+                                   tmpc_stream_t stream);
+int32_t tmpc_riccati_factor_il_f64(const TmpcDims* dims, const double* ops, double* factor, int32_t* status_out,
+                                   tmpc_stream_t stream);
+int32_t tmpc_riccati_solve_il_f32(const TmpcDims* dims, const float* factor, const float* rhs, float* x_out,
+                                  tmpc_stream_t stream);
+int32_t tmpc_riccati_solve_il_f64(const TmpcDims* dims, const double* factor, const double* rhs, double* x_out,
+                                  tmpc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

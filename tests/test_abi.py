@@ -12,7 +12,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 def declared_functions():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int32_t|uint32_t|size_t|const char\*)\s+(tmpc_\w+)\s*\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int32_t|uint32_t|int64_t|size_t|const char\*)\s+(tmpc_\w+)\s*\(", src, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -43,3 +43,12 @@ def test_transfer_poll_limit_hook_round_trips():
     prev = lib.tmpc_set_transfer_poll_limit(1234)
     assert prev == 1 << 26
     assert lib.tmpc_set_transfer_poll_limit(prev) == 1234
+
+
+def test_interleaved_sizes_without_gpu():
+    lib = _ffi.load()
+    assert lib.tmpc_interleaved_elems(37, 10) == 64 * 10
+    assert lib.tmpc_interleaved_elems(32, 10) == 32 * 10
+    assert lib.tmpc_interleaved_elems(0, 10) == 0
+    d = _ffi.TmpcDims(5, 4, 3, 2, 0, 0)  # T = 4, n = 3: 4 * 6 + 3 * 9
+    assert lib.tmpc_riccati_il_elems_per_problem(C.byref(d)) == 4 * 6 + 3 * 9

@@ -40,6 +40,8 @@ class TmpcAdmmConfig(C.Structure):
 LINSYS_PCG = 0
 LINSYS_DIRECT = 1
 LINSYS_PCG_PACKED = 2
+LAYOUT_REFERENCE = 0
+LAYOUT_INTERLEAVED = 1
 MODEL_QUADROTOR12 = 1
 MODEL_CLOHESSY_WILTSHIRE = 2
 
@@ -57,9 +59,16 @@ _SIGS = {
                                                       C.c_void_p]),
 }
 _SIGS["tmpc_riccati_factor_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
+_SIGS["tmpc_interleaved_elems"] = (C.c_size_t, [C.c_int32, C.c_int64])
+_SIGS["tmpc_riccati_il_elems_per_problem"] = (C.c_int64, [C.POINTER(TmpcDims)])
 _SIGS["tmpc_stream_operator_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 _SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 for _s in ("f32", "f64"):
+    _SIGS[f"tmpc_interleave_{_s}"] = (C.c_int32, [C.c_int32, C.c_int64, _P, _P, _P])
+    _SIGS[f"tmpc_deinterleave_{_s}"] = (C.c_int32, [C.c_int32, C.c_int64, _P, _P, _P])
+    _SIGS[f"tmpc_schur_interleave_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P])
+    _SIGS[f"tmpc_riccati_factor_il_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
+    _SIGS[f"tmpc_riccati_solve_il_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_riccati_factor_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P])
     _SIGS[f"tmpc_linearize_dynamics_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, C.c_int32, C.c_double, _P,
                                                           _P, _P, C.c_int32, _P, _P, _P])

@@ -46,13 +46,20 @@ def _deps_mtime() -> float:
     return max(os.path.getmtime(f) for f in files)
 
 
+def _obj_deps_mtime(src: str) -> float:
+    """An object depends on its own source, every header and this script."""
+    files = ([src] + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+             + [__file__])
+    return max(os.path.getmtime(f) for f in files)
+
+
 def needs_build() -> bool:
     return not os.path.exists(LIB) or os.path.getmtime(LIB) < _deps_mtime()
 
 
 def _compile(src: str, verbose: bool, extra) -> str:
     obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-    if os.path.exists(obj) and os.path.getmtime(obj) >= _deps_mtime():
+    if os.path.exists(obj) and os.path.getmtime(obj) >= _obj_deps_mtime(src):
         return obj
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *extra, "-c", src, "-o", obj]
     if verbose:

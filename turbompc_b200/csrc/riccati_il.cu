@@ -1,0 +1,451 @@
+// Block-tridiagonal Cholesky (block Riccati recursion) factor and solve on the
+// batch-interleaved layout: one problem per thread, 32 problems per warp.
+//
+// Batch-interleaved layout (TMPC_LAYOUT_INTERLEAVED): problems are grouped by
+// 32; inside a group an array of E elements per problem is stored
+// element-major and problem-minor,
+//     element e of problem b  at  ((b / 32) * E + e) * 32 + b % 32,
+// so when the 32 lanes of a warp (32 consecutive problems) touch the same
+// element, the warp issues one fully coalesced 128-byte (fp32) or 256-byte
+// (fp64) transaction.  Arrays hold ceil(Nb / 32) * 32 problem slots.
+//
+// Operator format (input of the factor), per problem, E = T n(n+1)/2 + N n^2:
+//   Theta_t  lower triangle, row-major packed: (i, j <= i) at t tri(n) + i(i+1)/2 + j
+//   Phi_t    = S(t+1, t), full row-major:    (i, k) at T tri(n) + (t n + i) n + k
+// Factor format: the same shape, L_t (lower, packed) in the Theta slots and
+// W_t = Phi_t L_t^-T in the Phi slots (S = L L^T with the block-bidiagonal L
+// of the recursion
+//   L_0 L_0^T = Theta_0,  W_{t-1} = Phi_{t-1} L_{t-1}^-T,  L_t L_t^T = Theta_t - W_{t-1} W_{t-1}^T).
+// This is the direct solve that replaces the reference's cuDSS path
+// (turbompc/solvers/linear_systems_solvers/csrc/cudss_blktridi.cu:60-184).
+//
+// Each thread keeps its stage's working matrix (packed lower, NB(NB+1)/2
+// values) in registers and runs the Cholesky fully unrolled there; W_{t-1} is
+// re-read from the factor it has just written (an L2 hit).  Block sizes are
+// compiled for NB in {4, 8, 12, 16} (fp64: up to 12); n < NB is padded with an
+// identity diagonal in registers only (memory holds exact n x n blocks).
+#include "tmpc_common.cuh"
+
+namespace tmpc {
+namespace il {
+
+constexpr int kWarp = 32;
+
+__host__ __device__ constexpr size_t tri(size_t n) { return n * (n + 1) / 2; }
+__host__ __device__ constexpr int LI(int i, int j) { return i * (i + 1) / 2 + j; }
+
+__host__ __device__ inline size_t op_elems(int T, int n) {
+  return (size_t)T * tri(n) + (size_t)(T - 1) * n * n;
+}
+__host__ __device__ inline size_t groups(int Nb) { return ((size_t)Nb + kWarp - 1) / kWarp; }
+
+template <typename R>
+__device__ __forceinline__ R ldro(const R* p) {
+  return __ldg(p);
+}
+
+// ---------------------------------------------------------------------------
+// Factor: one problem per thread.
+// ---------------------------------------------------------------------------
+template <int NB, typename R>
+__device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T, int n, bool valid, bool& ok) {
+  constexpr int TR = NB * (NB + 1) / 2;
+  const size_t trin = tri(n);
+  const size_t woff = (size_t)T * trin;
+  const size_t nn = (size_t)n * n;
+  R m[TR];
+  R dinv[NB];
+  for (int t = 0; t < T; ++t) {
+    // M = Theta_t (identity in the padded rows / columns)
+    const R* th = op + (size_t)t * trin * kWarp;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+#pragma unroll
+      for (int j = 0; j <= i; ++j) {
+        R v = (i == j) ? R(1) : R(0);
+        if (i < n && valid) v = ldro(th + (size_t)LI(i, j) * kWarp);
+        m[LI(i, j)] = v;
+      }
+    }
+    // M -= W_{t-1} W_{t-1}^T, one column k of W_{t-1} at a time (rank-1 updates)
+    if (t > 0) {
+      const R* W = f + (woff + (size_t)(t - 1) * nn) * kWarp;
+#pragma unroll
+      for (int k = 0; k < NB; ++k) {
+        if (k < n) {
+          R w[NB];
+#pragma unroll
+          for (int i = 0; i < NB; ++i) w[i] = (i < n) ? W[((size_t)i * n + k) * kWarp] : R(0);
+#pragma unroll
+          for (int i = 0; i < NB; ++i) {
+#pragma unroll
+            for (int j = 0; j <= i; ++j) m[LI(i, j)] = fma(-w[i], w[j], m[LI(i, j)]);
+          }
+        }
+      }
+    }
+    // Cholesky in registers (right-looking)
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const R d = m[LI(k, k)];
+      if (!(d > R(0)) || !isfinite(d)) ok = false;
+      const R s = sqrt(d);
+      const R inv = R(1) / s;
+      m[LI(k, k)] = s;
+      dinv[k] = inv;
+#pragma unroll
+      for (int i = k + 1; i < NB; ++i) m[LI(i, k)] *= inv;
+#pragma unroll
+      for (int j = k + 1; j < NB; ++j) {
+#pragma unroll
+        for (int i = j; i < NB; ++i) m[LI(i, j)] = fma(-m[LI(i, k)], m[LI(j, k)], m[LI(i, j)]);
+      }
+    }
+    // store L_t
+    R* lt = f + (size_t)t * trin * kWarp;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      if (i < n) {
+#pragma unroll
+        for (int j = 0; j <= i; ++j) lt[(size_t)LI(i, j) * kWarp] = m[LI(i, j)];
+      }
+    }
+    // W_t = Phi_t L_t^-T: row i solves L w = Phi_t[i, :]^T (forward substitution)
+    if (t < T - 1) {
+      const R* ph = op + (woff + (size_t)t * nn) * kWarp;
+      R* W = f + (woff + (size_t)t * nn) * kWarp;
+      R xn[NB];
+#pragma unroll
+      for (int k = 0; k < NB; ++k) xn[k] = (k < n && valid) ? ldro(ph + (size_t)k * kWarp) : R(0);
+      for (int i = 0; i < n; ++i) {
+        R x[NB];
+#pragma unroll
+        for (int k = 0; k < NB; ++k) x[k] = xn[k];
+        if (i + 1 < n) {  // next row's loads in flight during this row's substitution
+#pragma unroll
+          for (int k = 0; k < NB; ++k)
+            xn[k] = (k < n && valid) ? ldro(ph + ((size_t)(i + 1) * n + k) * kWarp) : R(0);
+        }
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+#pragma unroll
+          for (int c = 0; c < k; ++c) x[k] = fma(-m[LI(k, c)], x[c], x[k]);
+          x[k] *= dinv[k];
+        }
+#pragma unroll
+        for (int k = 0; k < NB; ++k)
+          if (k < n) W[((size_t)i * n + k) * kWarp] = x[k];
+      }
+    }
+  }
+}
+
+template <int NB, typename R>
+__global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, R* factor, int32_t* status, int Nb,
+                                                     int T, int n) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if ((b & ~(kWarp - 1)) >= Nb) return;  // the whole warp is past the batch
+  const bool valid = b < Nb;             // lanes past the batch factor the identity into the padding slots
+  const size_t E = op_elems(T, n);
+  const size_t base = (size_t)(b / kWarp) * E * kWarp + (b % kWarp);
+  bool ok = true;
+  factor_one<NB, R>(ops + base, factor + base, T, n, valid, ok);
+  if (valid && status) status[b] = ok ? 0 : TMPC_STATUS_SINGULAR_BLOCK;
+}
+
+// ---------------------------------------------------------------------------
+// Solve S x = b with the factor: one problem per thread.  The forward sweep
+// writes y into x_out (same slots), which the backward sweep reads back.
+// ---------------------------------------------------------------------------
+template <int NB, typename R>
+__global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs, R* x_out,
+                                                    int Nb, int T, int n) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= Nb) return;  // no warp-wide operation below: lanes past the batch leave at once
+  const size_t trin = tri(n), nn = (size_t)n * n;
+  const size_t woff = (size_t)T * trin;
+  const size_t fb = (size_t)(b / kWarp) * op_elems(T, n) * kWarp + (b % kWarp);
+  const size_t vb = (size_t)(b / kWarp) * T * n * kWarp + (b % kWarp);
+  const R* F = factor + fb;
+  const R* bv = rhs + vb;
+  R* xv = x_out + vb;
+  // forward: y_t = L_t^-1 (b_t - W_{t-1} y_{t-1})
+  R yp[NB];
+#pragma unroll
+  for (int k = 0; k < NB; ++k) yp[k] = R(0);
+  for (int t = 0; t < T; ++t) {
+    R u[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) u[k] = (k < n) ? ldro(bv + ((size_t)t * n + k) * kWarp) : R(0);
+    if (t > 0) {
+      const R* W = F + (woff + (size_t)(t - 1) * nn) * kWarp;
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        if (i < n) {
+          R s = R(0);
+#pragma unroll
+          for (int k = 0; k < NB; ++k)
+            if (k < n) s = fma(ldro(W + ((size_t)i * n + k) * kWarp), yp[k], s);
+          u[i] -= s;
+        }
+      }
+    }
+    const R* L = F + (size_t)t * trin * kWarp;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      if (k < n) {
+#pragma unroll
+        for (int c = 0; c < k; ++c) u[k] = fma(-ldro(L + (size_t)LI(k, c) * kWarp), u[c], u[k]);
+        u[k] = u[k] / ldro(L + (size_t)LI(k, k) * kWarp);
+        xv[((size_t)t * n + k) * kWarp] = u[k];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) yp[k] = (k < n) ? u[k] : R(0);
+  }
+  // backward: x_t = L_t^-T (y_t - W_t^T x_{t+1})
+  R xp[NB];
+#pragma unroll
+  for (int k = 0; k < NB; ++k) xp[k] = R(0);
+  for (int t = T - 1; t >= 0; --t) {
+    R u[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) u[k] = (k < n) ? xv[((size_t)t * n + k) * kWarp] : R(0);
+    if (t < T - 1) {
+      const R* W = F + (woff + (size_t)t * nn) * kWarp;
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        if (i < n) {
+#pragma unroll
+          for (int k = 0; k < NB; ++k)
+            if (k < n) u[k] = fma(-ldro(W + ((size_t)i * n + k) * kWarp), xp[i], u[k]);
+        }
+      }
+    }
+    const R* L = F + (size_t)t * trin * kWarp;
+#pragma unroll
+    for (int k = NB - 1; k >= 0; --k) {
+      if (k < n) {
+#pragma unroll
+        for (int i = k + 1; i < NB; ++i)
+          if (i < n) u[k] = fma(-ldro(L + (size_t)LI(i, k) * kWarp), u[i], u[k]);
+        u[k] = u[k] / ldro(L + (size_t)LI(k, k) * kWarp);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      if (k < n) xv[((size_t)t * n + k) * kWarp] = u[k];
+      xp[k] = (k < n) ? u[k] : R(0);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Layout conversion: [Nb][E] problem-major <-> interleaved, through a 32 x 32
+// shared-memory tile (coalesced on both sides).  With a gather map, element e
+// of the interleaved array takes the problem-major element src(e).
+// ---------------------------------------------------------------------------
+struct IdentityMap {
+  __device__ size_t operator()(size_t e) const { return e; }
+};
+// Reference-layout S [T][n][3n] -> operator format (Theta lower packed, Phi).
+struct SchurMap {
+  int T, n;
+  __device__ size_t operator()(size_t e) const {
+    const size_t trin = tri(n);
+    const size_t n3 = 3 * (size_t)n;
+    if (e < (size_t)T * trin) {
+      const size_t t = e / trin;
+      size_t r = e - t * trin;
+      size_t i = (size_t)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
+      while (i * (i + 1) / 2 > r) --i;
+      while ((i + 1) * (i + 2) / 2 <= r) ++i;
+      const size_t j = r - i * (i + 1) / 2;
+      return (t * n + i) * n3 + n + j;  // Theta_t[i][j] = S[t][i][n + j]
+    }
+    const size_t e2 = e - (size_t)T * trin;
+    const size_t nn = (size_t)n * n;
+    const size_t t = e2 / nn, rem = e2 - t * nn;
+    const size_t i = rem / n, k = rem - i * n;
+    return ((t + 1) * n + i) * n3 + k;  // Phi_t[i][k] = S[t+1][i][k]
+  }
+};
+
+template <typename R, class Map>
+__global__ void __launch_bounds__(256) interleave_kernel(const R* __restrict__ in, R* out, int Nb, size_t E_in,
+                                                         size_t E, Map map) {
+  __shared__ R tile[32][33];
+  const size_t grp = blockIdx.y;
+  const size_t e0 = (size_t)blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int r = ty; r < 32; r += 8) {
+    const size_t b = grp * 32 + r, e = e0 + tx;
+    tile[r][tx] = (b < (size_t)Nb && e < E) ? in[b * E_in + map(e)] : R(0);
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const size_t e = e0 + r;
+    if (e < E) out[(grp * E + e) * 32 + tx] = tile[tx][r];
+  }
+}
+
+template <typename R>
+__global__ void __launch_bounds__(256) deinterleave_kernel(const R* __restrict__ in, R* out, int Nb, size_t E) {
+  __shared__ R tile[32][33];
+  const size_t grp = blockIdx.y;
+  const size_t e0 = (size_t)blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int r = ty; r < 32; r += 8) {
+    const size_t e = e0 + r;
+    tile[r][tx] = e < E ? in[(grp * E + e) * 32 + tx] : R(0);
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const size_t b = grp * 32 + r, e = e0 + tx;
+    if (b < (size_t)Nb && e < E) out[b * E + e] = tile[tx][r];
+  }
+}
+
+inline bool grid_ok(int Nb, size_t E) { return groups(Nb) <= 65535 && (E + 31) / 32 <= 0x7fffffffu; }
+
+template <typename R, class Map>
+int interleave(int Nb, size_t E_in, size_t E, const R* in, R* out, Map map, cudaStream_t st) {
+  if (Nb < 0) return TMPC_ERR_BAD_DIMS;
+  if (Nb == 0 || E == 0) return TMPC_OK;
+  if (!in || !out) return TMPC_ERR_NULL_ARG;
+  if (!grid_ok(Nb, E)) return TMPC_ERR_BAD_DIMS;
+  dim3 grid((unsigned)((E + 31) / 32), (unsigned)groups(Nb)), block(32, 8);
+  interleave_kernel<R, Map><<<grid, block, 0, st>>>(in, out, Nb, E_in, E, map);
+  return (int)cudaPeekAtLastError();
+}
+
+template <typename R>
+int deinterleave(int Nb, size_t E, const R* in, R* out, cudaStream_t st) {
+  if (Nb < 0) return TMPC_ERR_BAD_DIMS;
+  if (Nb == 0 || E == 0) return TMPC_OK;
+  if (!in || !out) return TMPC_ERR_NULL_ARG;
+  if (!grid_ok(Nb, E)) return TMPC_ERR_BAD_DIMS;
+  dim3 grid((unsigned)((E + 31) / 32), (unsigned)groups(Nb)), block(32, 8);
+  deinterleave_kernel<R><<<grid, block, 0, st>>>(in, out, Nb, E);
+  return (int)cudaPeekAtLastError();
+}
+
+template <typename R>
+constexpr int max_nb() {
+  return sizeof(R) == 4 ? 16 : 12;
+}
+
+template <typename R, class F>
+int dispatch_il(int n, F&& f) {
+  if (n <= 4) return f(std::integral_constant<int, 4>{});
+  if (n <= 8) return f(std::integral_constant<int, 8>{});
+  if (n <= 12) return f(std::integral_constant<int, 12>{});
+  if constexpr (max_nb<R>() >= 16) {
+    if (n <= 16) return f(std::integral_constant<int, 16>{});
+  }
+  return TMPC_ERR_UNSUPPORTED;
+}
+
+int check(const TmpcDims* d) {
+  if (!d) return TMPC_ERR_NULL_ARG;
+  if (d->Nb < 0 || d->T < 2 || d->n < 1) return TMPC_ERR_BAD_DIMS;
+  return TMPC_OK;
+}
+
+template <typename R>
+int factor(const TmpcDims* d, const R* ops, R* fac, int32_t* status, cudaStream_t st) {
+  int rc = check(d);
+  if (rc) return rc;
+  if (d->n > max_nb<R>()) return TMPC_ERR_UNSUPPORTED;
+  if (d->Nb == 0) return TMPC_OK;
+  if (!ops || !fac) return TMPC_ERR_NULL_ARG;
+  return dispatch_il<R>(d->n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    const int grid = (int)((groups(d->Nb) * kWarp + 127) / 128);
+    factor_kernel<NB, R><<<grid, 128, 0, st>>>(ops, fac, status, d->Nb, d->T, d->n);
+    return (int)cudaPeekAtLastError();
+  });
+}
+
+template <typename R>
+int solve(const TmpcDims* d, const R* fac, const R* rhs, R* x, cudaStream_t st) {
+  int rc = check(d);
+  if (rc) return rc;
+  if (d->n > max_nb<R>()) return TMPC_ERR_UNSUPPORTED;
+  if (d->Nb == 0) return TMPC_OK;
+  if (!fac || !rhs || !x) return TMPC_ERR_NULL_ARG;
+  return dispatch_il<R>(d->n, [&](auto tag) {
+    constexpr int NB = decltype(tag)::value;
+    const int grid = (d->Nb + 127) / 128;
+    solve_kernel<NB, R><<<grid, 128, 0, st>>>(fac, rhs, x, d->Nb, d->T, d->n);
+    return (int)cudaPeekAtLastError();
+  });
+}
+
+}  // namespace il
+}  // namespace tmpc
+
+extern "C" {
+
+size_t tmpc_interleaved_elems(int32_t Nb, int64_t elems_per_problem) {
+  if (Nb <= 0 || elems_per_problem <= 0) return 0;
+  return tmpc::il::groups(Nb) * tmpc::il::kWarp * (size_t)elems_per_problem;
+}
+
+int64_t tmpc_riccati_il_elems_per_problem(const TmpcDims* dims) {
+  if (tmpc::il::check(dims)) return 0;
+  return (int64_t)tmpc::il::op_elems(dims->T, dims->n);
+}
+
+int32_t tmpc_interleave_f32(int32_t Nb, int64_t elems, const float* src, float* dst, tmpc_stream_t stream) {
+  if (elems < 0) return TMPC_ERR_BAD_DIMS;
+  return tmpc::il::interleave<float>(Nb, (size_t)elems, (size_t)elems, src, dst, tmpc::il::IdentityMap{},
+                                     (cudaStream_t)stream);
+}
+int32_t tmpc_interleave_f64(int32_t Nb, int64_t elems, const double* src, double* dst, tmpc_stream_t stream) {
+  if (elems < 0) return TMPC_ERR_BAD_DIMS;
+  return tmpc::il::interleave<double>(Nb, (size_t)elems, (size_t)elems, src, dst, tmpc::il::IdentityMap{},
+                                      (cudaStream_t)stream);
+}
+int32_t tmpc_deinterleave_f32(int32_t Nb, int64_t elems, const float* src, float* dst, tmpc_stream_t stream) {
+  if (elems < 0) return TMPC_ERR_BAD_DIMS;
+  return tmpc::il::deinterleave<float>(Nb, (size_t)elems, src, dst, (cudaStream_t)stream);
+}
+int32_t tmpc_deinterleave_f64(int32_t Nb, int64_t elems, const double* src, double* dst, tmpc_stream_t stream) {
+  if (elems < 0) return TMPC_ERR_BAD_DIMS;
+  return tmpc::il::deinterleave<double>(Nb, (size_t)elems, src, dst, (cudaStream_t)stream);
+}
+
+int32_t tmpc_schur_interleave_f32(const TmpcDims* dims, const float* S, float* ops, tmpc_stream_t stream) {
+  int rc = tmpc::il::check(dims);
+  if (rc) return rc;
+  const size_t Es = (size_t)dims->T * dims->n * 3 * dims->n;
+  return tmpc::il::interleave<float>(dims->Nb, Es, tmpc::il::op_elems(dims->T, dims->n), S, ops,
+                                     tmpc::il::SchurMap{dims->T, dims->n}, (cudaStream_t)stream);
+}
+int32_t tmpc_schur_interleave_f64(const TmpcDims* dims, const double* S, double* ops, tmpc_stream_t stream) {
+  int rc = tmpc::il::check(dims);
+  if (rc) return rc;
+  const size_t Es = (size_t)dims->T * dims->n * 3 * dims->n;
+  return tmpc::il::interleave<double>(dims->Nb, Es, tmpc::il::op_elems(dims->T, dims->n), S, ops,
+                                      tmpc::il::SchurMap{dims->T, dims->n}, (cudaStream_t)stream);
+}
+
+int32_t tmpc_riccati_factor_il_f32(const TmpcDims* dims, const float* ops, float* factor, int32_t* status,
+                                   tmpc_stream_t stream) {
+  return tmpc::il::factor<float>(dims, ops, factor, status, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_factor_il_f64(const TmpcDims* dims, const double* ops, double* factor, int32_t* status,
+                                   tmpc_stream_t stream) {
+  return tmpc::il::factor<double>(dims, ops, factor, status, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_solve_il_f32(const TmpcDims* dims, const float* factor, const float* rhs, float* x,
+                                  tmpc_stream_t stream) {
+  return tmpc::il::solve<float>(dims, factor, rhs, x, (cudaStream_t)stream);
+}
+int32_t tmpc_riccati_solve_il_f64(const TmpcDims* dims, const double* factor, const double* rhs, double* x,
+                                  tmpc_stream_t stream) {
+  return tmpc::il::solve<double>(dims, factor, rhs, x, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -347,3 +347,69 @@ def first_order_error(qp: QPData, z: torch.Tensor, state: ADMMState, slacks: Opt
                                         _ptr(_rho_vec(sw, qp) if sw is not None else None, dt, dev),
                                         int(use_slack), _ptr(conv), _ptr(eq), _ptr(ineq), _ptr(g), _stream(dev)))
     return conv, eq, ineq, g
+
+
+# ---------------------------------------------------------------------------
+# Batch-interleaved layout (TMPC_LAYOUT_INTERLEAVED): groups of 32 problems,
+# element-major and problem-minor inside a group.
+# ---------------------------------------------------------------------------
+def interleaved_numel(nb: int, elems_per_problem: int) -> int:
+    return int(_ffi.load().tmpc_interleaved_elems(int(nb), int(elems_per_problem)))
+
+
+def interleave(x: torch.Tensor) -> torch.Tensor:
+    """Problem-major (Nb, ...) -> flat interleaved tensor."""
+    lib = _ffi.load()
+    nb = x.shape[0]
+    e = x[0].numel() if nb > 0 else 0
+    out = torch.empty(max(interleaved_numel(nb, e), 1), dtype=x.dtype, device=x.device)
+    name = f"tmpc_interleave_{_suffix(x.dtype)}"
+    _ffi.check(name, getattr(lib, name)(nb, e, _ptr(x.contiguous()), out.data_ptr(), _stream(x.device)))
+    return out
+
+
+def deinterleave(flat: torch.Tensor, shape) -> torch.Tensor:
+    """Flat interleaved tensor -> problem-major tensor of ``shape`` (Nb, ...)."""
+    lib = _ffi.load()
+    out = torch.empty(shape, dtype=flat.dtype, device=flat.device)
+    nb = shape[0]
+    e = out[0].numel() if nb > 0 else 0
+    name = f"tmpc_deinterleave_{_suffix(flat.dtype)}"
+    _ffi.check(name, getattr(lib, name)(nb, e, flat.data_ptr(), _ptr(out), _stream(flat.device)))
+    return out
+
+
+def schur_interleave(S: torch.Tensor) -> torch.Tensor:
+    """Reference-layout S (Nb, T, n, 3n) -> the interleaved operator (Theta
+    lower-packed and Phi blocks) that riccati_factor_il takes."""
+    lib = _ffi.load()
+    B, T, n = S.shape[:3]
+    d = _ffi.TmpcDims(B, T, n, n, 0, 0)
+    e = int(lib.tmpc_riccati_il_elems_per_problem(C.byref(d)))
+    ops_il = torch.empty(max(interleaved_numel(B, e), 1), dtype=S.dtype, device=S.device)
+    name = f"tmpc_schur_interleave_{_suffix(S.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), _ptr(S), ops_il.data_ptr(), _stream(S.device)))
+    return ops_il
+
+
+def riccati_factor_il(ops_il: torch.Tensor, dims: _ffi.TmpcDims, factor: Optional[torch.Tensor] = None,
+                      status: Optional[torch.Tensor] = None):
+    """Block Cholesky on the interleaved operator; returns (factor, status)."""
+    lib = _ffi.load()
+    fac = torch.empty_like(ops_il) if factor is None else factor
+    st = torch.zeros(dims.Nb, dtype=torch.int32, device=ops_il.device) if status is None else status
+    name = f"tmpc_riccati_factor_il_{_suffix(ops_il.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(dims), ops_il.data_ptr(), fac.data_ptr(), _ptr(st),
+                                        _stream(ops_il.device)))
+    return fac, st
+
+
+def riccati_solve_il(factor: torch.Tensor, dims: _ffi.TmpcDims, rhs_il: torch.Tensor,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Solve S x = rhs on interleaved vectors (flat, from interleave)."""
+    lib = _ffi.load()
+    x = torch.empty_like(rhs_il) if out is None else out
+    name = f"tmpc_riccati_solve_il_{_suffix(factor.dtype)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(dims), factor.data_ptr(), rhs_il.data_ptr(), x.data_ptr(),
+                                        _stream(factor.device)))
+    return x
