@@ -12,10 +12,15 @@
 // Operator format (input of the factor), per problem, E = T n(n+1)/2 + N n^2:
 //   Theta_t  lower triangle, row-major packed: (i, j <= i) at t tri(n) + i(i+1)/2 + j
 //   Phi_t    = S(t+1, t), full row-major:    (i, k) at T tri(n) + (t n + i) n + k
-// Factor format: the same shape, L_t (lower, packed) in the Theta slots and
-// W_t = Phi_t L_t^-T in the Phi slots (S = L L^T with the block-bidiagonal L
-// of the recursion
-//   L_0 L_0^T = Theta_0,  W_{t-1} = Phi_{t-1} L_{t-1}^-T,  L_t L_t^T = Theta_t - W_{t-1} W_{t-1}^T).
+// Factor format: the same shape, L_t^-1 (lower, packed) in the Theta slots and
+// W_t = Phi_t L_t^-T in the Phi slots, for the block-bidiagonal L of S = L L^T
+// from the recursion
+//   L_0 L_0^T = Theta_0,  W_{t-1} = Phi_{t-1} L_{t-1}^-T,  L_t L_t^T = Theta_t - W_{t-1} W_{t-1}^T.
+// Keeping the inverse of each diagonal factor (inverted in registers right
+// after its Cholesky) turns every triangular solve into a matrix-vector
+// product whose rows are independent: with one problem per thread, the
+// substitution chains would otherwise leave each thread waiting on one
+// memory latency per row.
 // This is the direct solve that replaces the reference's cuDSS path
 // (turbompc/solvers/linear_systems_solvers/csrc/cudss_blktridi.cu:60-184).
 //
@@ -48,13 +53,13 @@ __device__ __forceinline__ R ldro(const R* p) {
 // Factor: one problem per thread.
 // ---------------------------------------------------------------------------
 template <int NB, typename R>
-__device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T, int n, bool valid, bool& ok) {
+__device__ __forceinline__ void factor_one(const R* __restrict__ op, R* __restrict__ f, int T, int n, bool valid,
+                                           bool& ok) {
   constexpr int TR = NB * (NB + 1) / 2;
   const size_t trin = tri(n);
   const size_t woff = (size_t)T * trin;
   const size_t nn = (size_t)n * n;
   R m[TR];
-  R dinv[NB];
   for (int t = 0; t < T; ++t) {
     // M = Theta_t (identity in the padded rows / columns)
     const R* th = op + (size_t)t * trin * kWarp;
@@ -92,7 +97,6 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T
       const R s = sqrt(d);
       const R inv = R(1) / s;
       m[LI(k, k)] = s;
-      dinv[k] = inv;
 #pragma unroll
       for (int i = k + 1; i < NB; ++i) m[LI(i, k)] *= inv;
 #pragma unroll
@@ -101,7 +105,23 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T
         for (int i = j; i < NB; ++i) m[LI(i, j)] = fma(-m[LI(i, k)], m[LI(j, k)], m[LI(i, j)]);
       }
     }
-    // store L_t
+    // L_t^-1 in place, column by column from the last: with X = L^-1,
+    // X[j][j] = 1 / L[j][j] and X[i][j] = -X[j][j] sum_{k=j+1..i} X[i][k] L[k][j]
+    // (rows i taken from the bottom up, so the L[k][j], k <= i, they read
+    // are not yet overwritten).
+#pragma unroll
+    for (int j = NB - 1; j >= 0; --j) {
+      const R xjj = R(1) / m[LI(j, j)];
+      m[LI(j, j)] = xjj;
+#pragma unroll
+      for (int i = NB - 1; i > j; --i) {
+        R acc = R(0);
+#pragma unroll
+        for (int k = j + 1; k <= i; ++k) acc = fma(m[LI(i, k)], m[LI(k, j)], acc);
+        m[LI(i, j)] = -xjj * acc;
+      }
+    }
+    // store L_t^-1
     R* lt = f + (size_t)t * trin * kWarp;
 #pragma unroll
     for (int i = 0; i < NB; ++i) {
@@ -110,7 +130,7 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T
         for (int j = 0; j <= i; ++j) lt[(size_t)LI(i, j) * kWarp] = m[LI(i, j)];
       }
     }
-    // W_t = Phi_t L_t^-T: row i solves L w = Phi_t[i, :]^T (forward substitution)
+    // W_t = Phi_t L_t^-T: row i is L_t^-1 Phi_t[i, :]^T
     if (t < T - 1) {
       const R* ph = op + (woff + (size_t)t * nn) * kWarp;
       R* W = f + (woff + (size_t)t * nn) * kWarp;
@@ -121,27 +141,28 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* f, int T
         R x[NB];
 #pragma unroll
         for (int k = 0; k < NB; ++k) x[k] = xn[k];
-        if (i + 1 < n) {  // next row's loads in flight during this row's substitution
+        if (i + 1 < n) {  // next row's loads in flight during this row's product
 #pragma unroll
           for (int k = 0; k < NB; ++k)
             xn[k] = (k < n && valid) ? ldro(ph + ((size_t)(i + 1) * n + k) * kWarp) : R(0);
         }
 #pragma unroll
         for (int k = 0; k < NB; ++k) {
+          if (k < n) {
+            R acc = R(0);
 #pragma unroll
-          for (int c = 0; c < k; ++c) x[k] = fma(-m[LI(k, c)], x[c], x[k]);
-          x[k] *= dinv[k];
+            for (int c = 0; c <= k; ++c) acc = fma(m[LI(k, c)], x[c], acc);
+            W[((size_t)i * n + k) * kWarp] = acc;
+          }
         }
-#pragma unroll
-        for (int k = 0; k < NB; ++k)
-          if (k < n) W[((size_t)i * n + k) * kWarp] = x[k];
       }
     }
   }
 }
 
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, R* factor, int32_t* status, int Nb,
+__global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, R* __restrict__ factor,
+                                                     int32_t* status, int Nb,
                                                      int T, int n) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if ((b & ~(kWarp - 1)) >= Nb) return;  // the whole warp is past the batch
@@ -158,7 +179,8 @@ __global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, 
 // writes y into x_out (same slots), which the backward sweep reads back.
 // ---------------------------------------------------------------------------
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs, R* x_out,
+__global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs,
+                                                    R* __restrict__ x_out,
                                                     int Nb, int T, int n) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= Nb) return;  // no warp-wide operation below: lanes past the batch leave at once
@@ -190,18 +212,17 @@ __global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor
         }
       }
     }
-    const R* L = F + (size_t)t * trin * kWarp;
+    const R* X = F + (size_t)t * trin * kWarp;  // L_t^-1
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
+      R acc = R(0);
       if (k < n) {
 #pragma unroll
-        for (int c = 0; c < k; ++c) u[k] = fma(-ldro(L + (size_t)LI(k, c) * kWarp), u[c], u[k]);
-        u[k] = u[k] / ldro(L + (size_t)LI(k, k) * kWarp);
-        xv[((size_t)t * n + k) * kWarp] = u[k];
+        for (int c = 0; c <= k; ++c) acc = fma(ldro(X + (size_t)LI(k, c) * kWarp), u[c], acc);
+        xv[((size_t)t * n + k) * kWarp] = acc;
       }
+      yp[k] = acc;
     }
-#pragma unroll
-    for (int k = 0; k < NB; ++k) yp[k] = (k < n) ? u[k] : R(0);
   }
   // backward: x_t = L_t^-T (y_t - W_t^T x_{t+1})
   R xp[NB];
@@ -222,20 +243,17 @@ __global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor
         }
       }
     }
-    const R* L = F + (size_t)t * trin * kWarp;
+    const R* X = F + (size_t)t * trin * kWarp;  // L_t^-1; x = (L_t^-1)^T u
 #pragma unroll
-    for (int k = NB - 1; k >= 0; --k) {
-      if (k < n) {
+    for (int c = 0; c < NB; ++c) {
+      R acc = R(0);
+      if (c < n) {
 #pragma unroll
-        for (int i = k + 1; i < NB; ++i)
-          if (i < n) u[k] = fma(-ldro(L + (size_t)LI(i, k) * kWarp), u[i], u[k]);
-        u[k] = u[k] / ldro(L + (size_t)LI(k, k) * kWarp);
+        for (int k = c; k < NB; ++k)
+          if (k < n) acc = fma(ldro(X + (size_t)LI(k, c) * kWarp), u[k], acc);
+        xv[((size_t)t * n + c) * kWarp] = acc;
       }
-    }
-#pragma unroll
-    for (int k = 0; k < NB; ++k) {
-      if (k < n) xv[((size_t)t * n + k) * kWarp] = u[k];
-      xp[k] = (k < n) ? u[k] : R(0);
+      xp[c] = acc;
     }
   }
 }
