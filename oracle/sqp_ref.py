@@ -177,6 +177,9 @@ class OCP:
         self.n = self.nx + self.nu
         self.dt = float(p["discretization_resolution"])
         self.scheme = int(p["discretization_scheme"])
+        # optimal_control_problem.py:168-171
+        self.rescale = bool(p.get("rescale_optimization_variables", False))
+        self.constrain_u0 = bool(p.get("constrain_initial_control", False))
         # optimal_control_problem.py:177-186 and :433-440
         keys = ("state_min_bounds", "state_max_bounds", "control_min_bounds", "control_max_bounds")
         if all(k in p for k in keys):
@@ -187,6 +190,14 @@ class OCP:
         else:
             self.state_mask = torch.zeros(self.nx, dtype=torch.bool)
             self.control_mask = torch.zeros(self.nu, dtype=torch.bool)
+
+    # ---- rescaling (optimal_control_problem.py:284-349)
+    def rescaling(self, p):
+        if not self.rescale:
+            return torch.ones(self.nx, dtype=F64), torch.ones(self.nu, dtype=F64)
+        sd = (p["state_rescaling_max"] - p["state_rescaling_min"]) / 2.0
+        cd = (p["control_rescaling_max"] - p["control_rescaling_min"]) / 2.0
+        return sd, cd
 
     # ---- cost (optimal_control_problem.py:982-1030)
     def _refs(self, p):
@@ -268,7 +279,8 @@ class OCP:
         return predict_next_state(self.model, self.dt, self.scheme, self._dp(p), x, u)
 
     def dynamics_rows(self, X, U, p):
-        """A_minus = [A B], A_plus = [-I 0], c (N, nx)."""
+        """A_minus = [A B], A_plus = [-I 0], c (N, nx), each row scaled by
+        1 / state_diff under rescaling (optimal_control_problem.py:1322-1331)."""
         N, nx = self.N, self.nx
 
         def f(xu):
@@ -280,12 +292,19 @@ class OCP:
         c = -val + (J @ XU[..., None])[..., 0]
         Ap = torch.zeros(N, nx, self.n, dtype=F64)
         Ap[:, :, :nx] = -torch.eye(nx, dtype=F64)
-        return J, Ap, c
+        rs = 1.0 / self.rescaling(p)[0]
+        return J * rs[:, None], Ap * rs[:, None], c * rs
 
     def equality_constraints(self, X, U, p):
+        """optimal_control_problem.py:841-912 (explicit schemes)."""
+        sd, cd = self.rescaling(p)
         x0c = X[0] - p["initial_state"]
         nxt = vmap(lambda x, u: self.next_state(x, u, p))(X[:-1], U[:-1])
-        return torch.cat([x0c, (nxt - X[1:]).reshape(-1)])
+        rows = torch.cat([x0c[None], nxt - X[1:]]) / sd
+        out = [rows.reshape(-1)]
+        if self.constrain_u0:
+            out.append((U[0] - p["initial_control"]) / cd)
+        return torch.cat(out)
 
     # ---- inequalities (optimal_control_problem.py:413-471; obstacle_avoidance.py:16-52)
     def step_inequality(self, x, u, p):
@@ -295,16 +314,21 @@ class OCP:
             xh = p["state_max_bounds"].expand(self.nx)[self.state_mask]
             ul = p["control_min_bounds"].expand(self.nu)[self.control_mask]
             uh = p["control_max_bounds"].expand(self.nu)[self.control_mask]
-            parts_g.append(torch.cat([x[self.state_mask], u[self.control_mask]]))
-            parts_l.append(torch.cat([xl, ul]))
-            parts_u.append(torch.cat([xh, uh]))
+            sc = torch.ones(int(self.state_mask.sum()) + int(self.control_mask.sum()), dtype=F64)
+            if self.rescale:  # optimal_control_problem.py:460-469
+                sd, cd = self.rescaling(p)
+                sc = torch.cat([sd[self.state_mask], cd[self.control_mask]])
+            parts_g.append(torch.cat([x[self.state_mask], u[self.control_mask]]) / sc)
+            parts_l.append(torch.cat([xl, ul]) / sc)
+            parts_u.append(torch.cat([xh, uh]) / sc)
         if self.obstacles:
             dim = int(p["obstacles_dimension"])
             c, r = p["obstacles_centers"], p["obstacles_radii"]
             g = 1.0 - torch.linalg.vector_norm(x[:dim] - c, dim=-1) / (r + 0.001)
-            parts_g.append(g)
-            parts_l.append(torch.full_like(g, -1e9))
-            parts_u.append(torch.zeros_like(g))
+            rs = 1.0 / self.rescaling(p)[0][:dim].mean() if self.rescale else 1.0  # obstacle_avoidance.py:40-45
+            parts_g.append(g * rs)
+            parts_l.append(torch.full_like(g, -1e9) * rs)
+            parts_u.append(torch.zeros_like(g) * rs)
         if not parts_g:
             z = torch.zeros(0, dtype=F64)
             return z, z, z
@@ -339,8 +363,10 @@ class OCP:
     def dynamics_lagrangian_hessian(self, X, U, p, lam):
         nx = self.nx
 
+        rs = 1.0 / self.rescaling(p)[0]
+
         def s(xu, l_):
-            return l_ @ self.next_state(xu[:nx], xu[nx:], p)
+            return l_ @ (rs * self.next_state(xu[:nx], xu[nx:], p))
 
         XU = torch.cat([X[:-1], U[:-1]], -1)
         H = vmap(hessian(s))(XU, lam)
@@ -352,13 +378,22 @@ class OCP:
         return torch.stack([hessian(lambda xu: mu[t] @ self.step_inequality(xu[:nx], xu[nx:], p)[0])(XU[t])
                             for t in range(self.T)])
 
-    # ---- the QP (turbompc_solver.py:1098-1156, without variable rescaling)
-    def qp(self, X, U, p):
+    # ---- the QP (turbompc_solver.py:1098-1156)
+    def qp(self, X, U, p, apply_variable_scaling=True):
         D, E, q = self.cost_blocks(X, U, p)
         Am, Ap, c = self.dynamics_rows(X, U, p)
         G, l, u = self.inequality_rows(X, U, p)
-        A0 = torch.cat([torch.eye(self.nx, dtype=F64), torch.zeros(self.nx, self.nu, dtype=F64)], 1)
-        c0 = p["initial_state"].clone()
+        sd, cd = self.rescaling(p)
+        # optimal_control_problem.py:914-980
+        A0 = torch.cat([torch.diag(1.0 / sd), torch.zeros(self.nx, self.nu, dtype=F64)], 1)
+        c0 = p["initial_state"] / sd
+        if self.constrain_u0:
+            A0 = torch.cat([A0, torch.cat([torch.zeros(self.nu, self.nx, dtype=F64), torch.diag(1.0 / cd)], 1)])
+            c0 = torch.cat([c0, p["initial_control"] / cd])
+        if self.rescale and apply_variable_scaling:  # qp_data.py:178-210, z = diag(sc) z_hat
+            sc = torch.cat([sd, cd])
+            D, E, q = D * sc[:, None] * sc[None, :], E * sc[:, None] * sc[None, :], q * sc
+            A0, Am, Ap, G = A0 * sc, Am * sc, Ap * sc, G * sc
         sw = float(p.get("slack_penalization_weight", 0.0))
         a = lambda t: t.detach().numpy()[None]
         return ref.QP(D=a(D), E=a(E), q=a(q), A0=a(A0), Am=a(Am), Ap=a(Ap), c0=a(c0), c=a(c), G=a(G), l=a(l),
@@ -438,10 +473,12 @@ def solve(ocp: OCP, X0, U0, cfg: ref.ADMMConfig, num_sqp: int, tol: float = 0.0,
     while (it < num_sqp and conv > tol) or it < 1:
         st_new, n_it = ref.admm_solve(qp, st, cfg, linsys=linsys)
         iters.append(int(n_it[0]))
-        z_new = st_new.x
-        Xn = torch.as_tensor(z_new[0, :, :ocp.nx])
-        Un = torch.as_tensor(z_new[0, :, ocp.nx:])
-        step = float(np.max(np.abs(z_new - z_prev)))
+        z_new = st_new.x  # QP (scaled) coordinates
+        sd, cd = ocp.rescaling(p)
+        Xn = torch.as_tensor(z_new[0, :, :ocp.nx]) * sd
+        Un = torch.as_tensor(z_new[0, :, ocp.nx:]) * cd
+        z_true = torch.cat([Xn, Un], -1).numpy()[None]
+        step = float(np.max(np.abs(z_true - z_prev)))
         if st_new.xi_g.shape[-1] > 0:
             step += float(np.max(np.abs(st_new.xi_g - slacks)))
         if it + 1 < num_sqp:
@@ -455,7 +492,7 @@ def solve(ocp: OCP, X0, U0, cfg: ref.ADMMConfig, num_sqp: int, tol: float = 0.0,
             if qp.use_slack:
                 g = g + st_new.xi_g
         lo, up = build_kkt_active_sets(ocp, st_new, g[0], qp_next.l[0], qp_next.u[0])
-        X, U, st, slacks, z_prev, qp, conv = Xn, Un, st_new, st_new.xi_g, z_new, qp_next, conv_new
+        X, U, st, slacks, z_prev, qp, conv = Xn, Un, st_new, st_new.xi_g, z_true, qp_next, conv_new
         it += 1
     return Solution(X.numpy(), U.numpy(), st, it, conv, lo, up, iters)
 
@@ -483,7 +520,7 @@ def vjp(ocp: OCP, sol: Solution, dl_dstates, dl_dcontrols, weight_keys=(), dl_ds
     U = torch.as_tensor(sol.controls, dtype=F64)
     st = sol.state
     nx, n, T, N = ocp.nx, ocp.n, ocp.T, ocp.N
-    qp = ocp.qp(X, U, p)
+    qp = ocp.qp(X, U, p, apply_variable_scaling=False)  # turbompc_solver.py:553-560
     m = qp.G.shape[2]
     D = qp.D[0].copy()
     lo = sol.active_lower.astype(np.float64)
@@ -514,7 +551,9 @@ def vjp(ocp: OCP, sol: Solution, dl_dstates, dl_dcontrols, weight_keys=(), dl_ds
     mult = solv[T * n:]
     n0 = qp.A0.shape[1]
     n_eq = n0 + N * nx
-    y_eq_lin = mult[:n_eq]
+    # [x0 rows, dynamics rows, u0 rows], the order of equality_constraints
+    # (turbompc_solver.py:736-744)
+    y_eq_lin = np.concatenate([mult[:nx], mult[n0:n_eq], mult[nx:n0]])
     dL_dgamma = 0.0
     if slack_branch:
         act = np.maximum(lo, up)
@@ -524,10 +563,14 @@ def vjp(ocp: OCP, sol: Solution, dl_dstates, dl_dcontrols, weight_keys=(), dl_ds
     else:
         y_ineq_lin = mult[n_eq:n_eq + T * m]
     # forward multipliers (turbompc_solver.py:862-880)
-    y_eq_star = np.concatenate([st.y_f0[0], st.y_fdyn[0].reshape(-1)])
+    y_eq_star = np.concatenate([st.y_f0[0, :nx], st.y_fdyn[0].reshape(-1), st.y_f0[0, nx:]])
     y_ineq_star = (-sign * st.y_g[0]).reshape(-1)
 
-    out = {"initial_state": y_eq_lin[:nx].copy()}
+    # turbompc_solver.py:990-1018: the x0 / u0 row multipliers, unscaled
+    sd, cd = ocp.rescaling(p)
+    out = {"initial_state": mult[:nx] / sd.numpy()}
+    if ocp.constrain_u0:
+        out["initial_control"] = mult[nx:n0] / cd.numpy()
     if weight_keys:
         leaves = [_get(p, k) for k in weight_keys]
         yes, yis = torch.as_tensor(y_eq_star), torch.as_tensor(y_ineq_star)

@@ -239,3 +239,57 @@ def test_soft_constraint_vjp_matches_oracle_fp64():
 
 def _oracle_ocp_lin(prog, params, b):
     return sr.OCP("linear", 4, 2, sr.problem_params(params, b), use_slack=True, eps_abs=EPS_KKT, eps_rel=EPS_KKT)
+
+
+def _rescaled_quadrotor(batch, N, dtype, device):
+    from tests.test_sqp_oracle import rescaled
+    from turbompc_b200.dynamics import Quadrotor12Dynamics
+    from turbompc_b200.problems.ocp import OptimalControlProblem
+    _, p = _make("quadrotor", batch, N, dtype, device)
+    p = {k: (v.to(dtype) if isinstance(v, torch.Tensor) and v.is_floating_point() else v)
+         for k, v in rescaled(p, 12, 4).items()}
+    p = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in p.items()}
+    p["initial_control"] = torch.tensor([2.0, 2.5, 2.4, 2.6], dtype=dtype, device=device)
+    return OptimalControlProblem(Quadrotor12Dynamics(), p), p
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_rescaled_variables_and_fixed_initial_control_match_oracle(dtype):
+    """rescale_optimization_variables + constrain_initial_control
+    (optimal_control_problem.py:284-325, 914-980): column-scaled QPs with
+    row-scaled constraints and n0 = n initial rows, solved in scaled
+    coordinates and unscaled after each ADMM solve (turbompc_solver.py:1582)."""
+    B, N, sqp, admm, pcg = 3, 20, 3, 30, 30
+    prog64, p64 = _rescaled_quadrotor(B, N, F64, "cpu")
+    s64 = TurboMPCSolver(prog64, _fixed(sqp, admm, pcg))
+    g64 = s64.initial_guess(p64)
+    cfg = _ocfg(admm, pcg)
+    osols = [sr.solve(_oracle_ocp("quadrotor", prog64, p64, b), g64.states[b], g64.controls[b], cfg, sqp)
+             for b in range(B)]
+    prog, params = _rescaled_quadrotor(B, N, dtype, "cuda")
+    s = TurboMPCSolver(prog, _fixed(sqp, admm, pcg), forward_backend="b200")
+    sol = s.solve(s.initial_guess(params), params)
+    _check_solution(sol, osols, dtype, "rescaled + fixed initial control")
+    # the fixed-count ADMM meets the initial-control rows to ~1e-4
+    np.testing.assert_allclose(sol.controls[:, 0].cpu().numpy(), np.tile([2.0, 2.5, 2.4, 2.6], (B, 1)), atol=5e-3)
+    if dtype == torch.float64:
+        x0 = params["initial_state"].detach().clone().requires_grad_(True)
+        u0 = params["initial_control"].detach().clone().requires_grad_(True)
+        wx = params["weights_penalization_reference_state_trajectory"].detach().clone().requires_grad_(True)
+        sol = s.solve(s.initial_guess(params), params, {"initial_state": x0, "initial_control": u0,
+                                                         "weights_penalization_reference_state_trajectory": wx})
+        rng = np.random.default_rng(8)
+        Ws, Wc = rng.normal(size=(B, N + 1, 12)), rng.normal(size=(B, N + 1, 4))
+        tt = lambda a: torch.as_tensor(a, dtype=dtype, device="cuda")
+        loss = (sol.states * tt(Ws)).sum() + (sol.controls * tt(Wc)).sum()
+        gx0, gu0, gwx = torch.autograd.grad(loss, [x0, u0, wx])
+        want = {"x0": [], "u0": 0.0, "wx": 0.0}
+        for b in range(B):
+            g, _ = sr.vjp(_oracle_ocp("quadrotor", prog64, p64, b), osols[b], Ws[b], Wc[b],
+                          weight_keys=(("weights_penalization_reference_state_trajectory",),))
+            want["x0"].append(g["initial_state"])
+            want["u0"] = want["u0"] + g["initial_control"]
+            want["wx"] = want["wx"] + g[("weights_penalization_reference_state_trajectory",)]
+        assert rel_err(gx0.cpu().numpy(), np.stack(want["x0"])) < 1e-6
+        assert rel_err(gu0.cpu().numpy(), want["u0"]) < 1e-6
+        assert rel_err(gwx.cpu().numpy(), want["wx"]) < 1e-6

@@ -98,12 +98,36 @@ def test_terminal_reference_and_linear_weight_in_q():
     np.testing.assert_allclose(q[5, :4].numpy(), -2.0 * 10.0 * r + np.array([1.0, 2.0, 3.0, 4.0]), atol=1e-13)
 
 
+def rescaled(p, nx, nu, u0=True):
+    """Turn on rescale_optimization_variables (and a fixed initial control)."""
+    p = dict(p)
+    p["rescale_optimization_variables"] = True
+    p["state_rescaling_min"] = torch.as_tensor(-np.linspace(1.0, 4.0, nx), dtype=F64)
+    p["state_rescaling_max"] = torch.as_tensor(np.linspace(2.0, 5.0, nx), dtype=F64)
+    p["control_rescaling_min"] = torch.as_tensor(np.linspace(-0.5, 0.0, nu), dtype=F64)
+    p["control_rescaling_max"] = torch.as_tensor(np.linspace(5.0, 6.0, nu), dtype=F64)
+    if u0:
+        p["constrain_initial_control"] = True
+        p["initial_control"] = torch.as_tensor(np.linspace(1.0, 2.0, nu), dtype=F64)
+    return p
+
+
 def _problem(kind, batch, N):
+    from turbompc_b200.dynamics import Quadrotor12Dynamics
     from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    from turbompc_b200.problems.ocp import OptimalControlProblem, OptimalControlProblemObstacle
     from turbompc_b200.problems.quadrotor import make_obstacle_problem, make_quadrotor_problem
     if kind == "quadrotor":
         prog, p = make_quadrotor_problem(batch, N=N, seed=3, dtype=F64, device="cpu")
         return prog, p, dict(model="quadrotor12")
+    if kind == "quadrotor_rescaled":
+        _, p = make_quadrotor_problem(batch, N=N, seed=3, dtype=F64, device="cpu")
+        p = rescaled(p, 12, 4)
+        return OptimalControlProblem(Quadrotor12Dynamics(), p), p, dict(model="quadrotor12")
+    if kind == "obstacles_rescaled":
+        _, p = make_obstacle_problem(batch, N=N, seed=3, dtype=F64, device="cpu")
+        p = rescaled(p, 12, 4, u0=False)
+        return OptimalControlProblemObstacle(Quadrotor12Dynamics(), p), p, dict(model="quadrotor12", obstacles=True)
     if kind == "obstacles":
         prog, p = make_obstacle_problem(batch, N=N, seed=3, dtype=F64, device="cpu")
         return prog, p, dict(model="quadrotor12", obstacles=True)
@@ -111,7 +135,7 @@ def _problem(kind, batch, N):
     return prog, p, dict(model="linear", mlp=True)
 
 
-@pytest.mark.parametrize("kind", ["quadrotor", "obstacles", "cw_mlp"])
+@pytest.mark.parametrize("kind", ["quadrotor", "obstacles", "cw_mlp", "quadrotor_rescaled", "obstacles_rescaled"])
 def test_b200_qp_builder_matches_oracle_qp(kind):
     from turbompc_b200.solver import TurboMPCSolver
     prog, p, kw = _problem(kind, 3, 8)
@@ -119,6 +143,9 @@ def test_b200_qp_builder_matches_oracle_qp(kind):
         p["weights_penalization_control_rate"] = torch.tensor([0.3, 0.1, 0.2, 0.4], dtype=F64)
     s = TurboMPCSolver(prog, {"num_sqp_iteration_max": 1})
     g = s.initial_guess(p)
+    if kind.endswith("rescaled"):
+        assert prog.rescale_optimization_variables
+        assert s._build_qp_data(g.states, g.controls, p).n0 == (16 if kind == "quadrotor_rescaled" else 12)
     gen = torch.Generator().manual_seed(4)
     X = g.states + 0.05 * torch.randn(g.states.shape, generator=gen, dtype=F64)
     U = g.controls + 0.3 * torch.rand(g.controls.shape, generator=gen, dtype=F64)
@@ -220,6 +247,43 @@ def test_oracle_vjp_matches_finite_differences_nonlinear_learned_cost():
         return sr.OCP("linear", 6, 3, p, mlp=True)
 
     _oracle_fd_check(make, key, [0, 7, 13, 30], 12, h=1e-5)
+
+
+@pytest.mark.parametrize("key", ["initial_state", "initial_control", "weights_penalization_control_squared"])
+def test_oracle_vjp_matches_finite_differences_rescaled_with_initial_control(key):
+    """Rescaled variables and a fixed initial control (optimal_control_problem.py:
+    284-325, 914-980; turbompc_solver.py:990-1018)."""
+    def make(w):
+        p = sr.problem_params(rescaled(_di_params(batch=1, N=6, rate=(0.2, 0.0), umax=0.6), 4, 2), 0)
+        p["initial_control"] = torch.tensor([0.3, -0.2], dtype=F64)
+        if w is not None:
+            p = sr._set(p, (key,), w)
+        return sr.OCP("linear", 4, 2, p, eps_abs=1e-9, eps_rel=1e-9)
+
+    o = make(None)
+    assert o.rescale and o.constrain_u0
+    cfg = ref.ADMMConfig(**CONVERGED.__dict__)
+    rng = np.random.default_rng(7)
+    Ws, Wc = rng.normal(size=(o.T, 4)), rng.normal(size=(o.T, 2))
+    X0 = torch.zeros(o.T, 4, dtype=F64)
+    X0[:] = o.p["initial_state"]
+    U0 = torch.zeros(o.T, 2, dtype=F64)
+    sol = sr.solve(o, X0, U0, cfg, 1, linsys="dense")
+    np.testing.assert_allclose(sol.controls[0], [0.3, -0.2], atol=1e-9)  # the initial control is fixed
+    assert (sol.active_lower | sol.active_upper).any()
+    wk = () if key in ("initial_state", "initial_control") else ((key,),)
+    grads, _ = sr.vjp(o, sol, Ws, Wc, weight_keys=wk)
+    g = grads[key] if key in grads else grads[(key,)]
+    base = sr._get(o.p, (key,)).clone()
+    h = 1e-5
+    for i in range(base.numel()):
+        vals = []
+        for sgn in (1, -1):
+            w = base.clone()
+            w.view(-1)[i] += sgn * h
+            vals.append(_loss_and_cot(sr.solve(make(w), X0, U0, cfg, 1, linsys="dense"), Ws, Wc))
+        fd = (vals[0] - vals[1]) / (2 * h)
+        assert abs(float(np.asarray(g).reshape(-1)[i]) - fd) <= 1e-5 * max(1.0, abs(fd)), (key, i, g, fd)
 
 
 def test_oracle_vjp_matches_finite_differences_slack():

@@ -75,7 +75,9 @@ def backward_qp(solver, sol, params, dl_dstates, dl_dcontrols, dl_dslack=None):
     q = -(dL/dz - G_act^T dL/dslack) (turbompc_solver.py:587-605)."""
     prog = solver.program
     kkt = sol.kkt_state
-    qp = solver._build_qp_data(kkt.states, kkt.controls, params)
+    # true (unscaled) variables: cotangents are taken w.r.t. them; the
+    # problem's row scaling of the constraints stays (turbompc_solver.py:553-560)
+    qp = solver._build_qp_data(kkt.states, kkt.controls, params, apply_variable_scaling=False)
     D = qp.cost.D
     if solver._use_full_hessian:
         D = D + prog.get_dynamics_lagrangian_hessian(kkt.states, kkt.controls, params, sol.admm_state.y_f_dyn)
@@ -137,8 +139,12 @@ class _SolveFn(torch.autograd.Function):
             dz, mult = dz.to(dt), mult.to(dt)
         nx = prog.num_state_variables
         Nb, T = sol.states.shape[0], sol.states.shape[1]
-        n_eq = bq.n0 + (T - 1) * nx
-        y_eq_lin = mult[:, :n_eq]
+        n0 = bq.n0
+        n_eq = n0 + (T - 1) * nx
+        # equality_constraints orders its rows [x0, dynamics, u0]; the KKT
+        # system orders them [A0 rows (x0 then u0), dynamics]
+        # (turbompc_solver.py:736-744)
+        y_eq_lin = torch.cat([mult[:, :nx], mult[:, n0:n_eq], mult[:, nx:n0]], 1)
         st = sol.admm_state
         lo_m, up_m = kkt.ineq_active_lower_idx.to(dt), kkt.ineq_active_upper_idx.to(dt)
         sign = lo_m - up_m
@@ -153,7 +159,7 @@ class _SolveFn(torch.autograd.Function):
             dL_dgamma = (sign * st.xi_g * act * g_dx).sum((-1, -2))
         else:
             y_ineq_lin = mult[:, n_eq:].reshape(Nb, T, m)
-        y_eq_star = torch.cat([st.y_f_0, st.y_f_dyn.reshape(Nb, -1)], 1)
+        y_eq_star = torch.cat([st.y_f_0[:, :nx], st.y_f_dyn.reshape(Nb, -1), st.y_f_0[:, nx:]], 1)
         y_ineq_star = -sign * st.y_g
 
         with torch.enable_grad():

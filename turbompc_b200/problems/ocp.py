@@ -18,7 +18,17 @@ problem and stage).  Required keys:
 Optional: state_min_bounds / state_max_bounds / control_min_bounds /
 control_max_bounds, weights_linear_penalization_final_state,
 dynamics_state_dot_params (dict of tensors broadcast against (Nb, N, ...)),
-use_slack_variables, slack_penalization_weight.
+use_slack_variables, slack_penalization_weight,
+rescale_optimization_variables with state_rescaling_min / _max (nx,) and
+control_rescaling_min / _max (nu,) (optimal_control_problem.py:284-325),
+constrain_initial_control with initial_control ((nu,) or (Nb, nu);
+optimal_control_problem.py:914-980).
+
+With rescaling, the constraint rows this class returns are row-scaled as the
+reference's are (dynamics and initial rows by 1 / state_diff, the initial
+control rows by 1 / control_diff, box rows by 1 / their variable's scale,
+obstacle rows by 1 / mean(state_diff[:dim])); the solver then applies the
+column scaling z = diag(state_diff, control_diff) z_hat (qp_data.py:178-210).
 """
 from __future__ import annotations
 
@@ -59,6 +69,12 @@ class OptimalControlProblem:
             raise NotImplementedError("implicit trapezoid integration is not supported by the b200 backend")
         self._use_slack = bool(params.get("use_slack_variables", False))
         self._penalize_control_reference = bool(params.get("penalize_control_reference", False))
+        self._rescale = bool(params.get("rescale_optimization_variables", False))
+        self._constrain_u0 = bool(params.get("constrain_initial_control", False))
+        if self._constrain_u0 and "initial_control" not in params:
+            raise ValueError("initial_control must be provided when constrain_initial_control is True.")
+        if self._rescale:
+            self.rescaling(params, torch.zeros(1, dtype=torch.float64))  # shape checks
         self._set_active_bounds(params)
 
     # ------------------------------------------------------------------ sizes
@@ -88,11 +104,54 @@ class OptimalControlProblem:
 
     @property
     def constrain_initial_control(self) -> bool:
-        return False
+        return self._constrain_u0
 
     @property
     def rescale_optimization_variables(self) -> bool:
-        return False
+        return self._rescale
+
+    @property
+    def num_initial_equalities(self) -> int:
+        """Rows of A0: nx, or nx + nu with a fixed initial control."""
+        return self.num_state_variables + (self.num_control_variables if self._constrain_u0 else 0)
+
+    # ------------------------------------------------------------ rescaling
+    def rescaling(self, params, like):
+        """(state_diff (nx,), control_diff (nu,)) with x = state_diff * x_hat,
+        u = control_diff * u_hat; ones without rescaling
+        (optimal_control_problem.py:284-325)."""
+        nx, nu = self.num_state_variables, self.num_control_variables
+        if not self._rescale:
+            return (torch.ones(nx, dtype=like.dtype, device=like.device),
+                    torch.ones(nu, dtype=like.dtype, device=like.device))
+        vals = {}
+        for k, dim in (("state_rescaling_min", nx), ("state_rescaling_max", nx), ("control_rescaling_min", nu),
+                       ("control_rescaling_max", nu)):
+            if k not in params:
+                raise KeyError(f"{k} is required with rescale_optimization_variables")
+            v = _t(params[k], like)
+            if tuple(v.shape) != (dim,):
+                raise ValueError(f"{k} must have shape ({dim},), got {tuple(v.shape)}")
+            vals[k] = v
+        return ((vals["state_rescaling_max"] - vals["state_rescaling_min"]) / 2.0,
+                (vals["control_rescaling_max"] - vals["control_rescaling_min"]) / 2.0)
+
+    def scale_states_controls(self, states, controls, params):
+        sd, cd = self.rescaling(params, states)
+        return states / sd, controls / cd
+
+    def unscale_states_controls(self, states, controls, params):
+        sd, cd = self.rescaling(params, states)
+        return states * sd, controls * cd
+
+    def dynamics_plus_rows(self, params, like, Nb):
+        """A_plus = -[I 0] (the coefficient of z_{t+1} in the explicit-scheme
+        dynamics rows), row-scaled like A_minus."""
+        nx, nu, N = self.num_state_variables, self.num_control_variables, self.horizon
+        sd, _ = self.rescaling(params, like)
+        Ap = torch.zeros(Nb, N, nx, nx + nu, dtype=like.dtype, device=like.device)
+        Ap[..., :nx] = -torch.diag(1.0 / sd)
+        return Ap
 
     @property
     def num_inequality_constraints(self) -> int:
@@ -170,8 +229,12 @@ class OptimalControlProblem:
         if spec is not None and self._scheme in (DiscretizationScheme.EULER, DiscretizationScheme.MIDPOINT,
                                                  DiscretizationScheme.RUNGEKUTTA4):
             from .. import ops
-            return ops.linearize_dynamics(spec[0], spec[1], int(self._scheme),
-                                          float(params["discretization_resolution"]), states, controls)
+            Am, c = ops.linearize_dynamics(spec[0], spec[1], int(self._scheme),
+                                           float(params["discretization_resolution"]), states, controls)
+            if self._rescale:
+                rs = 1.0 / self.rescaling(params, states)[0]
+                Am, c = (Am * rs[:, None]).contiguous(), (c * rs).contiguous()
+            return Am, c
         _, _, As, Bs, Cs = self.get_dynamics_linearized_matrices(states, controls, params)
         return torch.cat([As, Bs], dim=-1).contiguous(), Cs[:, 1:].contiguous()
 
@@ -199,6 +262,9 @@ class OptimalControlProblem:
         eye = torch.eye(nx, dtype=states.dtype, device=states.device)
         As_next = (-eye).expand(states.shape[0], N, nx, nx)
         Bs_next = torch.zeros_like(Bs)
+        if self._rescale:  # row scaling 1 / state_diff (optimal_control_problem.py:1322-1331)
+            rs = 1.0 / self.rescaling(params, states)[0]
+            As_next, As, Bs, Cs = As_next * rs[:, None], As * rs[:, None], Bs * rs[:, None], Cs * rs
         return As_next, Bs_next, As, Bs, Cs
 
     # ----------------------------------------------------------------- cost
@@ -297,15 +363,30 @@ class OptimalControlProblem:
                          1)
         Gbox = torch.cat([sel, selu], 0).expand(Nb, T, -1, n)
         lo, hi = self._box(params, states, Nb, T)
+        if self._rescale:  # g / scale (optimal_control_problem.py:460-469)
+            bs = self._box_scale(params, states)
+            Gbox, lo, hi = Gbox / bs[:, None], lo / bs, hi / bs
         extra = self._extra_inequalities_linearized(states, controls, params)
         if extra is None:
             return Gbox.contiguous(), lo.contiguous(), hi.contiguous()
         Ge, le, ue = extra
+        if self._rescale:
+            es = self._extra_row_scale(params, states)
+            Ge, le, ue = Ge * es, le * es, ue * es
         return (torch.cat([Gbox, Ge], 2).contiguous(), torch.cat([lo, le], 2).contiguous(),
                 torch.cat([hi, ue], 2).contiguous())
 
     def _extra_inequalities_linearized(self, states, controls, params):
         return None
+
+    def _box_scale(self, params, like):
+        """Scale of each active box row (its variable's state / control diff)."""
+        sd, cd = self.rescaling(params, like)
+        return torch.cat([sd[self._state_mask.to(like.device)], cd[self._control_mask.to(like.device)]])
+
+    def _extra_row_scale(self, params, like):
+        """Row scale of the extra (nonlinear) inequality rows under rescaling."""
+        return 1.0
 
     # ------------------------------------- nonlinear constraint functions (backward)
     def equality_constraints(self, states, controls, params):
@@ -314,7 +395,12 @@ class OptimalControlProblem:
         its Jacobian is the QP's [A0; A_minus/A_plus] rows."""
         x0c = states[:, 0] - _t(params["initial_state"], states)
         dyn = self.next_states(states, controls, params) - states[:, 1:]
-        return torch.cat([x0c, dyn.reshape(states.shape[0], -1)], dim=1)
+        sd, cd = self.rescaling(params, states)
+        rows = torch.cat([x0c[:, None], dyn], 1) / sd
+        out = [rows.reshape(states.shape[0], -1)]
+        if self._constrain_u0:  # appended last, as optimal_control_problem.py:895-910
+            out.append((controls[:, 0] - _t(params["initial_control"], states)) / cd)
+        return torch.cat(out, dim=1)
 
     def inequality_values(self, states, controls, params):
         """Nonlinear g(x, u) with its bounds, each (Nb, T, m), in the row order of
@@ -325,11 +411,15 @@ class OptimalControlProblem:
         sm, cm = self._state_mask.to(states.device), self._control_mask.to(states.device)
         g = torch.cat([states[..., sm], controls[..., cm]], -1)
         lo, hi = self._box(params, states, Nb, T)
+        if self._rescale:
+            bs = self._box_scale(params, states)
+            g, lo, hi = g / bs, lo / bs, hi / bs
         extra = self._extra_inequality_values(states, controls, params)
         if extra is not None:
-            g = torch.cat([g, extra[0]], -1)
-            lo = torch.cat([lo, extra[1]], -1)
-            hi = torch.cat([hi, extra[2]], -1)
+            es = self._extra_row_scale(params, states) if self._rescale else 1.0
+            g = torch.cat([g, extra[0] * es], -1)
+            lo = torch.cat([lo, extra[1] * es], -1)
+            hi = torch.cat([hi, extra[2] * es], -1)
         del z, nx
         return g, lo, hi
 
@@ -365,8 +455,11 @@ class OptimalControlProblem:
         dp = self._dyn_params(params, states)
         lam = lambdas.detach()
 
+        rs = 1.0 / self.rescaling(params, states)[0]
+
         def fn(zz):
-            return (lam * predict_next_state(self._dynamics, dt, self._scheme, dp, zz[..., :nx], zz[..., nx:])).sum(-1)
+            return (lam * rs * predict_next_state(self._dynamics, dt, self._scheme, dp, zz[..., :nx],
+                                                  zz[..., nx:])).sum(-1)
 
         z = torch.cat([states[:, :N], controls[:, :N]], -1).detach()
         H = self._stagewise_hessian(fn, z)
@@ -385,12 +478,22 @@ class OptimalControlProblem:
         return self._stagewise_hessian(fn, z)
 
     def get_initial_equality_linearized_matrices(self, params, like):
-        """A0 = [I 0], c0 = initial_state (optimal_control_problem.py:914-980)."""
+        """A0 = [I 0], c0 = initial_state, plus [0 I], initial_control with a
+        fixed initial control; row-scaled under rescaling
+        (optimal_control_problem.py:914-980)."""
         nx, nu = self.num_state_variables, self.num_control_variables
-        x0 = params["initial_state"]
-        A0 = torch.cat([torch.eye(nx, dtype=like.dtype, device=like.device),
-                        torch.zeros(nx, nu, dtype=like.dtype, device=like.device)], 1)
-        return A0.expand(x0.shape[0], nx, nx + nu).contiguous(), _t(x0, like).contiguous()
+        x0 = _t(params["initial_state"], like)
+        Nb = x0.shape[0]
+        sd, cd = self.rescaling(params, like)
+        A0 = torch.cat([torch.diag(1.0 / sd), torch.zeros(nx, nu, dtype=like.dtype, device=like.device)], 1)
+        A0 = A0.expand(Nb, nx, nx + nu)
+        c0 = x0 / sd
+        if self._constrain_u0:
+            Au = torch.cat([torch.zeros(nu, nx, dtype=like.dtype, device=like.device), torch.diag(1.0 / cd)], 1)
+            A0 = torch.cat([A0, Au.expand(Nb, nu, nx + nu)], 1)
+            u0 = _t(params["initial_control"], like).expand(Nb, nu)
+            c0 = torch.cat([c0, u0 / cd], 1)
+        return A0.contiguous(), c0.contiguous()
 
 
 class OptimalControlProblemObstacle(OptimalControlProblem):
@@ -429,3 +532,8 @@ class OptimalControlProblemObstacle(OptimalControlProblem):
         lo = torch.full_like(g, -1e9) - off
         hi = torch.zeros_like(g) - off
         return G, lo, hi
+
+    def _extra_row_scale(self, params, like):
+        """obstacle_avoidance.py:40-45: 1 / mean(state_diff[:dim])."""
+        dim = int(params["obstacles_dimension"])
+        return 1.0 / self.rescaling(params, like)[0][:dim].mean()

@@ -23,7 +23,8 @@ import torch
 
 from . import ops
 from .ops import ADMMState, AdmmConfig
-from .qp_data import QPCostBlocks, QPData, QPEqualityBlocks, QPInequalityBlocks, qpdata_from_ocp_blocks
+from .qp_data import (QPCostBlocks, QPData, QPEqualityBlocks, QPInequalityBlocks, qpdata_from_ocp_blocks,
+                      scale_qp_data)
 
 DEFAULT_SOLVER_PARAMS: Dict[str, Any] = {
     # turbompc/solvers/params/turbompc.yaml:1-23
@@ -249,34 +250,55 @@ class TurboMPCSolver:
         return make_differentiable_solve(self)
 
     # ------------------------------------------------------------ QP build
-    def _build_qp_data(self, states, controls, params, prev: Optional[QPData] = None) -> QPData:
+    def _build_qp_data(self, states, controls, params, prev: Optional[QPData] = None,
+                       apply_variable_scaling: bool = True) -> QPData:
         """turbompc_solver.py:1098-1156.  With ``prev`` (the previous SQP
         iterate's QP of the same solve) the blocks that do not depend on the
         linearisation point are reused: the tracking cost (D, E, q), the
-        initial-state rows (A0, c0), A_plus = [-I 0] and, without extra
-        nonlinear inequalities, the box rows (G, l, u).  The dynamics rows
-        (A_minus, c) are recomputed."""
+        initial rows (A0, c0), A_plus = -[I 0] and, without extra nonlinear
+        inequalities, the box rows (G, l, u).  The dynamics rows (A_minus, c)
+        are recomputed.  With the problem's rescale_optimization_variables
+        and apply_variable_scaling, the column scaling z = diag(state_diff,
+        control_diff) z_hat is applied (qp_data.py:178-210); the constraint
+        rows come row-scaled from the problem either way."""
         prog = self._program
         A_minus, c_dyn = prog.linearized_dynamics_rows(states, controls, params)
+        scale = apply_variable_scaling and getattr(prog, "rescale_optimization_variables", False)
+        col = None
+        if scale:
+            sd, cd = prog.rescaling(params, states)
+            col = torch.cat([sd, cd])
         if prev is not None and getattr(prog, "state_independent_cost", False):
             ineq = prev.ineq
             if not prog.state_independent_inequalities:
                 G, l, u = prog.get_inequalities_linearized_matrices(states, controls, params)
+                if col is not None:
+                    G = G * col
                 ineq = QPInequalityBlocks(G.contiguous(), l.contiguous(), u.contiguous(),
                                           prev.ineq.slack_penalization_weight, prev.ineq.use_slack_variables)
+            if col is not None:
+                A_minus = (A_minus * col).contiguous()
             return QPData(prev.cost, QPEqualityBlocks(prev.eq.A0, A_minus, prev.eq.A_plus, prev.eq.c0, c_dyn), ineq)
         D, E, q = prog.get_cost_linearized_blocks(states, controls, params)
         G, l, u = prog.get_inequalities_linearized_matrices(states, controls, params)
         A0, c0 = prog.get_initial_equality_linearized_matrices(params, states)
-        Nb, T, nx = states.shape
-        A_plus = torch.zeros_like(A_minus)
-        A_plus[..., :nx] = -torch.eye(nx, dtype=states.dtype, device=states.device)
+        Nb = states.shape[0]
+        if hasattr(prog, "dynamics_plus_rows"):
+            A_plus = prog.dynamics_plus_rows(params, states, Nb)
+        else:
+            nx = states.shape[-1]
+            A_plus = torch.zeros_like(A_minus)
+            A_plus[..., :nx] = -torch.eye(nx, dtype=states.dtype, device=states.device)
         sw = params.get("slack_penalization_weight", None)
         if sw is not None:
             sw = torch.as_tensor(sw, dtype=states.dtype, device=states.device).expand(states.shape[0]).contiguous()
         c = lambda t: t.contiguous()
-        return QPData(QPCostBlocks(c(D), c(E), c(q)), QPEqualityBlocks(c(A0), A_minus, A_plus, c(c0), c_dyn),
-                      QPInequalityBlocks(c(G), c(l), c(u), sw, prog.use_slack_variables))
+        qp = QPData(QPCostBlocks(c(D), c(E), c(q)), QPEqualityBlocks(c(A0), A_minus, A_plus, c(c0), c_dyn),
+                    QPInequalityBlocks(c(G), c(l), c(u), sw, prog.use_slack_variables))
+        if scale:
+            sd, cd = prog.rescaling(params, states)
+            qp = scale_qp_data(qp, sd, cd).map(lambda t: t.contiguous())
+        return qp
 
     def _first_order_error(self, qp: QPData, states, controls, slacks, st: ADMMState):
         """turbompc_solver.py:1158-1225 (first_order criterion): the fused CUDA
@@ -318,7 +340,8 @@ class TurboMPCSolver:
 
     def _build_kkt_state(self, states, controls, st: ADMMState, g, l, u) -> KKTState:
         """turbompc_solver.py:1387-1439."""
-        y_f = torch.cat([st.y_f_0[:, None, :], st.y_f_dyn], 1)
+        nx = self._program.num_state_variables
+        y_f = torch.cat([st.y_f_0[:, None, :nx], st.y_f_dyn], 1)
         y_ineq = st.y_g
         slack = st.xi_g
         a = self._params["admm"]
@@ -358,13 +381,16 @@ class TurboMPCSolver:
         kkt = None
         sw = qp.ineq.slack_penalization_weight
         kstatus = torch.zeros(Nb, dtype=torch.int32, device=dev)
+        rescale = bool(getattr(self._program, "rescale_optimization_variables", False))
         for k in range(max_iter):
             if k > 0 and tol > 0 and not bool(active.any()):
                 break
             st_new, iters, status = ops.admm_solve(qp, st, cfg, slack_weight=sw, workspace=self._workspace)
             kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
-            xb = st_new.x_blocks
+            xb = st_new.x_blocks  # QP (scaled) coordinates
             s_new, c_new = xb[..., :nx], xb[..., nx:]
+            if rescale:
+                s_new, c_new = self._program.unscale_states_controls(s_new, c_new, params)
             sl_new = st_new.xi_g
             z_new = torch.cat([s_new, c_new], -1)
             step = _inf(z_new - z_prev)
@@ -373,18 +399,18 @@ class TurboMPCSolver:
             if crit == "first_order":
                 if k + 1 < max_iter:
                     qp_next = self._build_qp_data(s_new, c_new, params, prev=qp)
-                    cv, ev, iv, g = self._first_order_error(qp_next, s_new, c_new, sl_new, st_new)
+                    cv, ev, iv, g = self._first_order_error(qp_next, xb[..., :nx], xb[..., nx:], sl_new, st_new)
                 else:
                     qp_next = qp
                     cv = step if k == 0 else conv
                     ev = iv = torch.zeros_like(cv)
-                    g = torch.einsum("btki,bti->btk", qp.ineq.G, z_new)
+                    g = torch.einsum("btki,bti->btk", qp.ineq.G, xb)
                     if qp.ineq.use_slack_variables:
                         g = g + sl_new
             else:
                 qp_next = self._build_qp_data(s_new, c_new, params, prev=qp) if k + 1 < max_iter else qp
                 cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), torch.einsum(
-                    "btki,bti->btk", qp_next.ineq.G, z_new)
+                    "btki,bti->btk", qp_next.ineq.G, xb)
             kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
             # Masked update (problems already converged keep their iterate).
             a3 = active[:, None, None]
