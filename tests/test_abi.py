@@ -52,3 +52,22 @@ def test_interleaved_sizes_without_gpu():
     assert lib.tmpc_interleaved_elems(0, 10) == 0
     d = _ffi.TmpcDims(5, 4, 3, 2, 0, 0)  # T = 4, n = 3: 4 * 6 + 3 * 9
     assert lib.tmpc_riccati_il_elems_per_problem(C.byref(d)) == 4 * 6 + 3 * 9
+
+
+def test_ffi_handlers_compile_to_nothing_without_xla_headers(tmp_path):
+    """csrc/ffi/admm_b200_ffi.cc is guarded by __has_include on the jaxlib
+    FFI header: without it (here) it must still compile, to an empty object."""
+    import shutil
+    import subprocess
+    from turbompc_b200 import build
+    gxx = shutil.which("g++")
+    if gxx is None:
+        import pytest
+        pytest.skip("no g++")
+    obj = tmp_path / "ffi.o"
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(build.nvcc())), "include")
+    res = subprocess.run([gxx, "-std=c++17", "-c", build.FFI_SRC, "-I" + build.INCLUDE, "-I" + cuda_inc, "-o",
+                          str(obj)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    nm = subprocess.run(["nm", str(obj)], capture_output=True, text=True).stdout
+    assert "AdmmB200Cuda" not in nm

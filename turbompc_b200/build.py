@@ -93,9 +93,35 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     return LIB
 
 
+FFI_SRC = os.path.join(CSRC, "ffi", "admm_b200_ffi.cc")
+FFI_LIB = os.path.join(LIBDIR, "libtmpc_b200_ffi.so")
+
+
+def build_ffi(xla_include: str) -> str:
+    """Compile the XLA FFI handlers (csrc/ffi/admm_b200_ffi.cc) against the
+    jaxlib FFI headers in ``xla_include`` (``jax.ffi.include_dir()``) into
+    _lib/libtmpc_b200_ffi.so, linked to the main library.  Only where jaxlib
+    is installed; the handlers compile to nothing without its headers."""
+    if not os.path.exists(os.path.join(xla_include, "xla", "ffi", "api", "ffi.h")):
+        raise RuntimeError(f"no XLA FFI headers under {xla_include}")
+    build()
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-I" + xla_include, "-I" + INCLUDE, "-I" + cuda_inc,
+           FFI_SRC, "-o", FFI_LIB, "-L" + LIBDIR, "-ltmpc_b200", "-Wl,-rpath,$ORIGIN",
+           "-L" + os.path.join(os.path.dirname(cuda_inc), "lib64"), "-lcudart"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"FFI build failed:\n{res.stdout}\n{res.stderr}")
+    return FFI_LIB
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ffi", metavar="XLA_INCLUDE", default="",
+                    help="also build the XLA FFI handlers against these jaxlib headers")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    if a.ffi:
+        print(build_ffi(a.ffi))

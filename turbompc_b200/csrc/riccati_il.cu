@@ -24,9 +24,11 @@
 // This is the direct solve that replaces the reference's cuDSS path
 // (turbompc/solvers/linear_systems_solvers/csrc/cudss_blktridi.cu:60-184).
 //
-// Each thread keeps its stage's working matrix (packed lower, NB(NB+1)/2
-// values) in registers and runs the Cholesky fully unrolled there; W_{t-1} is
-// re-read from the factor it has just written (an L2 hit).  Block sizes are
+// Factor: each thread keeps its stage's working matrix (packed lower,
+// NB(NB+1)/2 values) in registers and runs the Cholesky fully unrolled there;
+// W_{t-1} is re-read from the factor it has just written (an L2 hit).
+// Solve: four warps per group of 32 problems, each owning a quarter of the
+// rows (see solve_kernel).  Block sizes are
 // compiled for NB in {4, 8, 12, 16} (fp64: up to 12); n < NB is padded with an
 // identity diagonal in registers only (memory holds exact n x n blocks).
 #include "tmpc_common.cuh"
@@ -160,8 +162,11 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* __restri
   }
 }
 
+#ifndef TMPC_IL_FACTOR_MINB
+#define TMPC_IL_FACTOR_MINB 1
+#endif
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, R* __restrict__ factor,
+__global__ void __launch_bounds__(128, TMPC_IL_FACTOR_MINB) factor_kernel(const R* __restrict__ ops, R* __restrict__ factor,
                                                      int32_t* status, int Nb,
                                                      int T, int n) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -175,86 +180,116 @@ __global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, 
 }
 
 // ---------------------------------------------------------------------------
-// Solve S x = b with the factor: one problem per thread.  The forward sweep
-// writes y into x_out (same slots), which the backward sweep reads back.
+// Solve S x = b with the factor.  One block of four warps per group of 32
+// problems: lane l of every warp works on problem l of the group, and warp w
+// owns rows [w NB/4, (w+1) NB/4) of every stage's products, so each problem's
+// rows are spread over four threads (four times the memory-level parallelism
+// of one thread per problem).  The stage vectors a product needs in full go
+// through shared memory, [row][lane], between barriers.  The forward sweep
+// writes y into x_out (the same slots, by the thread that owns the row),
+// which the backward sweep reads back.
 // ---------------------------------------------------------------------------
+constexpr int kSolveWarps = 4;
+
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) solve_kernel(const R* __restrict__ factor, const R* __restrict__ rhs,
-                                                    R* __restrict__ x_out,
-                                                    int Nb, int T, int n) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= Nb) return;  // no warp-wide operation below: lanes past the batch leave at once
+__global__ void __launch_bounds__(32 * kSolveWarps) solve_kernel(const R* __restrict__ factor,
+                                                                 const R* __restrict__ rhs, R* __restrict__ x_out,
+                                                                 int Nb, int T, int n) {
+  constexpr int RPW = NB / kSolveWarps;  // rows per warp
+  __shared__ R ush[NB][kWarp];           // the vector being multiplied
+  __shared__ R vsh[NB][kWarp];           // y_{t-1} (forward) / x_{t+1} (backward)
+  const int lane = threadIdx.x & (kWarp - 1), w = threadIdx.x / kWarp;
+  const size_t grp = blockIdx.x;
+  const bool valid = grp * kWarp + lane < (size_t)Nb;
   const size_t trin = tri(n), nn = (size_t)n * n;
   const size_t woff = (size_t)T * trin;
-  const size_t fb = (size_t)(b / kWarp) * op_elems(T, n) * kWarp + (b % kWarp);
-  const size_t vb = (size_t)(b / kWarp) * T * n * kWarp + (b % kWarp);
-  const R* F = factor + fb;
-  const R* bv = rhs + vb;
-  R* xv = x_out + vb;
+  const R* F = factor + grp * op_elems(T, n) * kWarp + lane;
+  const R* bv = rhs + grp * (size_t)T * n * kWarp + lane;
+  R* xv = x_out + grp * (size_t)T * n * kWarp + lane;
+  const int r0 = w * RPW;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) vsh[r0 + r][lane] = R(0);
+  __syncthreads();
+  // Every factor row a thread needs in a stage is loaded into registers at
+  // the top of the stage, before the barriers, so a stage costs one memory
+  // latency (the compiler does not move loads across __syncthreads).
   // forward: y_t = L_t^-1 (b_t - W_{t-1} y_{t-1})
-  R yp[NB];
-#pragma unroll
-  for (int k = 0; k < NB; ++k) yp[k] = R(0);
   for (int t = 0; t < T; ++t) {
-    R u[NB];
-#pragma unroll
-    for (int k = 0; k < NB; ++k) u[k] = (k < n) ? ldro(bv + ((size_t)t * n + k) * kWarp) : R(0);
-    if (t > 0) {
-      const R* W = F + (woff + (size_t)(t - 1) * nn) * kWarp;
-#pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        if (i < n) {
-          R s = R(0);
-#pragma unroll
-          for (int k = 0; k < NB; ++k)
-            if (k < n) s = fma(ldro(W + ((size_t)i * n + k) * kWarp), yp[k], s);
-          u[i] -= s;
-        }
-      }
-    }
+    const R* W = F + (woff + (size_t)(t > 0 ? t - 1 : 0) * nn) * kWarp;
     const R* X = F + (size_t)t * trin * kWarp;  // L_t^-1
+    R wr[RPW][NB], xr[RPW][NB], bi[RPW];
 #pragma unroll
-    for (int k = 0; k < NB; ++k) {
-      R acc = R(0);
-      if (k < n) {
+    for (int r = 0; r < RPW; ++r) {
+      const int i = r0 + r;
+      const bool on = i < n && valid;
+      bi[r] = on ? ldro(bv + ((size_t)t * n + i) * kWarp) : R(0);
 #pragma unroll
-        for (int c = 0; c <= k; ++c) acc = fma(ldro(X + (size_t)LI(k, c) * kWarp), u[c], acc);
-        xv[((size_t)t * n + k) * kWarp] = acc;
+      for (int k = 0; k < NB; ++k) {
+        wr[r][k] = (on && t > 0 && k < n) ? ldro(W + ((size_t)i * n + k) * kWarp) : R(0);
+        xr[r][k] = (on && k <= i) ? ldro(X + (size_t)LI(i, k) * kWarp) : R(0);
       }
-      yp[k] = acc;
     }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      R u = bi[r];
+#pragma unroll
+      for (int k = 0; k < NB; ++k) u = fma(-wr[r][k], vsh[k][lane], u);
+      ush[r0 + r][lane] = u;
+    }
+    __syncthreads();
+    R y[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      R acc = R(0);
+#pragma unroll
+      for (int c = 0; c < NB; ++c) acc = fma(xr[r][c], ush[c][lane], acc);
+      y[r] = acc;
+      if (r0 + r < n && valid) xv[((size_t)t * n + r0 + r) * kWarp] = acc;
+    }
+    __syncthreads();  // every read of ush / vsh of this stage is done
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) vsh[r0 + r][lane] = y[r];
   }
-  // backward: x_t = L_t^-T (y_t - W_t^T x_{t+1})
-  R xp[NB];
 #pragma unroll
-  for (int k = 0; k < NB; ++k) xp[k] = R(0);
+  for (int r = 0; r < RPW; ++r) vsh[r0 + r][lane] = R(0);
+  __syncthreads();
+  // backward: x_t = L_t^-T (y_t - W_t^T x_{t+1}); thread row k needs column k
+  // of W_t and column k of L_t^-1
   for (int t = T - 1; t >= 0; --t) {
-    R u[NB];
+    const R* W = F + (woff + (size_t)(t < T - 1 ? t : 0) * nn) * kWarp;
+    const R* X = F + (size_t)t * trin * kWarp;
+    R wc[RPW][NB], xc[RPW][NB], yi[RPW];
 #pragma unroll
-    for (int k = 0; k < NB; ++k) u[k] = (k < n) ? xv[((size_t)t * n + k) * kWarp] : R(0);
-    if (t < T - 1) {
-      const R* W = F + (woff + (size_t)t * nn) * kWarp;
+    for (int r = 0; r < RPW; ++r) {
+      const int k = r0 + r;
+      const bool on = k < n && valid;
+      yi[r] = on ? xv[((size_t)t * n + k) * kWarp] : R(0);
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
-        if (i < n) {
-#pragma unroll
-          for (int k = 0; k < NB; ++k)
-            if (k < n) u[k] = fma(-ldro(W + ((size_t)i * n + k) * kWarp), xp[i], u[k]);
-        }
+        wc[r][i] = (on && t < T - 1 && i < n) ? ldro(W + ((size_t)i * n + k) * kWarp) : R(0);
+        xc[r][i] = (on && i >= k && i < n) ? ldro(X + (size_t)LI(i, k) * kWarp) : R(0);
       }
     }
-    const R* X = F + (size_t)t * trin * kWarp;  // L_t^-1; x = (L_t^-1)^T u
 #pragma unroll
-    for (int c = 0; c < NB; ++c) {
+    for (int r = 0; r < RPW; ++r) {
+      R u = yi[r];
+#pragma unroll
+      for (int i = 0; i < NB; ++i) u = fma(-wc[r][i], vsh[i][lane], u);
+      ush[r0 + r][lane] = u;
+    }
+    __syncthreads();
+    R x[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
       R acc = R(0);
-      if (c < n) {
 #pragma unroll
-        for (int k = c; k < NB; ++k)
-          if (k < n) acc = fma(ldro(X + (size_t)LI(k, c) * kWarp), u[k], acc);
-        xv[((size_t)t * n + c) * kWarp] = acc;
-      }
-      xp[c] = acc;
+      for (int i = 0; i < NB; ++i) acc = fma(xc[r][i], ush[i][lane], acc);
+      x[r] = acc;
+      if (r0 + r < n && valid) xv[((size_t)t * n + r0 + r) * kWarp] = acc;
     }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) vsh[r0 + r][lane] = x[r];
   }
 }
 
@@ -394,8 +429,8 @@ int solve(const TmpcDims* d, const R* fac, const R* rhs, R* x, cudaStream_t st) 
   if (!fac || !rhs || !x) return TMPC_ERR_NULL_ARG;
   return dispatch_il<R>(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    const int grid = (d->Nb + 127) / 128;
-    solve_kernel<NB, R><<<grid, 128, 0, st>>>(fac, rhs, x, d->Nb, d->T, d->n);
+    const int grid = (int)groups(d->Nb);  // one block of kSolveWarps warps per group of 32 problems
+    solve_kernel<NB, R><<<grid, 32 * kSolveWarps, 0, st>>>(fac, rhs, x, d->Nb, d->T, d->n);
     return (int)cudaPeekAtLastError();
   });
 }
