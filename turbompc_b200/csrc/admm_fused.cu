@@ -6,6 +6,7 @@ namespace tmpc {
 
 template <typename R>
 size_t admm_ws_bytes(const TmpcDims& d) {
+  if (d.n > 32) return admm_generic_ws_bytes<R>(d);
   size_t out = 0;
   dispatch_nb(d.n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
@@ -20,6 +21,7 @@ size_t admm_ws_bytes(const TmpcDims& d) {
 template <typename R>
 size_t admm_ws_bytes_cfg(const TmpcDims& d, const TmpcAdmmConfig* cfg) {
   if (!cfg || cfg->linsys != TMPC_LINSYS_DIRECT) return admm_ws_bytes<R>(d);
+  if (d.n > 32) return 0;  // the direct solve is compiled for n <= 32
   size_t out = 0;
   dispatch_nb(d.n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
@@ -64,6 +66,10 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
   if constexpr (std::is_same<R, float>::value) {
     if (cfg->linsys == TMPC_LINSYS_PCG && admm_rows_ok(d->T, d->n, d->nx, d->n0, d->m))
       return launch_admm_rows(P, st);
+  }
+  if (d->n > 32) {  // stage blocks wider than 32: operators in the workspace (admm_generic.cu)
+    if (cfg->linsys == TMPC_LINSYS_DIRECT) return TMPC_ERR_UNSUPPORTED;
+    return launch_admm_generic<R>(P, ws_bytes, st);
   }
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;

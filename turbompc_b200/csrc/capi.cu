@@ -33,7 +33,10 @@ const char* tmpc_error_string(int32_t code) {
     case TMPC_OK: return "ok";
     case TMPC_ERR_NULL_ARG: return "null pointer argument";
     case TMPC_ERR_BAD_DIMS: return "invalid dimensions";
-    case TMPC_ERR_UNSUPPORTED: return "unsupported configuration (block size n > 32 or unknown option)";
+    case TMPC_ERR_UNSUPPORTED:
+      return "unsupported configuration (block size n beyond the entry point's limit: 96 for the fused PCG "
+             "solve and the reference-layout assembly / PCG, 32 for the other operator formats and the direct "
+             "solve; or an unknown option)";
     case TMPC_ERR_WORKSPACE: return "workspace or factor buffer missing, too small or not 16-byte aligned";
     case TMPC_ERR_SMEM: return "problem does not fit the shared-memory budget of one CTA";
     case TMPC_ERR_SCRATCH_LIMIT:

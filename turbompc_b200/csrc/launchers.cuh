@@ -26,6 +26,15 @@ template <int NB, typename R>
 int launch_pcg_packed(const TmpcDims* d, const R* o, const R* rhs, const R* x0, R* xo, uint32_t* it, R eps,
                       int max_iter, cudaStream_t st);
 
+// Stage blocks wider than 32 (32 < n <= 96; admm_generic.cu).
+template <typename R>
+size_t admm_generic_ws_bytes(const TmpcDims& d);
+template <typename R>
+int launch_admm_generic(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st);
+template <typename R>
+int assemble_generic(const TmpcDims* d, const TmpcQP* qp, const R* rho, R sigma, R rff, R* S, R* P, int32_t* status,
+                     cudaStream_t st);
+
 // Register-resident kernel for 8 < n <= 16, T <= 64, fp32 (admm_rows.cu).
 bool admm_rows_ok(int T, int n, int nx, int n0, int m);
 int launch_admm_rows(const AdmmParams<float>& P, cudaStream_t st);

@@ -99,6 +99,7 @@ int schur_assemble(const TmpcDims* d, const TmpcQP* qp, const R* rho, double sig
   if (d->n0 > 0 && !qp->A0) return TMPC_ERR_NULL_ARG;
   if (d->m > 0 && !qp->G) return TMPC_ERR_NULL_ARG;
   if (d->Nb == 0) return TMPC_OK;
+  if (d->n > 32) return assemble_generic<R>(d, qp, rho, (R)sigma, (R)rff, S, P, status, st);
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
     return launch_assemble_ref<NB, R>(d, qp, rho, (R)sigma, (R)rff, S, P, status, st);
