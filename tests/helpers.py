@@ -48,3 +48,21 @@ def oracle_admm_solve(qp, state0, cfg, slack_weight=None, out=None, workspace=No
     g = lambda a: torch.as_tensor(a, dtype=dt, device=dev)
     st = TState(g(so.x), g(so.y_g), g(so.y_f0), g(so.y_fdyn), g(so.z_g), g(so.xi_g), g(so.rho))
     return st, torch.as_tensor(it, dtype=torch.int64, device=dev), torch.zeros(qp.Nb, dtype=torch.int32, device=dev)
+
+
+def wide_problem(batch, nx, nu, N, m, seed):
+    """Stable LTI dynamics (A = I + 0.1 G, the configuration-2 generator) with
+    every QP term non-zero: q, c, a small coupling E (P stays positive
+    definite) and m general G rows with |G z| <= 1; well conditioned at wide
+    blocks (cond(S) ~ 1e2 at n = 48..96), unlike random_dense, whose random
+    dynamics grow along the horizon at nx = 32."""
+    rng = np.random.default_rng(seed)
+    b = synthetic.random_lti(batch, nx, nu, N, seed=seed)
+    n, T = nx + nu, N + 1
+    b["q"] = rng.normal(size=(batch, T, n))
+    b["c"] = 0.1 * rng.normal(size=(batch, N, nx))
+    b["E"] = 0.02 * rng.normal(size=(batch, N, n, n)) / np.sqrt(n)
+    b["G"] = rng.normal(size=(batch, T, m, n)) / np.sqrt(n)
+    b["l"] = -np.ones((batch, T, m))
+    b["u"] = np.ones((batch, T, m))
+    return b

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from oracle import admm_ref as ref
-from tests.helpers import dense_blocks, oracle_qp, rel_err
+from tests.helpers import dense_blocks, oracle_qp, rel_err, wide_problem
 from turbompc_b200 import _ffi, ops
 from turbompc_b200.problems import synthetic
 
@@ -34,7 +34,7 @@ def test_schur_assembly_wide_blocks_matches_oracle(nx, nu):
 
 @pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
 def test_pcg_wide_blocks_matches_oracle(dtype):
-    b = dense_blocks(4, 32, 16, 8, 4, seed=3)
+    b = wide_problem(4, 32, 16, 8, 4, seed=3)
     qd = synthetic.to_qpdata(b, dtype=torch.float64, device="cuda")
     S, P, _ = ops.schur_assemble(qd, 0.1, 1e-6, 100.0)
     g = torch.Generator(device="cuda").manual_seed(1)
@@ -69,9 +69,9 @@ FIXED = dict(max_iter=12, pcg_max_iter=20, check_every=0, adapt_rho_every=0, eps
 
 
 @pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
-@pytest.mark.parametrize("nx,nu,N", [(32, 16, 10), (40, 20, 6)])
+@pytest.mark.parametrize("nx,nu,N", [(32, 16, 10), (40, 20, 6), (64, 32, 5)])
 def test_fused_admm_wide_blocks_matches_oracle(dtype, nx, nu, N):
-    b = dense_blocks(3, nx, nu, N, 6, seed=nx + N)
+    b = wide_problem(3, nx, nu, N, 6, seed=nx + N)
     out, it, so, ito = _run(b, dtype, FIXED)
     tol = 1e-6 if dtype == torch.float64 else 1e-3
     assert (it.cpu().numpy() == ito).all()
@@ -80,7 +80,7 @@ def test_fused_admm_wide_blocks_matches_oracle(dtype, nx, nu, N):
 
 
 def test_fused_admm_wide_blocks_checks_slack_and_rho_adaptation_fp64():
-    b = dense_blocks(4, 32, 16, 6, 4, seed=9)
+    b = wide_problem(4, 32, 16, 6, 4, seed=9)
     cfg = dict(FIXED, max_iter=60, pcg_max_iter=8, check_every=5, adapt_rho_every=10, eps_abs=1e-4, eps_rel=1e-4)
     out, it, so, ito = _run(b, torch.float64, cfg, slack=10.0)
     assert (it.cpu().numpy() == ito).all(), (it, ito)
