@@ -324,6 +324,39 @@ int32_t tmpc_linearize_dynamics_f64(const TmpcDims* dims, int32_t model, int32_t
                                     int32_t n_params, double* A_minus, double* c, tmpc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * QP producers of the benchmark problems beyond the dynamics rows, batched
+ * over (problem, stage); dims: Nb, T, n = nx + nu, nx (n0, m unused).
+ *
+ * Spherical obstacle rows (turbompc/problems/obstacle_avoidance.py:16-52,
+ * linearised as get_inequalities_linearized_matrices does,
+ * optimal_control_problem.py:580-626): for p = states[b][t][:dim],
+ *   g_k = 1 - ||p - c_k|| / (r_k + 0.001), G_k = dg_k / dz,
+ *   l_k = -1e9 - (g_k - G_k z), u_k = -(g_k - G_k z),  all times row_scale.
+ * states [Nb][T][nx], centers [Nb][K][dim], radii [Nb][K];
+ * outputs G [Nb][T][K][n], l, u [Nb][T][K].
+ * ------------------------------------------------------------------------- */
+int32_t tmpc_obstacle_rows_f32(const TmpcDims* dims, int32_t dim, int32_t n_obstacles, const float* states,
+                               const float* centers, const float* radii, double row_scale, float* G, float* l,
+                               float* u, tmpc_stream_t stream);
+int32_t tmpc_obstacle_rows_f64(const TmpcDims* dims, int32_t dim, int32_t n_obstacles, const double* states,
+                               const double* centers, const double* radii, double row_scale, double* G, double* l,
+                               double* u, tmpc_stream_t stream);
+/* A learned stage cost s * w2 . tanh(W1 z + b1) (z = [x, u], every stage)
+ * quadratised exactly and added in place to the cost blocks (the
+ * stage-separable case of get_cost_linearized_blocks,
+ * optimal_control_problem.py:1068-1174):  D_t += H, q_t += grad - H z with
+ * grad = s W1^T (w2 * (1 - th^2)), H = s W1^T diag(w2 * (-2 th (1 - th^2))) W1,
+ * th = tanh(W1 z + b1).  W1 [hidden][n], b1, w2 [hidden] (shared by the
+ * batch); D [Nb][T][n][n], q [Nb][T][n]; n <= 16.  No counterpart kernel in
+ * the reference (its learned costs go through jax.grad / jax.hessian). */
+int32_t tmpc_mlp_cost_blocks_f32(const TmpcDims* dims, int32_t hidden, const float* states, const float* controls,
+                                 const float* W1, const float* b1, const float* w2, double scale, float* D, float* q,
+                                 tmpc_stream_t stream);
+int32_t tmpc_mlp_cost_blocks_f64(const TmpcDims* dims, int32_t hidden, const double* states,
+                                 const double* controls, const double* W1, const double* b1, const double* w2,
+                                 double scale, double* D, double* q, tmpc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Batch-interleaved layout and the direct solve on it.
  *
  * TMPC_LAYOUT_REFERENCE is the problem-major layout every entry point above

@@ -1,0 +1,48 @@
+"""The CUDA producers of the obstacle rows (tmpc_obstacle_rows_*) and of the
+learned stage cost's quadratisation (tmpc_mlp_cost_blocks_*) against their
+PyTorch forms, which tests/test_sqp_oracle.py pins to the oracle's autodiff QP
+(fp64 1e-12, fp32 1e-5 relative); the whole solves of configurations 4 and 5
+in tests/test_gpu_sqp_oracle.py run these kernels too."""
+import pytest
+import torch
+
+from tests.helpers import rel_err
+from turbompc_b200 import ops
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.float64: 1e-12, torch.float32: 1e-5}
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_obstacle_rows_kernel_matches_torch(dtype):
+    from turbompc_b200.problems.quadrotor import make_obstacle_problem
+    prog, p = make_obstacle_problem(37, N=9, n_obstacles=8, seed=3, dtype=dtype, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(2)
+    X = torch.randn(37, 10, 12, generator=g, device="cuda", dtype=dtype)
+    U = torch.rand(37, 10, 4, generator=g, device="cuda", dtype=dtype)
+    c, r = p["obstacles_centers"], p["obstacles_radii"]
+    G, lo, hi = ops.obstacle_rows(X, c, r, 3, 16)
+    G2, lo2, hi2 = prog._obstacle_rows_torch(X.cpu(), U.cpu(), c.cpu(), r.cpu(), 3)
+    assert rel_err(G.cpu().numpy(), G2.numpy()) < TOL[dtype]
+    assert rel_err(hi.cpu().numpy(), hi2.numpy()) < TOL[dtype]
+    assert rel_err(lo.cpu().numpy(), lo2.numpy()) < TOL[dtype]
+    # scaled rows
+    Gs, los, his = ops.obstacle_rows(X, c, r, 3, 16, row_scale=0.25)
+    assert rel_err(Gs.cpu().numpy(), 0.25 * G2.numpy()) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+@pytest.mark.parametrize("hidden", [16, 64])
+def test_mlp_cost_blocks_kernel_matches_torch(dtype, hidden):
+    from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    prog, p = make_learned_cost_problem(21, N=12, hidden=hidden, seed=4, dtype=dtype, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    X = torch.randn(21, 13, 6, generator=gen, device="cuda", dtype=dtype)
+    U = 0.1 * torch.randn(21, 13, 3, generator=gen, device="cuda", dtype=dtype)
+    D, E, q = prog.get_cost_linearized_blocks(X, U, p)  # CUDA kernel path
+    pc = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in p.items()}
+    pc["dynamics_state_dot_params"] = {k: v.cpu() for k, v in p["dynamics_state_dot_params"].items()}
+    D2, E2, q2 = prog.get_cost_linearized_blocks(X.cpu(), U.cpu(), pc)  # PyTorch path
+    assert rel_err(D.cpu().numpy(), D2.numpy()) < TOL[dtype]
+    assert rel_err(q.cpu().numpy(), q2.numpy()) < TOL[dtype] * 10
+    assert torch.equal(E.cpu(), E2)

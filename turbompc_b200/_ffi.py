@@ -64,6 +64,10 @@ _SIGS["tmpc_riccati_il_elems_per_problem"] = (C.c_int64, [C.POINTER(TmpcDims)])
 _SIGS["tmpc_stream_operator_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 _SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32])
 for _s in ("f32", "f64"):
+    _SIGS[f"tmpc_obstacle_rows_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, C.c_int32, _P, _P, _P,
+                                                     C.c_double, _P, _P, _P, _P])
+    _SIGS[f"tmpc_mlp_cost_blocks_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, _P, _P, _P, _P, _P,
+                                                       C.c_double, _P, _P, _P])
     _SIGS[f"tmpc_interleave_{_s}"] = (C.c_int32, [C.c_int32, C.c_int64, _P, _P, _P])
     _SIGS[f"tmpc_deinterleave_{_s}"] = (C.c_int32, [C.c_int32, C.c_int64, _P, _P, _P])
     _SIGS[f"tmpc_schur_interleave_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P])

@@ -413,3 +413,43 @@ def riccati_solve_il(factor: torch.Tensor, dims: _ffi.TmpcDims, rhs_il: torch.Te
     _ffi.check(name, getattr(lib, name)(C.byref(dims), factor.data_ptr(), rhs_il.data_ptr(), x.data_ptr(),
                                         _stream(factor.device)))
     return x
+
+
+# ---------------------------------------------------------------------------
+# QP producers beyond the dynamics rows
+# ---------------------------------------------------------------------------
+def obstacle_rows(states: torch.Tensor, centers: torch.Tensor, radii: torch.Tensor, dim: int, n: int,
+                  row_scale: float = 1.0):
+    """Linearised spherical obstacle rows (tmpc_obstacle_rows_*): returns
+    (G (Nb, T, K, n), l, u (Nb, T, K))."""
+    lib = _ffi.load()
+    states = states.contiguous()
+    Nb, T, nx = states.shape
+    K = centers.shape[1]
+    dt, dev = states.dtype, states.device
+    G = torch.empty(Nb, T, K, n, dtype=dt, device=dev)
+    lo = torch.empty(Nb, T, K, dtype=dt, device=dev)
+    hi = torch.empty_like(lo)
+    d = _ffi.TmpcDims(Nb, T, n, nx, 0, 0)
+    name = f"tmpc_obstacle_rows_{_suffix(dt)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), int(dim), int(K), _ptr(states), _ptr(centers.contiguous(), dt, dev),
+                                        _ptr(radii.contiguous(), dt, dev), float(row_scale), _ptr(G), _ptr(lo),
+                                        _ptr(hi), _stream(dev)))
+    return G, lo, hi
+
+
+def mlp_cost_blocks_(D: torch.Tensor, q: torch.Tensor, states: torch.Tensor, controls: torch.Tensor,
+                     W1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor, scale: float):
+    """Adds the exact quadratisation of s * w2 . tanh(W1 z + b1) to D and q in
+    place (tmpc_mlp_cost_blocks_*); D (Nb, T, n, n), q (Nb, T, n) contiguous."""
+    lib = _ffi.load()
+    Nb, T, nx = states.shape
+    nu = controls.shape[-1]
+    dt, dev = D.dtype, D.device
+    d = _ffi.TmpcDims(Nb, T, nx + nu, nx, 0, 0)
+    name = f"tmpc_mlp_cost_blocks_{_suffix(dt)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), int(W1.shape[0]), _ptr(states.contiguous(), dt, dev),
+                                        _ptr(controls.contiguous(), dt, dev), _ptr(W1.contiguous(), dt, dev),
+                                        _ptr(b1.contiguous(), dt, dev), _ptr(w2.contiguous(), dt, dev), float(scale),
+                                        _ptr(D, dt, dev), _ptr(q, dt, dev), _stream(dev)))
+    return D, q

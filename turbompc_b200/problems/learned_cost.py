@@ -35,8 +35,20 @@ class OptimalControlProblemLearnedCost(OptimalControlProblem):
                 float(params["mlp_scale"]))
 
     def get_cost_linearized_blocks(self, states, controls, params):
+        """Tracking blocks plus the MLP term's exact quadratisation: one CUDA
+        kernel (tmpc_mlp_cost_blocks_*) on GPU tensors, PyTorch otherwise."""
         D, E, q = super().get_cost_linearized_blocks(states, controls, params)
         W1, b1, w2, s = self._mlp(params, states)
+        if states.is_cuda and states.shape[-1] + controls.shape[-1] <= 16:
+            from .. import ops
+            D, q = D.contiguous(), q.contiguous()
+            ops.mlp_cost_blocks_(D, q, states, controls, W1.detach(), b1.detach(), w2.detach(), s)
+            return D, E, q
+        return self._mlp_blocks_torch(D, E, q, states, controls, W1, b1, w2, s)
+
+    def _mlp_blocks_torch(self, D, E, q, states, controls, W1, b1, w2, s):
+        """The same quadratisation in PyTorch operations (host tensors; the
+        CUDA kernel's test reference)."""
         z = torch.cat([states, controls], -1)  # (Nb, T, n)
         a = torch.einsum("hn,btn->bth", W1, z) + b1
         th = torch.tanh(a)

@@ -514,9 +514,20 @@ class OptimalControlProblemObstacle(OptimalControlProblem):
         return g, torch.full_like(g, -1e9), torch.zeros_like(g)
 
     def _extra_inequalities_linearized(self, states, controls, params):
+        """The obstacle rows: one CUDA kernel (tmpc_obstacle_rows_*) on GPU
+        tensors, PyTorch otherwise."""
         dim = int(params["obstacles_dimension"])
         c = _t(params["obstacles_centers"], states)  # (Nb, K, dim)
         r = _t(params["obstacles_radii"], states)  # (Nb, K)
+        if states.is_cuda:
+            from .. import ops
+            # the rescaling row scale is applied by the caller
+            return ops.obstacle_rows(states, c, r, dim, states.shape[-1] + controls.shape[-1])
+        return self._obstacle_rows_torch(states, controls, c, r, dim)
+
+    def _obstacle_rows_torch(self, states, controls, c, r, dim):
+        """The same rows in PyTorch operations (host tensors; the CUDA
+        kernel's test reference)."""
         Nb, T, nx = states.shape
         nu = controls.shape[-1]
         p = states[..., :dim]  # (Nb, T, dim)
