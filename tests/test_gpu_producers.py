@@ -46,3 +46,22 @@ def test_mlp_cost_blocks_kernel_matches_torch(dtype, hidden):
     assert rel_err(D.cpu().numpy(), D2.numpy()) < TOL[dtype]
     assert rel_err(q.cpu().numpy(), q2.numpy()) < TOL[dtype] * 10
     assert torch.equal(E.cpu(), E2)
+
+
+def test_repeated_learned_cost_solves_are_identical():
+    """From the second SQP iteration on the linearisation points are views of
+    the ADMM iterate; the producer wrappers must keep their contiguous copies
+    alive until the launch (a freed copy's block was handed to the next
+    temporary and overwritten before the kernel read it)."""
+    from turbompc_b200.problems.learned_cost import make_learned_cost_problem
+    from turbompc_b200.solver import TurboMPCSolver
+    prog, p = make_learned_cost_problem(3, N=10, hidden=16, seed=2, dtype=torch.float64, device="cuda")
+    sp = {"num_sqp_iteration_max": 3, "tol_convergence": 0.0,
+          "admm": {"max_iter": 30, "check_termination_every": 0, "adapt_rho_every": 0, "eps_abs": 0.0,
+                   "eps_rel": 0.0, "pcg": {"max_iter": 10, "tol_epsilon": 0.0}}}
+    s = TurboMPCSolver(prog, sp)
+    g = s.initial_guess(p)
+    first = s.solve(g, p)
+    for _ in range(3):
+        again = s.solve(g, p)
+        assert torch.equal(again.controls, first.controls) and torch.equal(again.states, first.states)

@@ -108,3 +108,18 @@ def test_learned_cost_quadratisation_matches_autograd():
     Pz[:, :-1] += torch.einsum("btji,btj->bti", E, zz[:, 1:])
     assert torch.allclose(q, grad - Pz, atol=1e-9)
     assert (torch.linalg.eigvalsh(D) > 0).all()
+
+
+def test_gradient_accuracy_problem_data_is_stable_and_seeded():
+    """benchmarking/linear-system/utils.py:28-62: eigenvalues of A inside the
+    unit circle, the legacy NumPy stream seeded by the seed."""
+    import numpy as np
+    from turbompc_b200.gradient_accuracy import problem_data
+    Q, R, A, B, b, x0 = problem_data(16, 3, 8, 4)
+    assert np.abs(np.linalg.eigvals(A)).max() < 1.0
+    assert x0.shape == (16, 8) and B.shape == (8, 4) and b.shape == (8,)
+    rs = np.random.RandomState(3)
+    rs.randn(8, 8)  # A's draw comes first, then B's
+    assert np.array_equal(B, rs.randn(8, 4))
+    Q2, R2, A2, B2, b2, x02 = problem_data(16, 3, 8, 4)
+    assert np.array_equal(A, A2) and np.array_equal(x0, x02)

@@ -62,6 +62,12 @@ def _suffix(dtype: torch.dtype) -> str:
     raise TypeError(f"turbompc_b200 kernels support float32/float64, got {dtype}")
 
 
+# Every tensor whose pointer goes to the library must stay referenced until the
+# call has enqueued its kernel: a temporary such as ``x.contiguous()`` passed
+# straight to _ptr is freed as soon as _ptr returns, and the caching allocator
+# may hand its block to the next temporary, whose copy kernel (enqueued first)
+# then overwrites the data the launch was meant to read.  Wrappers bind such
+# temporaries to local names first.
 def _ptr(t: Optional[torch.Tensor], dtype=None, device=None) -> Optional[int]:
     if t is None:
         return None
@@ -338,14 +344,14 @@ def first_order_error(qp: QPData, z: torch.Tensor, state: ADMMState, slacks: Opt
     g = torch.empty(qp.Nb, qp.T, qp.m, dtype=dt, device=dev)
     use_slack = bool(qp.ineq.use_slack_variables) and qp.m > 0
     sw = qp.ineq.slack_penalization_weight if use_slack else None
+    yf0, yfd, yg = state.y_f_0.contiguous(), state.y_f_dyn.contiguous(), state.y_g.contiguous()
+    sl = slacks.contiguous() if use_slack else None
+    swv = _rho_vec(sw, qp) if sw is not None else None
     name = f"tmpc_first_order_error_{_suffix(dt)}"
     _ffi.check(name, getattr(lib, name)(C.byref(dims_of(qp)), C.byref(_qp_c(qp)), _ptr(z, dt, dev),
-                                        _ptr(state.y_f_0.contiguous(), dt, dev),
-                                        _ptr(state.y_f_dyn.contiguous(), dt, dev),
-                                        _ptr(state.y_g.contiguous(), dt, dev),
-                                        _ptr(slacks.contiguous() if use_slack else None, dt, dev),
-                                        _ptr(_rho_vec(sw, qp) if sw is not None else None, dt, dev),
-                                        int(use_slack), _ptr(conv), _ptr(eq), _ptr(ineq), _ptr(g), _stream(dev)))
+                                        _ptr(yf0, dt, dev), _ptr(yfd, dt, dev), _ptr(yg, dt, dev), _ptr(sl, dt, dev),
+                                        _ptr(swv, dt, dev), int(use_slack), _ptr(conv), _ptr(eq), _ptr(ineq),
+                                        _ptr(g), _stream(dev)))
     return conv, eq, ineq, g
 
 
@@ -363,8 +369,9 @@ def interleave(x: torch.Tensor) -> torch.Tensor:
     nb = x.shape[0]
     e = x[0].numel() if nb > 0 else 0
     out = torch.empty(max(interleaved_numel(nb, e), 1), dtype=x.dtype, device=x.device)
+    xc = x.contiguous()
     name = f"tmpc_interleave_{_suffix(x.dtype)}"
-    _ffi.check(name, getattr(lib, name)(nb, e, _ptr(x.contiguous()), out.data_ptr(), _stream(x.device)))
+    _ffi.check(name, getattr(lib, name)(nb, e, _ptr(xc), out.data_ptr(), _stream(x.device)))
     return out
 
 
@@ -431,10 +438,11 @@ def obstacle_rows(states: torch.Tensor, centers: torch.Tensor, radii: torch.Tens
     lo = torch.empty(Nb, T, K, dtype=dt, device=dev)
     hi = torch.empty_like(lo)
     d = _ffi.TmpcDims(Nb, T, n, nx, 0, 0)
+    cc, rr = centers.contiguous(), radii.contiguous()
     name = f"tmpc_obstacle_rows_{_suffix(dt)}"
-    _ffi.check(name, getattr(lib, name)(C.byref(d), int(dim), int(K), _ptr(states), _ptr(centers.contiguous(), dt, dev),
-                                        _ptr(radii.contiguous(), dt, dev), float(row_scale), _ptr(G), _ptr(lo),
-                                        _ptr(hi), _stream(dev)))
+    _ffi.check(name, getattr(lib, name)(C.byref(d), int(dim), int(K), _ptr(states), _ptr(cc, dt, dev),
+                                        _ptr(rr, dt, dev), float(row_scale), _ptr(G), _ptr(lo), _ptr(hi),
+                                        _stream(dev)))
     return G, lo, hi
 
 
@@ -447,9 +455,10 @@ def mlp_cost_blocks_(D: torch.Tensor, q: torch.Tensor, states: torch.Tensor, con
     nu = controls.shape[-1]
     dt, dev = D.dtype, D.device
     d = _ffi.TmpcDims(Nb, T, nx + nu, nx, 0, 0)
+    xs, us = states.contiguous(), controls.contiguous()
+    w1c, b1c, w2c = W1.contiguous(), b1.contiguous(), w2.contiguous()
     name = f"tmpc_mlp_cost_blocks_{_suffix(dt)}"
-    _ffi.check(name, getattr(lib, name)(C.byref(d), int(W1.shape[0]), _ptr(states.contiguous(), dt, dev),
-                                        _ptr(controls.contiguous(), dt, dev), _ptr(W1.contiguous(), dt, dev),
-                                        _ptr(b1.contiguous(), dt, dev), _ptr(w2.contiguous(), dt, dev), float(scale),
+    _ffi.check(name, getattr(lib, name)(C.byref(d), int(W1.shape[0]), _ptr(xs, dt, dev), _ptr(us, dt, dev),
+                                        _ptr(w1c, dt, dev), _ptr(b1c, dt, dev), _ptr(w2c, dt, dev), float(scale),
                                         _ptr(D, dt, dev), _ptr(q, dt, dev), _stream(dev)))
     return D, q
