@@ -239,6 +239,43 @@ def admm_only(nb, linsys="auto", reps=3, pcg=PCG, admm=ADMM):
                       "us_per_problem": round(1e3 * ms / nb, 3), "status_nonzero": int((st != 0).sum())}))
 
 
+def il_only(point, reps=2):
+    """Profiling aid: the batch-interleaved factor and solve of one LTI point
+    ('nx,nu,N,batch,dtype'), `reps` launches each after one warm-up, timed
+    with CUDA events (one JSON line)."""
+    import torch
+
+    from turbompc_b200 import _ffi, ops
+    from turbompc_b200.problems import synthetic
+
+    f = point.split(",")
+    nx, nu, N, batch, dt = int(f[0]), int(f[1]), int(f[2]), int(f[3]), f[4]
+    tdt = torch.float32 if dt == "f32" else torch.float64
+    n, T = nx + nu, N + 1
+    small = synthetic.to_qpdata(synthetic.random_lti(64, nx, nu, N, seed=1000 + nx + N), dtype=tdt, device="cuda")
+    S, _, _ = ops.schur_assemble(small, 0.1, 1e-6, 1000.0)
+    S = S.repeat((batch + 63) // 64, 1, 1, 1)[:batch].contiguous()
+    dims = _ffi.TmpcDims(batch, T, n, nx, 0, 0)
+    ops_il = ops.schur_interleave(S)
+    del S
+    g = torch.Generator(device="cuda").manual_seed(7)
+    rhs_il = ops.interleave(torch.randn(batch, T, n, generator=g, device="cuda", dtype=tdt))
+    fac, st = ops.riccati_factor_il(ops_il, dims)
+    x = ops.riccati_solve_il(fac, dims, rhs_il)
+    torch.cuda.synchronize()
+    e0, e1, e2 = torch.cuda.Event(True), torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(reps):
+        ops.riccati_factor_il(ops_il, dims, fac, st)
+    e1.record()
+    for _ in range(reps):
+        ops.riccati_solve_il(fac, dims, rhs_il, x)
+    e2.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"il_only": point, "factor_ms": e0.elapsed_time(e1) / reps, "solve_ms": e1.elapsed_time(e2) / reps,
+                      "status_nonzero": int((st != 0).sum())}))
+
+
 def pcg_sweep(points, reps=5, pcg_iters=PCG, emit=None):
     """Config 2 (linear-system kernel sweep): standalone PCG (fixed iterations,
     tol 0) on assembled packed operators and the direct block-Cholesky solve,
@@ -478,6 +515,8 @@ def main():
                     help="with --admm-only: auto (register-resident kernel where it applies) or the packed kernel")
     ap.add_argument("--admm-pcg", type=int, default=PCG, help="with --admm-only: PCG iterations per ADMM iteration")
     ap.add_argument("--admm-iters", type=int, default=ADMM, help="with --admm-only: ADMM iterations per launch")
+    ap.add_argument("--il-only", default="", metavar="POINT",
+                    help="profiling aid: interleaved factor + solve of one 'nx,nu,N,batch,dtype' point, then exit")
     ap.add_argument("--config", default="", choices=["", "obstacles", "cw_mlp"],
                     help="time config 4 (obstacles) or config 5 (cw_mlp) on one GPU instead of the default run")
     ap.add_argument("--pcg-sweep", default="", metavar="POINTS",
@@ -496,6 +535,8 @@ def main():
             a = item.split(",")
             pts.append((int(a[0]), int(a[1]), int(a[2]), int(a[3]), a[4]))
         return pcg_sweep(pts)
+    if args.il_only:
+        return il_only(args.il_only)
     if args.admm_only:
         return admm_only(args.admm_only, args.admm_linsys, pcg=args.admm_pcg, admm=args.admm_iters)
 

@@ -57,7 +57,7 @@ def problem_data(batch: int, seed: int, nx: int, nu: int):
 def make_problem(seed: int, batch: int, horizon: int, nx: int, nu: int, umax: float, device="cuda",
                  dtype=torch.float64):
     Q, R, A, B, b, x0 = problem_data(batch, seed, nx, nu)
-    t = lambda a: torch.as_tensor(np.asarray(a), dtype=dtype, device=device)
+    t = lambda a: torch.as_tensor(np.array(a), dtype=dtype, device=device)
     N = horizon - 1
     params = {
         "horizon": N, "discretization_resolution": 1.0, "discretization_scheme": 0,
