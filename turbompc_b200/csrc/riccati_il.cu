@@ -164,8 +164,13 @@ __device__ __forceinline__ void factor_one(const R* __restrict__ op, R* __restri
 
 // (Capping the factor at 168 registers for three blocks per SM measured slower
 // at every size: 10-47 % at n = 9 and 16, fp32 and fp64.)
+// One warp per block: at 200-255 registers per thread an SM holds 8 of these
+// warps, and small blocks spread a modest batch over every SM (128-thread
+// blocks left 20 of 148 SMs idle at 16,384 problems; the time did not change:
+// each warp's chain of dependent stages sets it).
+constexpr int kFactorThreads = 32;
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, R* __restrict__ factor,
+__global__ void __launch_bounds__(kFactorThreads) factor_kernel(const R* __restrict__ ops, R* __restrict__ factor,
                                                      int32_t* status, int Nb,
                                                      int T, int n) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -190,6 +195,8 @@ __global__ void __launch_bounds__(128) factor_kernel(const R* __restrict__ ops, 
 // ---------------------------------------------------------------------------
 constexpr int kSolveWarps = 4;
 
+// (Register caps for 3 or 4 resident blocks per SM measured slower at 16,384
+// problems, 1.2-2.5x, and within 1 % at 65,536.)
 template <int NB, typename R>
 __global__ void __launch_bounds__(32 * kSolveWarps) solve_kernel(const R* __restrict__ factor,
                                                                  const R* __restrict__ rhs, R* __restrict__ x_out,
@@ -413,8 +420,8 @@ int factor(const TmpcDims* d, const R* ops, R* fac, int32_t* status, cudaStream_
   if (!ops || !fac) return TMPC_ERR_NULL_ARG;
   return dispatch_il<R>(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    const int grid = (int)((groups(d->Nb) * kWarp + 127) / 128);
-    factor_kernel<NB, R><<<grid, 128, 0, st>>>(ops, fac, status, d->Nb, d->T, d->n);
+    const int grid = (int)((groups(d->Nb) * kWarp + kFactorThreads - 1) / kFactorThreads);
+    factor_kernel<NB, R><<<grid, kFactorThreads, 0, st>>>(ops, fac, status, d->Nb, d->T, d->n);
     return (int)cudaPeekAtLastError();
   });
 }
