@@ -154,65 +154,79 @@ struct RowsInvAcc {
 };
 
 struct RowOps {
-  float ti[2][16];  // Theta_t^-1 rows q, q + 8
-  float lr[2][16];  // S(t, t-1) rows
-  float lc[2][16];  // S(t, t+1) rows
+  float2 ti[2][8];  // Theta_t^-1 rows q, q + 8, as column pairs (2c, 2c + 1)
+  float2 lr[2][8];  // S(t, t-1) rows
+  float2 lc[2][8];  // S(t, t+1) rows
 };
 
-// a_i += m_i . v for the two owned rows; v is a broadcast 16-vector in shared memory.
-// (A two-partial-sum form, as in rows_bdot_split, measured 0.7 % slower here.)
-__device__ __forceinline__ void rows_bdot(float& a0, float& a1, const float (&m0)[16], const float (&m1)[16],
+// The block-row products use the paired FP32 FMA of sm_100 (FFMA2 through
+// __ffma2_rn): each row keeps two partial sums, one over the even and one
+// over the odd columns, so a 16-entry row costs eight paired FMAs and one add
+// instead of sixteen FMAs, and the dependent chain is eight long.  A float4 of
+// the broadcast vector supplies the column pairs (2c, 2c + 1) directly.
+__device__ __forceinline__ float2 f2lo(const float4 w) { return make_float2(w.x, w.y); }
+__device__ __forceinline__ float2 f2hi(const float4 w) { return make_float2(w.z, w.w); }
+
+// a_i = m_i . v for the two owned rows; v is a broadcast 16-vector in shared memory.
+__device__ __forceinline__ void rows_bdot(float& a0, float& a1, const float2 (&m0)[8], const float2 (&m1)[8],
                                           const float* v) {
+  float2 e0 = make_float2(0.f, 0.f), e1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const float4 w = *reinterpret_cast<const float4*>(v + 4 * c);
-    a0 = fmaf(m0[4 * c], w.x, a0); a1 = fmaf(m1[4 * c], w.x, a1);
-    a0 = fmaf(m0[4 * c + 1], w.y, a0); a1 = fmaf(m1[4 * c + 1], w.y, a1);
-    a0 = fmaf(m0[4 * c + 2], w.z, a0); a1 = fmaf(m1[4 * c + 2], w.z, a1);
-    a0 = fmaf(m0[4 * c + 3], w.w, a0); a1 = fmaf(m1[4 * c + 3], w.w, a1);
+    e0 = __ffma2_rn(m0[2 * c], f2lo(w), e0);
+    e1 = __ffma2_rn(m1[2 * c], f2lo(w), e1);
+    e0 = __ffma2_rn(m0[2 * c + 1], f2hi(w), e0);
+    e1 = __ffma2_rn(m1[2 * c + 1], f2hi(w), e1);
   }
+  a0 = e0.x + e0.y;
+  a1 = e1.x + e1.y;
 }
 
-// a_i = m_i . v with two partial sums per row (chunks 0, 2 and 1, 3) to halve
-// the dependent FMA chain on the latency-critical preconditioner steps.
-__device__ __forceinline__ void rows_bdot_split(float& a0, float& a1, const float (&m0)[16], const float (&m1)[16],
+// Same as rows_bdot with four partial sums per row (column pairs 0-3 and
+// 4-7 kept apart) for the latency-critical preconditioner steps.
+__device__ __forceinline__ void rows_bdot_split(float& a0, float& a1, const float2 (&m0)[8], const float2 (&m1)[8],
                                                 const float* v) {
-  float e0 = 0.f, e1 = 0.f, o0 = 0.f, o1 = 0.f;
+  float2 e0 = make_float2(0.f, 0.f), e1 = make_float2(0.f, 0.f);
+  float2 o0 = make_float2(0.f, 0.f), o1 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int c = 0; c < 4; c += 2) {
+  for (int c = 0; c < 2; ++c) {
     const float4 w = *reinterpret_cast<const float4*>(v + 4 * c);
-    const float4 u = *reinterpret_cast<const float4*>(v + 4 * c + 4);
-    e0 = fmaf(m0[4 * c], w.x, e0); e1 = fmaf(m1[4 * c], w.x, e1);
-    o0 = fmaf(m0[4 * c + 4], u.x, o0); o1 = fmaf(m1[4 * c + 4], u.x, o1);
-    e0 = fmaf(m0[4 * c + 1], w.y, e0); e1 = fmaf(m1[4 * c + 1], w.y, e1);
-    o0 = fmaf(m0[4 * c + 5], u.y, o0); o1 = fmaf(m1[4 * c + 5], u.y, o1);
-    e0 = fmaf(m0[4 * c + 2], w.z, e0); e1 = fmaf(m1[4 * c + 2], w.z, e1);
-    o0 = fmaf(m0[4 * c + 6], u.z, o0); o1 = fmaf(m1[4 * c + 6], u.z, o1);
-    e0 = fmaf(m0[4 * c + 3], w.w, e0); e1 = fmaf(m1[4 * c + 3], w.w, e1);
-    o0 = fmaf(m0[4 * c + 7], u.w, o0); o1 = fmaf(m1[4 * c + 7], u.w, o1);
+    const float4 u = *reinterpret_cast<const float4*>(v + 8 + 4 * c);
+    e0 = __ffma2_rn(m0[2 * c], f2lo(w), e0);
+    e1 = __ffma2_rn(m1[2 * c], f2lo(w), e1);
+    o0 = __ffma2_rn(m0[4 + 2 * c], f2lo(u), o0);
+    o1 = __ffma2_rn(m1[4 + 2 * c], f2lo(u), o1);
+    e0 = __ffma2_rn(m0[2 * c + 1], f2hi(w), e0);
+    e1 = __ffma2_rn(m1[2 * c + 1], f2hi(w), e1);
+    o0 = __ffma2_rn(m0[5 + 2 * c], f2hi(u), o0);
+    o1 = __ffma2_rn(m1[5 + 2 * c], f2hi(u), o1);
   }
-  a0 = e0 + o0;
-  a1 = e1 + o1;
+  a0 = (e0.x + e0.y) + (o0.x + o0.y);
+  a1 = (e1.x + e1.y) + (o1.x + o1.y);
 }
 
 // Same as rows_bdot with the two matrix rows read from shared memory (Theta rows).
 __device__ __forceinline__ void rows_sdot(float& a0, float& a1, const float* r0, const float* r1, const float* v) {
+  float2 e0 = make_float2(0.f, 0.f), e1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const float4 w = *reinterpret_cast<const float4*>(v + 4 * c);
     const float4 m0 = *reinterpret_cast<const float4*>(r0 + 4 * c);
     const float4 m1 = *reinterpret_cast<const float4*>(r1 + 4 * c);
-    a0 = fmaf(m0.x, w.x, a0); a1 = fmaf(m1.x, w.x, a1);
-    a0 = fmaf(m0.y, w.y, a0); a1 = fmaf(m1.y, w.y, a1);
-    a0 = fmaf(m0.z, w.z, a0); a1 = fmaf(m1.z, w.z, a1);
-    a0 = fmaf(m0.w, w.w, a0); a1 = fmaf(m1.w, w.w, a1);
+    e0 = __ffma2_rn(f2lo(m0), f2lo(w), e0);
+    e1 = __ffma2_rn(f2lo(m1), f2lo(w), e1);
+    e0 = __ffma2_rn(f2hi(m0), f2hi(w), e0);
+    e1 = __ffma2_rn(f2hi(m1), f2hi(w), e1);
   }
+  a0 = e0.x + e0.y;
+  a1 = e1.x + e1.y;
 }
 
 // y = (S v) at the owned rows; vt points at row t of the buffer holding v
 // (row t + 1 is stage t).
 __device__ __forceinline__ void rows_smv(float (&y)[2], const RowOps& o, const float* th_row, const float* vt) {
-  float l0 = 0.f, l1 = 0.f, d0 = 0.f, d1 = 0.f, u0 = 0.f, u1 = 0.f;
+  float l0, l1, d0, d1, u0, u1;
   rows_bdot(l0, l1, o.lr[0], o.lr[1], vt);
   rows_sdot(d0, d1, th_row, th_row + 8 * RowsGeo::TSTR, vt + RowsGeo::BSTR);
   rows_bdot(u0, u1, o.lc[0], o.lc[1], vt + 2 * RowsGeo::BSTR);
@@ -230,7 +244,7 @@ __device__ __forceinline__ void rows_smv(float (&y)[2], const RowOps& o, const f
 // 7e-6 with the explicit Theta product.
 __device__ __forceinline__ void rows_smv_prec(float (&y)[2], const RowOps& o, const float* vt, const float (&fw)[2],
                                               const float (&r)[2]) {
-  float l0 = 0.f, l1 = 0.f, u0 = 0.f, u1 = 0.f;
+  float l0, l1, u0, u1;
   rows_bdot(l0, l1, o.lr[0], o.lr[1], vt);
   rows_bdot(u0, u1, o.lc[0], o.lc[1], vt + 2 * RowsGeo::BSTR);
   y[0] = (l0 + (fw[0] - r[0])) + u0;
@@ -256,7 +270,7 @@ __device__ __forceinline__ void rows_prec(float (&z)[2], float (&fw)[2], const f
   wrow[q] = w0;
   wrow[q + 8] = w1;
   __syncthreads();
-  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  float a0, a1, b0, b1;
   rows_bdot(a0, a1, o.lr[0], o.lr[1], wb);
   rows_bdot(b0, b1, o.lc[0], o.lc[1], wb + 2 * VS);
   fw[0] = a0 + b0;
@@ -282,12 +296,10 @@ struct __align__(16) RowOpsSave {
 #pragma unroll
     for (int c = 0; c < 24; ++c) {
       const float4 w = p[c];
-      float* dst = c < 8 ? &o.ti[c >> 2][(c & 3) * 4] : (c < 16 ? &o.lr[(c - 8) >> 2][(c & 3) * 4]
-                                                               : &o.lc[(c - 16) >> 2][(c & 3) * 4]);
-      dst[0] = w.x;
-      dst[1] = w.y;
-      dst[2] = w.z;
-      dst[3] = w.w;
+      float2* dst = c < 8 ? &o.ti[c >> 2][(c & 3) * 2] : (c < 16 ? &o.lr[(c - 8) >> 2][(c & 3) * 2]
+                                                                : &o.lc[(c - 16) >> 2][(c & 3) * 2]);
+      dst[0] = f2lo(w);
+      dst[1] = f2hi(w);
     }
   }
 };
