@@ -103,3 +103,44 @@ def test_interleaved_empty_batch_and_unsupported_sizes():
     assert lib.tmpc_riccati_factor_il_f64(d, 1, 1, None, None) == -3  # fp64 instances stop at n = 12
     d = _ffi.TmpcDims(4, 5, 17, 17, 0, 0)
     assert lib.tmpc_riccati_factor_il_f32(d, 1, 1, None, None) == -3
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+@pytest.mark.parametrize("nb,nx,nu,N", [(70, 6, 3, 12), (33, 12, 4, 9)])
+def test_interleaved_staged_and_global_memory_kernels_agree(dtype, nb, nx, nu, N):
+    """16-byte aligned arrays run the kernels that stage each stage's blocks in
+    shared memory with cp.async; arrays offset by one element (not 16-byte
+    aligned) run the kernels that read global memory directly.  Same
+    arithmetic in the same order: the results agree to rounding."""
+    n = nx + nu
+    if dtype == torch.float64 and n > 12:
+        pytest.skip("fp64 interleaved instances cover n <= 12")
+    S = _schur(nb, nx, nu, N, dtype, seed=7)
+    T = N + 1
+    d = _ffi.TmpcDims(nb, T, n, n, 0, 0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rhs = torch.randn(nb, T, n, generator=g, device="cuda", dtype=dtype)
+    ops_il = ops.schur_interleave(S)
+    rhs_il = ops.interleave(rhs)
+    fac, st = ops.riccati_factor_il(ops_il, d)
+    x = ops.riccati_solve_il(fac, d, rhs_il)
+
+    def shifted(t):  # same values at an address 1 element past a 16-byte boundary
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+        v = buf[1:]
+        v.copy_(t.reshape(-1))
+        assert v.data_ptr() % 16 != 0
+        return v
+
+    ops_u, rhs_u = shifted(ops_il), shifted(rhs_il)
+    fac_u, x_u = shifted(torch.zeros_like(fac)), shifted(torch.zeros_like(x))
+    _, st_u = ops.riccati_factor_il(ops_u, d, factor=fac_u)
+    ops.riccati_solve_il(fac_u, d, rhs_u, out=x_u)
+    torch.cuda.synchronize()
+    assert int(st.abs().sum()) == 0 and int(st_u.abs().sum()) == 0
+    tol = 1e-12 if dtype == torch.float64 else 1e-6
+    assert rel_err(fac_u.cpu().numpy(), fac.reshape(-1).cpu().numpy()) < tol
+    # the solution slots of the padding problems (past nb) are never written
+    xa = ops.deinterleave(x, (nb, T, n)).cpu().numpy()
+    xb = ops.deinterleave(x_u.clone(), (nb, T, n)).cpu().numpy()
+    assert rel_err(xb, xa) < tol

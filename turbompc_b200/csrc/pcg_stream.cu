@@ -81,15 +81,6 @@ __global__ void __launch_bounds__(256) assemble_stream_kernel(TmpcQP qpa, const 
 
 constexpr int kStreamThreads = 256;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(a), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
 
 // Per-warp staging buffer size (elements): 2 slots x stages per pass x {D, L}.
 template <int NB, int G>

@@ -220,4 +220,17 @@ int dispatch_nb(int n, F&& f) {
   return TMPC_ERR_UNSUPPORTED;
 }
 
+// Asynchronous 16-byte global -> shared copies (cp.async, cached in L2 only),
+// committed in groups and waited for by group count; no registers are held
+// while the copies are in flight.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(a), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 }  // namespace tmpc
