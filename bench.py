@@ -32,7 +32,7 @@ METRIC = "MPC solves/sec (quadrotor N=50, batch 65536)"
 # profiles/admm_rows_quadrotor_b592_fp32.txt (592 problems, scaled per problem:
 # the kernel reads each problem's QP once and writes its state once, so the
 # traffic grows in proportion to the problems processed).
-NCU_DRAM_BYTES_PER_PROBLEM = 258.0e3
+NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
 
 
 def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG):
@@ -83,7 +83,7 @@ def fp32_peak_tflops():
 # Shared-memory pipe share (l1tex data-pipe wavefronts, % of peak) of the
 # fused kernel on this workload, from the ncu capture summarised in
 # profiles/admm_rows_quadrotor_b592_fp32.txt.
-NCU_SMEM_PIPE_SHARE = 0.484
+NCU_SMEM_PIPE_SHARE = 0.502
 
 
 class ClockSampler:
