@@ -222,7 +222,7 @@ def admm_only(nb, linsys="auto", reps=3, pcg=PCG, admm=ADMM):
 
     b = synthetic.random_lti(nb, 12, 4, N_HORIZON, seed=0)
     qd = synthetic.to_qpdata(b, dtype=torch.float32, device="cuda")
-    ls = _ffi.LINSYS_PCG if linsys == "auto" else _ffi.LINSYS_PCG_PACKED
+    ls = {"auto": _ffi.LINSYS_PCG, "packed": _ffi.LINSYS_PCG_PACKED, "direct": _ffi.LINSYS_DIRECT}[linsys]
     cfg = ops.AdmmConfig(max_iter=admm, pcg_max_iter=pcg, check_every=0, adapt_rho_every=0, eps_abs=0.0,
                          eps_rel=0.0, pcg_eps=0.0, linsys=ls)
     s0 = ops.admm_initial_state(qd, 0.1)
@@ -511,8 +511,8 @@ def main():
     ap.add_argument("--admm-only", type=int, default=0, metavar="NB",
                     help="profiling aid: one fused ADMM launch (30 ADMM x 30 PCG, fp32) on NB quadrotor-shaped "
                          "synthetic QPs, then exit")
-    ap.add_argument("--admm-linsys", default="auto", choices=["auto", "packed"],
-                    help="with --admm-only: auto (register-resident kernel where it applies) or the packed kernel")
+    ap.add_argument("--admm-linsys", default="auto", choices=["auto", "packed", "direct"],
+                    help="with --admm-only: auto (register-resident kernel where it applies), the packed kernel, or the direct (block-Cholesky) solve")
     ap.add_argument("--admm-pcg", type=int, default=PCG, help="with --admm-only: PCG iterations per ADMM iteration")
     ap.add_argument("--admm-iters", type=int, default=ADMM, help="with --admm-only: ADMM iterations per launch")
     ap.add_argument("--il-only", default="", metavar="POINT",

@@ -22,6 +22,8 @@ template <typename R>
 size_t admm_ws_bytes_cfg(const TmpcDims& d, const TmpcAdmmConfig* cfg) {
   if (!cfg || cfg->linsys != TMPC_LINSYS_DIRECT) return admm_ws_bytes<R>(d);
   if (d.n > 32) return 0;  // the direct solve is compiled for n <= 32
+  const size_t il = admm_il_ws_bytes<R>(d);  // the batch-interleaved path where it applies
+  if (il > 0) return il;
   size_t out = 0;
   dispatch_nb(d.n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
@@ -73,7 +75,10 @@ int admm_solve(const TmpcDims* d, const TmpcQP* qp, const TmpcAdmmState* in, con
   }
   return dispatch_nb(d->n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    if (cfg->linsys == TMPC_LINSYS_DIRECT) return launch_admm_direct_nb<NB, R>(P, ws_bytes, st);
+    if (cfg->linsys == TMPC_LINSYS_DIRECT) {
+      if (admm_il_ws_bytes<R>(*d) > 0) return launch_admm_direct_il<R>(P, ws_bytes, st);
+      return launch_admm_direct_nb<NB, R>(P, ws_bytes, st);
+    }
     return launch_admm_nb<NB, R>(P, ws_bytes, st);
   });
 }

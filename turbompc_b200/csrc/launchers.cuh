@@ -35,6 +35,14 @@ template <typename R>
 int assemble_generic(const TmpcDims* d, const TmpcQP* qp, const R* rho, R sigma, R rff, R* S, R* P, int32_t* status,
                      cudaStream_t st);
 
+// Direct solve on the batch-interleaved layout (admm_il.cu): workspace bytes
+// (0 where it does not apply) and the launch (TMPC_ERR_UNSUPPORTED where it
+// does not apply).
+template <typename R>
+size_t admm_il_ws_bytes(const TmpcDims& d);
+template <typename R>
+int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t st);
+
 // Register-resident kernel for 8 < n <= 16, T <= 64, fp32 (admm_rows.cu).
 bool admm_rows_ok(int T, int n, int nx, int n0, int m);
 int launch_admm_rows(const AdmmParams<float>& P, cudaStream_t st);
