@@ -45,7 +45,7 @@
 namespace tmpc {
 namespace il {
 
-constexpr int kIlWarps = 8;
+constexpr int kIlWarps = 16;  // one warp per stage row (NB <= 16)
 constexpr int kIlThreads = 32 * kIlWarps;
 
 // Element counts per problem of the interleaved workspace arrays.
@@ -150,31 +150,114 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
 }
 
 // ---------------------------------------------------------------------------
-// Theta_t (lower, packed) and Phi_t of one problem at its rho, written into
-// the interleaved operator (the factor's input format), one CTA per problem,
-// with the assembly arithmetic of assemble.cuh.
+// Theta_t (lower, packed) and Phi_t at each problem's rho, written into the
+// interleaved operator (the factor's input format): one thread per (problem,
+// stage), the 32 problems of a group in one warp.  The sums of assemble.cuh
+// (admm.py:93-101), in the same order, formed as rank-1 updates of register
+// accumulators, one row of G / A0 / A- / A+ at a time (each row read once,
+// coalesced from the interleaved copies):
+//   Theta = ((D + sigma I) + rho_ineq sum_k g_k g_k^T) + rho_f sum_k a_k a_k^T
+//   Phi_t = E_t + rho_f sum_k Ap_t[k]^T Am_t[k]   (rows of Phi in two halves)
+// D and E come from the caller's problem-major arrays (Theta's element (r, c),
+// r >= c, takes D[c][r], as the other assembly paths do).
 // ---------------------------------------------------------------------------
-template <typename R>
-struct IlOpAcc {
-  R* ops;
-  int b, T, n;
-  size_t E;
-  __device__ void set_theta(int t, int i, int j, R v) const {  // i <= j: lower element (j, i)
-    if (i < n && j < n) ops[ix(b, E, (size_t)t * tri(n) + LI(j, i))] = v;
-  }
-  __device__ void set_phi(int t, int i, int j, R v) const {
-    if (i < n && j < n) ops[ix(b, E, (size_t)T * tri(n) + ((size_t)t * n + i) * n + j)] = v;
-  }
-};
-
 template <int NB, typename R>
-__global__ void __launch_bounds__(128) il_assemble_kernel(IlArgs<R> A, TmpcQP qp, const int* gate) {
+__global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP qp, const int* gate) {
   if (gate && *gate == 0) return;
-  const int b = blockIdx.x;
-  const QPView<R> v = qp_view<R>(qp, b, A.T, A.n, A.nx, A.n0, A.m);
-  const R rho = A.rho[b];
-  const IlOpAcc<R> acc{A.ops, b, A.T, A.n, op_elems(A.T, A.n)};
-  assemble_theta_phi<NB>(acc, v, rho * A.rff, rho, A.sigma, A.T, A.n, A.nx, A.n0, A.m);
+  constexpr int TR = NB * (NB + 1) / 2;
+  constexpr int HB = NB / 2;
+  static_assert(HB * NB <= TR, "Phi half-block fits the accumulators");
+  const int lane = threadIdx.x, t = blockIdx.y, grp = blockIdx.x;
+  const int b = grp * kWarp + lane;
+  if (b >= A.Nb) return;
+  const int T = A.T, N = T - 1, n = A.n, nx = A.nx, n0 = A.n0, m = A.m;
+  const IlSizes z(T, n, nx, n0, m);
+  const int trin = (int)tri(n);
+  const R rho = A.rho[b], rf = rho * A.rff;
+  auto lv = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp + lane; };
+  R* O = lv(A.ops, z.ops);
+  const R* Gl = m > 0 ? lv(A.g, z.g) : nullptr;
+  const R* A0l = n0 > 0 ? lv(A.a0, z.a0) : nullptr;
+  const R* AMl = lv(A.am, z.am);
+  const R* APl = lv(A.ap, z.am);
+  const R* D = static_cast<const R*>(qp.D) + ((size_t)b * T + t) * n * n;
+  R acc[TR];
+  // rank-1 updates acc += a a^T from a row of n values at p (interleaved, stride 32)
+  auto rank1 = [&](const R* p) {
+    R a[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) a[j] = j < n ? p[j * kWarp] : R(0);
+#pragma unroll
+    for (int r = 0; r < NB; ++r)
+#pragma unroll
+      for (int c = 0; c <= r; ++c) acc[LI(r, c)] = fma(a[c], a[r], acc[LI(r, c)]);
+  };
+  // ---- Theta_t: (D + sigma I) + rho_ineq G^T G
+#pragma unroll
+  for (int e = 0; e < TR; ++e) acc[e] = R(0);
+  for (int k = 0; k < m; ++k) rank1(Gl + (size_t)(t * m + k) * n * kWarp);
+#pragma unroll
+  for (int r = 0; r < NB; ++r)
+#pragma unroll
+    for (int c = 0; c <= r; ++c) {
+      if (r < n) {
+        R v = D[c * n + r];
+        if (r == c) v += A.sigma;
+        v += rho * acc[LI(r, c)];
+        acc[LI(r, c)] = v;
+      }
+    }
+  // park (D + sigma I) + rho G^T G in the output, then + rho_f A^T A
+#pragma unroll
+  for (int r = 0; r < NB; ++r)
+#pragma unroll
+    for (int c = 0; c <= r; ++c)
+      if (r < n) O[(size_t)(t * trin + LI(r, c)) * kWarp] = acc[LI(r, c)];
+#pragma unroll
+  for (int e = 0; e < TR; ++e) acc[e] = R(0);
+  if (t == 0) {
+    for (int k = 0; k < n0; ++k) rank1(A0l + (size_t)k * n * kWarp);
+    if (N > 0)
+      for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)k * n * kWarp);
+  } else {
+    for (int k = 0; k < nx; ++k) rank1(APl + (size_t)((t - 1) * nx + k) * n * kWarp);
+    if (t < N)
+      for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)(t * nx + k) * n * kWarp);
+  }
+#pragma unroll
+  for (int r = 0; r < NB; ++r)
+#pragma unroll
+    for (int c = 0; c <= r; ++c)
+      if (r < n) {
+        R* o = O + (size_t)(t * trin + LI(r, c)) * kWarp;
+        *o = *o + rf * acc[LI(r, c)];
+      }
+  if (t >= N) return;
+  // ---- Phi_t = E_t + rho_f Ap_t^T Am_t, rows [h, h + NB/2)
+  const R* E = static_cast<const R*>(qp.E) + ((size_t)b * N + t) * n * n;
+  for (int h = 0; h < n; h += HB) {
+#pragma unroll
+    for (int e = 0; e < HB * NB; ++e) acc[e] = R(0);
+    for (int k = 0; k < nx; ++k) {
+      const R* ap = APl + (size_t)(t * nx + k) * n * kWarp;
+      const R* am = AMl + (size_t)(t * nx + k) * n * kWarp;
+      R x[HB], y[NB];
+#pragma unroll
+      for (int i = 0; i < HB; ++i) x[i] = h + i < n ? ap[(h + i) * kWarp] : R(0);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) y[j] = j < n ? am[j * kWarp] : R(0);
+#pragma unroll
+      for (int i = 0; i < HB; ++i)
+#pragma unroll
+        for (int j = 0; j < NB; ++j) acc[i * NB + j] = fma(x[i], y[j], acc[i * NB + j]);
+    }
+#pragma unroll
+    for (int i = 0; i < HB; ++i)
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+        if (h + i < n && j < n)
+          O[(size_t)(T * trin + (t * n + h + i) * n + j) * kWarp] = E[(h + i) * n + j] + rf * acc[i * NB + j];
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -247,85 +330,116 @@ size_t il_admm_smem(int n, int nx, int n0, int m) {
   return e * kWarp * sizeof(R);
 }
 
+// sum_{k < cnt} a[k sa] v[k 32] with four partial sums, unrolled to NB terms
+// (a and v point at this lane's element 0).
 template <int NB, typename R>
+__device__ __forceinline__ R il_dot(const R* a, int sa, const R* v, int cnt) {
+  R s[4] = {R(0), R(0), R(0), R(0)};
+#pragma unroll
+  for (int k = 0; k < NB; ++k)
+    if (k < cnt) s[k & 3] = fma(a[k * sa], v[k * kWarp], s[k & 3]);
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+// EX: n == NB, so every stage-block loop has compile-time bounds and strides.
+template <int NB, typename R, bool EX>
 __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> A, int it0, int it1) {
   constexpr int NW = kIlWarps;
-  constexpr int RPT = (NB + NW - 1) / NW;  // rows of a stage per thread
+  static_assert(NB <= NW, "one warp per stage row");
   constexpr int V = 16 / sizeof(R);
+  constexpr int L32 = kWarp;
   extern __shared__ __align__(16) unsigned char il_smem[];
   const int lane = threadIdx.x & (kWarp - 1), w = threadIdx.x / kWarp;
   const int grp = blockIdx.x;
   const int b = grp * kWarp + lane;
-  const int T = A.T, N = T - 1, n = A.n, nx = A.nx, n0 = A.n0, m = A.m;
+  const int T = A.T, N = T - 1, n = EX ? NB : A.n, nx = A.nx, n0 = A.n0, m = A.m;
   const bool act = b < A.Nb && A.act[b] != 0;
   if (!__syncthreads_or(act)) return;  // every problem of the group has converged
   const IlSizes z(T, n, nx, n0, m);
-  const size_t trin = tri(n), nn = (size_t)n * n, woff = (size_t)T * trin;
-  const R rho = A.rho[b], rf = rho * A.rff, al = A.alpha, sw = A.sw[b];
+  const int trin = (int)tri(n), nn = n * n, woff = T * trin;
+  const R rho = A.rho[b], rf = rho * A.rff, al = A.alpha, sw = A.sw[b], sigma = A.sigma;
   const bool slack = A.use_slack != 0;
-  // group bases of the interleaved arrays (element e, lane: base[e * 32 + lane])
+  // group bases of the interleaved arrays (element e of this group: base[e * 32 + lane])
   auto gb = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp; };
-  R* F = gb(A.ops, z.ops);
-  R* Q = gb(A.q, z.q);
-  R* AM = gb(A.am, z.am);
-  R* AP = gb(A.ap, z.am);
-  R* Gm = m > 0 ? gb(A.g, z.g) : nullptr;
-  R* CC = gb(A.c, z.c);
-  R* LL = m > 0 ? gb(A.l, z.lu) : nullptr;
-  R* UU = m > 0 ? gb(A.u, z.lu) : nullptr;
-  R* X = gb(A.x, z.x);
+  const R* F = gb(A.ops, z.ops);
+  const R* Q = gb(A.q, z.q);
+  const R* AM = gb(A.am, z.am);
+  const R* AP = gb(A.ap, z.am);
+  const R* Gm = m > 0 ? gb(A.g, z.g) : nullptr;
+  const R* CC = gb(A.c, z.c);
+  const R* LL = m > 0 ? gb(A.l, z.lu) : nullptr;
+  const R* UU = m > 0 ? gb(A.u, z.lu) : nullptr;
+  R* X = gb(A.x, z.x) + lane;
   R* YFD = gb(A.yfd, z.yfd);
   R* ZG = m > 0 ? gb(A.zg, z.zm) : nullptr;
   R* YG = m > 0 ? gb(A.yg, z.zm) : nullptr;
-  R* XIG = m > 0 ? gb(A.xig, z.zm) : nullptr;
+  R* XIG = m > 0 ? gb(A.xig, z.zm) + lane : nullptr;
   R* GAM = gb(A.gam, z.x);
   R* YS = gb(A.ys, z.x);
+  R* const A0l = n0 > 0 ? gb(A.a0, z.a0) + lane : nullptr;
+  R* const C0l = n0 > 0 ? gb(A.c0, z.c0) + lane : nullptr;
+  R* const YF0l = n0 > 0 ? gb(A.yf0, z.yf0) + lane : nullptr;
   R* sm = reinterpret_cast<R*>(il_smem);
   const int SA = il_fwd_elems(n), SB = il_buf_b_elems(n, nx, m);
   R* BA = sm;
-  R* BB = sm + (size_t)SA * kWarp;
-  R* ush = BB + (size_t)SB * kWarp;
-  R* xs0 = ush + NB * kWarp;
-  R* xs1 = xs0 + NB * kWarp;
-  R* ctv = xs1 + NB * kWarp;
-  R* gtv = ctv + (size_t)nx * kWarp;
-  R* ct0v = gtv + (size_t)m * kWarp;
-  auto S = [&](R* p, int e) -> R& { return p[(size_t)e * kWarp + lane]; };  // shared / group element e of this lane
-  // copy `elems` interleaved elements from src (group base + e0 * 32) to dst, 16 bytes per cp.async
+  R* BB = sm + SA * L32;
+  R* ush = BB + SB * L32;
+  R* xs0 = ush + NB * L32;
+  R* xs1 = xs0 + NB * L32;
+  R* ctv = xs1 + NB * L32;
+  R* gtv = ctv + nx * L32;
+  R* ct0v = gtv + m * L32;
+  // copy `elems` interleaved elements (contiguous from src) to dst, 16 bytes per cp.async
   auto copy = [&](R* dst, const R* src, int elems) {
-    const int chunks = elems * kWarp / V;
+    const int chunks = elems * (L32 / V);
     for (int c = threadIdx.x; c < chunks; c += kIlThreads) cp_async16(dst + c * V, src + c * V);
   };
   // buffer B (backward) offsets
   const int oAm = 0, oAp = nx * n, oG = 2 * nx * n, oq = oG + m * n, oc = oq + n, ox = oc + nx, oyf = ox + n,
             ozg = oyf + nx, oyg = ozg + m, ol = oyg + m, ou = ol + m;
   auto fetch_fwd = [&](R* dst, int t) {
-    copy(dst, F + (size_t)t * trin * kWarp, (int)trin);
-    if (t > 0) copy(dst + trin * kWarp, F + (woff + (size_t)(t - 1) * nn) * kWarp, (int)nn);
-    copy(dst + (trin + nn) * kWarp, GAM + (size_t)t * n * kWarp, n);
+    copy(dst, F + (size_t)t * trin * L32, trin);
+    if (t > 0) copy(dst + trin * L32, F + ((size_t)woff + (size_t)(t - 1) * nn) * L32, nn);
+    copy(dst + (trin + nn) * L32, GAM + (size_t)t * n * L32, n);
   };
   auto fetch_bwd_a = [&](int t) {
-    copy(BA, F + (size_t)t * trin * kWarp, (int)trin);
-    if (t < N) copy(BA + trin * kWarp, F + (woff + (size_t)t * nn) * kWarp, (int)nn);
-    copy(BA + (trin + nn) * kWarp, YS + (size_t)t * n * kWarp, n);
+    copy(BA, F + (size_t)t * trin * L32, trin);
+    if (t < N) copy(BA + trin * L32, F + ((size_t)woff + (size_t)t * nn) * L32, nn);
+    copy(BA + (trin + nn) * L32, YS + (size_t)t * n * L32, n);
   };
   auto fetch_bwd_b = [&](int t) {
     if (t < N) {
-      copy(BB + (size_t)oAm * kWarp, AM + (size_t)t * nx * n * kWarp, nx * n);
-      copy(BB + (size_t)oAp * kWarp, AP + (size_t)t * nx * n * kWarp, nx * n);
-      copy(BB + (size_t)oc * kWarp, CC + (size_t)t * nx * kWarp, nx);
-      copy(BB + (size_t)oyf * kWarp, YFD + (size_t)t * nx * kWarp, nx);
+      copy(BB + oAm * L32, AM + (size_t)t * nx * n * L32, nx * n);
+      copy(BB + oAp * L32, AP + (size_t)t * nx * n * L32, nx * n);
+      copy(BB + oc * L32, CC + (size_t)t * nx * L32, nx);
+      copy(BB + oyf * L32, YFD + (size_t)t * nx * L32, nx);
     }
     if (m > 0) {
-      copy(BB + (size_t)oG * kWarp, Gm + (size_t)t * m * n * kWarp, m * n);
-      copy(BB + (size_t)ozg * kWarp, ZG + (size_t)t * m * kWarp, m);
-      copy(BB + (size_t)oyg * kWarp, YG + (size_t)t * m * kWarp, m);
-      copy(BB + (size_t)ol * kWarp, LL + (size_t)t * m * kWarp, m);
-      copy(BB + (size_t)ou * kWarp, UU + (size_t)t * m * kWarp, m);
+      copy(BB + oG * L32, Gm + (size_t)t * m * n * L32, m * n);
+      copy(BB + ozg * L32, ZG + (size_t)t * m * L32, m);
+      copy(BB + oyg * L32, YG + (size_t)t * m * L32, m);
+      copy(BB + ol * L32, LL + (size_t)t * m * L32, m);
+      copy(BB + ou * L32, UU + (size_t)t * m * L32, m);
     }
-    copy(BB + (size_t)oq * kWarp, Q + (size_t)t * n * kWarp, n);
-    copy(BB + (size_t)ox * kWarp, X + (size_t)t * n * kWarp, n);
+    copy(BB + oq * L32, Q + (size_t)t * n * L32, n);
+    copy(BB + ox * L32, gb(A.x, z.x) + (size_t)t * n * L32, n);
   };
+  // this lane's views of the buffers and vectors
+  R* const BAl = BA + lane;
+  R* const BBl = BB + lane;
+  R* const ushl = ush + lane;
+  R* const xs0l = xs0 + lane;
+  R* const xs1l = xs1 + lane;
+  R* const ctvl = ctv + lane;
+  R* const gtvl = gtv + lane;
+  R* const ct0vl = ct0v + lane;
+  R* const YSl = YS + lane;
+  R* const GAMl = GAM + lane;
+  R* const YFDl = YFD + lane;
+  R* const ZGl = m > 0 ? ZG + lane : nullptr;
+  R* const YGl = m > 0 ? YG + lane : nullptr;
+  const int i = w;  // the stage row / column this warp owns (NB <= NW)
+  const bool own = i < n;
 
   for (int it = it0; it < it1; ++it) {
     // ---------------- forward sweep: y_t = L_t^-1 (gamma_t - W_{t-1} y_{t-1})
@@ -334,180 +448,136 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
     fetch_fwd(BB, 1);
     cp_async_commit();
     for (int t = 0; t < T; ++t) {
-      R* buf = (t & 1) ? BB : BA;
+      R* bufl = ((t & 1) ? BB : BA) + lane;
       cp_async_wait<1>();
       __syncthreads();
-      R* Wb = buf + trin * kWarp;
-      R* gb_ = buf + (trin + nn) * kWarp;
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int i = w + NW * r;
-        if (i < n) {
-          R u = S(gb_, i);
-          if (t > 0)
-            for (int k = 0; k < n; ++k) u = fma(-S(Wb, i * n + k), S(xs0, k), u);
-          S(ush, i) = u;
-        }
+      if (own) {
+        R u = bufl[(trin + nn + i) * L32];
+        if (t > 0) u -= il_dot<NB>(bufl + (trin + i * n) * L32, L32, xs0l, n);
+        ushl[i * L32] = u;
       }
       __syncthreads();
-      R y[RPT];
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int i = w + NW * r;
-        R acc = R(0);
-        if (i < n) {
-          for (int c = 0; c <= i; ++c) acc = fma(S(buf, LI(i, c)), S(ush, c), acc);
-          if (act) S(YS, t * n + i) = acc;
-        }
-        y[r] = acc;
+      R y = R(0);
+      if (own) {
+        y = il_dot<NB>(bufl + (i * (i + 1) / 2) * L32, L32, ushl, i + 1);
+        if (act) YSl[(t * n + i) * L32] = y;
       }
       __syncthreads();  // every read of this stage's buffer, ush and xs0 is done
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int i = w + NW * r;
-        if (i < n) S(xs0, i) = y[r];
-      }
-      if (t + 2 < T) fetch_fwd(buf, t + 2);
+      if (own) xs0l[i * L32] = y;
+      if (t + 2 < T) fetch_fwd(bufl - lane, t + 2);
       cp_async_commit();
     }
     cp_async_wait<0>();
     __syncthreads();
 
     // ---------------- backward sweep with the ADMM-level updates
-    // x~_{t+1} in xs[(t + 1) & 1], x~_t into xs[t & 1]; gamma_t's pieces of
-    // step t wait in registers for the A+ terms of step t - 1.
-    R gval[RPT], gam_[RPT], giq[RPT];
-#pragma unroll
-    for (int r = 0; r < RPT; ++r) {
-      gval[r] = gam_[r] = giq[r] = R(0);
-      const int i = w + NW * r;
-      if (i < n) S((N & 1) ? xs0 : xs1, i) = R(0);  // x~_T = 0 (slot of t = N + 1)
-    }
+    // x~_{t+1} in xs[(t + 1) & 1], x~_t into xs[t & 1]; the pieces of gamma_t
+    // formed at step t wait in registers for the A+ terms of step t - 1.
+    R gval = R(0), geq = R(0), giq = R(0);
     fetch_bwd_a(N);
     cp_async_commit();
     fetch_bwd_b(N);
     cp_async_commit();
     for (int t = N; t >= 0; --t) {
-      R* xt = (t & 1) ? xs1 : xs0;   // x~_t
-      R* xn = (t & 1) ? xs0 : xs1;   // x~_{t+1}
+      R* xtl = (t & 1) ? xs1l : xs0l;  // x~_t
+      R* xnl = (t & 1) ? xs0l : xs1l;  // x~_{t+1}
       cp_async_wait<1>();
       __syncthreads();
-      R* Wb = BA + trin * kWarp;
-      R* yb = BA + (trin + nn) * kWarp;
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int k = w + NW * r;
-        if (k < n) {
-          R u = S(yb, k);
-          if (t < N)
-            for (int i = 0; i < n; ++i) u = fma(-S(Wb, i * n + k), S(xn, i), u);
-          S(ush, k) = u;
-        }
+      if (own) {
+        R u = BAl[(trin + nn + i) * L32];
+        if (t < N) u -= il_dot<NB>(BAl + (trin + i) * L32, n * L32, xnl, n);  // column i of W_t
+        ushl[i * L32] = u;
       }
       __syncthreads();
-      R xv[RPT];
+      R xv = R(0);
+      if (own) {  // row i of L_t^-T: sum_{r >= i} Linv[r][i] u_r
+        R s[4] = {R(0), R(0), R(0), R(0)};
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int k = w + NW * r;
-        R acc = R(0);
-        if (k < n) {
-          for (int i = k; i < n; ++i) acc = fma(S(BA, LI(i, k)), S(ush, i), acc);
-          S(xt, k) = acc;
-        }
-        xv[r] = acc;
+        for (int r = 0; r < NB; ++r)
+          if (r >= i && r < n) s[r & 3] = fma(BAl[(r * (r + 1) / 2 + i) * L32], ushl[r * L32], s[r & 3]);
+        xv = (s[0] + s[1]) + (s[2] + s[3]);
+        xtl[i * L32] = xv;
       }
       cp_async_wait<0>();
       __syncthreads();  // x~_t complete, buffer B of stage t landed, buffer A consumed
       if (t > 0) fetch_bwd_a(t - 1);
       cp_async_commit();
-      // dynamics rows of stage t: C x~ = Am_t x~_t + Ap_t x~_{t+1}
-      if (t < N) {
-        for (int r = w; r < nx; r += NW) {
-          R s1 = R(0), s2 = R(0);
-          for (int j = 0; j < n; ++j) s1 = fma(S(BB, oAm + r * n + j), S(xt, j), s1);
-          for (int j = 0; j < n; ++j) s2 = fma(S(BB, oAp + r * n + j), S(xn, j), s2);
-          const R cx = s1 + s2;
-          const R cr = S(BB, oc + r);
-          const R y = S(BB, oyf + r) + rf * al * (cx - cr);
-          if (act) S(YFD, t * nx + r) = y;
-          S(ctv, r) = rf * cr - y;
-        }
-      }
-      // inequality rows of stage t
-      for (int k = w; k < m; k += NW) {
-        R gx = R(0);
-        for (int j = 0; j < n; ++j) gx = fma(S(BB, oG + k * n + j), S(xt, j), gx);
-        const R zold = S(BB, ozg + k), ygo = S(BB, oyg + k);
-        const R zt = al * gx + (R(1) - al) * zold + ygo / rho;
-        R cl = zt;
-        const R lb = S(BB, ol + k), ub = S(BB, ou + k);
-        if (cl < lb) cl = lb;
-        if (cl > ub) cl = ub;
-        R znew;
-        if (slack) {
-          const R f = sw / (sw + rho);
-          znew = (R(1) - f) * zt + f * cl;
-          if (act) S(XIG, t * m + k) = (rho / (sw + rho)) * (cl - zt);
+      // constraint rows of stage t: dynamics (A- x~_t + A+ x~_{t+1}), inequality, initial
+      for (int q = w; q < nx + m; q += NW) {
+        if (q < nx) {
+          if (t < N) {
+            const R cx = il_dot<NB>(BBl + (oAm + q * n) * L32, L32, xtl, n) +
+                         il_dot<NB>(BBl + (oAp + q * n) * L32, L32, xnl, n);
+            const R cr = BBl[(oc + q) * L32];
+            const R y = BBl[(oyf + q) * L32] + rf * al * (cx - cr);
+            if (act) YFDl[(t * nx + q) * L32] = y;
+            ctvl[q * L32] = rf * cr - y;
+          }
         } else {
-          znew = cl;
+          const int k = q - nx;
+          const R gx = il_dot<NB>(BBl + (oG + k * n) * L32, L32, xtl, n);
+          const R zold = BBl[(ozg + k) * L32], ygo = BBl[(oyg + k) * L32];
+          const R zt = al * gx + (R(1) - al) * zold + ygo / rho;
+          R cl = zt;
+          const R lb = BBl[(ol + k) * L32], ub = BBl[(ou + k) * L32];
+          if (cl < lb) cl = lb;
+          if (cl > ub) cl = ub;
+          R znew;
+          if (slack) {
+            const R f = sw / (sw + rho);
+            znew = (R(1) - f) * zt + f * cl;
+            if (act) XIG[(t * m + k) * L32] = (rho / (sw + rho)) * (cl - zt);
+          } else {
+            znew = cl;
+          }
+          const R ygn = ygo + rho * (al * gx + (R(1) - al) * zold - znew);
+          if (act) {
+            ZGl[(t * m + k) * L32] = znew;
+            YGl[(t * m + k) * L32] = ygn;
+          }
+          gtvl[k * L32] = rho * znew - ygn;
         }
-        const R ygn = ygo + rho * (al * gx + (R(1) - al) * zold - znew);
-        if (act) {
-          S(ZG, t * m + k) = znew;
-          S(YG, t * m + k) = ygn;
-        }
-        S(gtv, k) = rho * znew - ygn;
       }
-      // initial-condition rows (stage 0)
       if (t == 0) {
         for (int k = w; k < n0; k += NW) {
-          R s = R(0);
-          for (int j = 0; j < n; ++j) s = fma(A.a0[ix(b, z.a0, (size_t)k * n + j)], S(xt, j), s);
-          const R c0 = A.c0[ix(b, z.c0, k)];
-          const R y = A.yf0[ix(b, z.yf0, k)] + rf * al * (s - c0);
-          if (act) A.yf0[ix(b, z.yf0, k)] = y;
-          S(ct0v, k) = rf * c0 - y;
+          const R s = il_dot<NB>(A0l + k * n * L32, L32, xtl, n);
+          const R c0 = C0l[k * L32];
+          const R y = YF0l[k * L32] + rf * al * (s - c0);
+          if (act) YF0l[k * L32] = y;
+          ct0vl[k * L32] = rf * c0 - y;
         }
       }
-      // relaxation of x_t
-      R xr[RPT];
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int j = w + NW * r;
-        xr[r] = R(0);
-        if (j < n) {
-          xr[r] = al * xv[r] + (R(1) - al) * S(BB, ox + j);
-          if (act) S(X, t * n + j) = xr[r];
-        }
+      R xr = R(0);
+      if (own) {  // relaxation of x_t
+        xr = al * xv + (R(1) - al) * BBl[(ox + i) * L32];
+        if (act) X[(t * n + i) * L32] = xr;
       }
       __syncthreads();  // ctv, gtv, ct0v complete
-      // gamma for the next iteration
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int j = w + NW * r;
-        if (j >= n) continue;
-        // A+ terms of the dynamics rows of stage t complete gamma_{t+1}
-        if (t < N) {
-          R ap = R(0);
-          for (int k = 0; k < nx; ++k) ap += S(BB, oAp + k * n + j) * S(ctv, k);
-          if (act) S(GAM, (t + 1) * n + j) = (gval[r] + (ap + gam_[r])) + giq[r];
+      if (own) {  // gamma for the next iteration (column i)
+        if (t < N) {  // the A+ terms of the dynamics rows of stage t complete gamma_{t+1}
+          const R ap = il_dot<NB>(BBl + (oAp + i) * L32, n * L32, ctvl, nx);
+          if (act) GAMl[((t + 1) * n + i) * L32] = (gval + (ap + geq)) + giq;
         }
-        R val = A.sigma * xr[r] - S(BB, oq + j);
+        const R val = sigma * xr - BBl[(oq + i) * L32];
         R eq = R(0);
         if (t == 0) {
-          for (int k = 0; k < n0; ++k) eq += A.a0[ix(b, z.a0, (size_t)k * n + j)] * S(ct0v, k);
+          for (int k = 0; k < n0; ++k) eq += A0l[(k * n + i) * L32] * ct0vl[k * L32];
         }
         if (t < N) {
-          for (int k = 0; k < nx; ++k) eq += S(BB, oAm + k * n + j) * S(ctv, k);
+          if (t == 0) {
+            for (int k = 0; k < nx; ++k) eq += BBl[(oAm + k * n + i) * L32] * ctvl[k * L32];
+          } else {
+            eq = il_dot<NB>(BBl + (oAm + i) * L32, n * L32, ctvl, nx);
+          }
         }
         R iq = R(0);
-        for (int k = 0; k < m; ++k) iq += S(BB, oG + k * n + j) * S(gtv, k);
+        for (int k = 0; k < m; ++k) iq += BBl[(oG + k * n + i) * L32] * gtvl[k * L32];
         if (t == 0) {
-          if (act) S(GAM, j) = (val + eq) + iq;
+          if (act) GAMl[i * L32] = (val + eq) + iq;
         } else {
-          gval[r] = val;
-          gam_[r] = eq;
-          giq[r] = iq;
+          gval = val;
+          geq = eq;
+          giq = iq;
         }
       }
       __syncthreads();  // buffer B, ctv, gtv consumed
@@ -687,14 +757,15 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
     constexpr int NB = decltype(tag)::value;
     const size_t smem = il_admm_smem<NB, R>(n, nx, n0, m);
     const size_t csmem = il_check_smem<NB, R>(T, nx, n0, m);
-    chk((int)cudaFuncSetAttribute(il_admm_kernel<NB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    auto kadmm = n == NB ? il_admm_kernel<NB, R, true> : il_admm_kernel<NB, R, false>;
+    chk((int)cudaFuncSetAttribute(kadmm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     chk((int)cudaFuncSetAttribute(il_check_kernel<NB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem));
     if (rc) return rc;
     const dim3 ggrid((unsigned)groups(Nb), (unsigned)T);
     // operator, factor (in place) and the first gamma; with `gate`, only
     // when a check opened it, gamma only for the flagged problems
     auto build = [&](const int* gate) {
-      il_assemble_kernel<NB, R><<<Nb, 128, 0, st>>>(A, P.qp, gate);
+      il_assemble_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, P.qp, gate);
       chk((int)cudaPeekAtLastError());
       chk(launch_factor<NB, R>(Nb, T, n, A.ops, A.ops, A.fstat, gate, st));
       il_gamma_kernel<R><<<ggrid, kWarp, 0, st>>>(A, gate, gate ? 1 : 0);
@@ -706,7 +777,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
     };
     auto iterate = [&](int a, int e) {
       if (e <= a) return;
-      il_admm_kernel<NB, R><<<(unsigned)groups(Nb), kIlThreads, smem, st>>>(A, a, e);
+      kadmm<<<(unsigned)groups(Nb), kIlThreads, smem, st>>>(A, a, e);
       chk((int)cudaPeekAtLastError());
     };
     build(nullptr);
