@@ -121,6 +121,17 @@ const char* tmpc_error_string(int32_t code);
  * exercise the status path on copies that do complete. */
 uint32_t tmpc_set_transfer_poll_limit(uint32_t polls);
 
+/* Diagnostics hook, no counterpart in the reference.  While enabled, every
+ * tmpc_admm_solve_* call that runs the batch-interleaved direct solve
+ * (linsys = TMPC_LINSYS_DIRECT with n <= 16 in fp32, n <= 12 in fp64) records
+ * a CUDA event pair on its stream around its ADMM iteration kernels (after
+ * the layout conversion, assembly and factor; before the conversion back), at
+ * most 1024 pairs.  _timing(enable) returns the previous setting; _read waits
+ * for the recorded pairs, writes up to max_out elapsed times in ms (call
+ * order), releases every pair and returns the number written. */
+int32_t tmpc_admm_iteration_timing(int32_t enable);
+int32_t tmpc_admm_iteration_timing_read(float* ms_out, int32_t max_out);
+
 /* ---------------------------------------------------------------------------
  * Schur complement + preconditioner assembly.
  * Replaces compute_S_Phiinv (turbompc/solvers/admm/admm.py:71-154): writes the

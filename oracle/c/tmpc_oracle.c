@@ -11,6 +11,10 @@
  *   ADMM loop          admm/csrc/admm_fused.cu:701-925 at fixed iteration counts
  *                      (residual checks / rho adaptation disabled)
  *   PCG                admm/csrc/admm_fused.cu:54-161
+ *   direct solve       (pcg_iters < 0) block-tridiagonal Cholesky of S, factored
+ *                      once per problem and applied every ADMM iteration: the
+ *                      semantics of the cuDSS backend (admm/csrc/admm_cudss.cu),
+ *                      an exact solve of S x = gamma
  * Compiled twice (float / double) from the macro body below.
  */
 #include <math.h>
@@ -65,7 +69,7 @@
   /* S, Phiinv (T, n, 3n) for one problem; scratch: th (T n n), ti (T n n), ph (N n n), w (2 n n) */           \
   static void schur_##SUF(const R* D, const R* E, const R* A0, const R* Am, const R* Ap, const R* G, int T,    \
                           int n, int nx, int n0, int m, R rf, R ri, R sigma, R* S, R* P, R* th, R* ti, R* ph,  \
-                          R* w) {                                                                             \
+                          R* w, int direct) {                                                                 \
     int N = T - 1;                                                                                            \
     for (int t = 0; t < T; ++t)                                                                               \
       for (int i = 0; i < n; ++i)                                                                             \
@@ -94,6 +98,7 @@
             a += Ap[((size_t)t * nx + k) * n + i] * Am[((size_t)t * nx + k) * n + j];                         \
           ph[((size_t)t * n + i) * n + j] = E[((size_t)t * n + i) * n + j] + rf * a;                          \
         }                                                                                                     \
+    if (direct) return;                                                                                       \
     for (int t = 0; t < T; ++t) inv_##SUF(th + (size_t)t * n * n, ti + (size_t)t * n * n, w, n);              \
     memset(S, 0, sizeof(R) * (size_t)T * n * 3 * n);                                                          \
     memset(P, 0, sizeof(R) * (size_t)T * n * 3 * n);                                                          \
@@ -127,6 +132,71 @@
             }                                                                                                 \
             P[((size_t)t * n + i) * 3 * n + (side == 0 ? 0 : 2 * n) + j] = s;                                 \
           }                                                                                                   \
+      }                                                                                                       \
+    }                                                                                                         \
+  }                                                                                                           \
+  /* Block Cholesky S = L L^T in place: th_t <- L_t (lower), ph_t <- W_t = Phi_t L_t^-T, with            \
+     L_0 L_0^T = Theta_0, L_t L_t^T = Theta_t - W_{t-1} W_{t-1}^T.  Returns 0, or -1 on a non-positive pivot. */ \
+  static int chol_##SUF(R* th, R* ph, int T, int n) {                                                         \
+    for (int t = 0; t < T; ++t) {                                                                             \
+      R* L = th + (size_t)t * n * n;                                                                          \
+      if (t > 0) {                                                                                            \
+        const R* W = ph + (size_t)(t - 1) * n * n;                                                            \
+        for (int i = 0; i < n; ++i)                                                                           \
+          for (int j = 0; j <= i; ++j) {                                                                      \
+            R s = 0;                                                                                          \
+            for (int k = 0; k < n; ++k) s += W[i * n + k] * W[j * n + k];                                     \
+            L[i * n + j] -= s;                                                                                \
+          }                                                                                                   \
+      }                                                                                                       \
+      for (int j = 0; j < n; ++j) {                                                                           \
+        R d = L[j * n + j];                                                                                   \
+        for (int k = 0; k < j; ++k) d -= L[j * n + k] * L[j * n + k];                                         \
+        if (!(d > 0)) return -1;                                                                              \
+        d = (R)sqrt((double)d);                                                                               \
+        L[j * n + j] = d;                                                                                     \
+        for (int i = j + 1; i < n; ++i) {                                                                     \
+          R s = L[i * n + j];                                                                                 \
+          for (int k = 0; k < j; ++k) s -= L[i * n + k] * L[j * n + k];                                       \
+          L[i * n + j] = s / d;                                                                               \
+        }                                                                                                     \
+      }                                                                                                       \
+      if (t < T - 1) { /* W_t rows: solve L_t w^T = phi_i^T (forward substitution) */                         \
+        R* W = ph + (size_t)t * n * n;                                                                        \
+        for (int i = 0; i < n; ++i)                                                                           \
+          for (int k = 0; k < n; ++k) {                                                                       \
+            R s = W[i * n + k];                                                                               \
+            for (int c = 0; c < k; ++c) s -= L[k * n + c] * W[i * n + c];                                     \
+            W[i * n + k] = s / L[k * n + k];                                                                  \
+          }                                                                                                   \
+      }                                                                                                       \
+    }                                                                                                         \
+    return 0;                                                                                                 \
+  }                                                                                                           \
+  /* x = S^-1 g with the block Cholesky factor; y scratch (T n) */                                            \
+  static void chol_solve_##SUF(const R* Lb, const R* Wb, const R* g, R* x, R* y, int T, int n) {              \
+    for (int t = 0; t < T; ++t) {                                                                             \
+      const R* L = Lb + (size_t)t * n * n;                                                                    \
+      for (int i = 0; i < n; ++i) {                                                                           \
+        R s = g[t * n + i];                                                                                   \
+        if (t > 0) {                                                                                          \
+          const R* W = Wb + (size_t)(t - 1) * n * n;                                                          \
+          for (int k = 0; k < n; ++k) s -= W[i * n + k] * y[(t - 1) * n + k];                                 \
+        }                                                                                                     \
+        for (int c = 0; c < i; ++c) s -= L[i * n + c] * y[t * n + c];                                         \
+        y[t * n + i] = s / L[i * n + i];                                                                      \
+      }                                                                                                       \
+    }                                                                                                         \
+    for (int t = T - 1; t >= 0; --t) {                                                                        \
+      const R* L = Lb + (size_t)t * n * n;                                                                    \
+      for (int i = n - 1; i >= 0; --i) {                                                                      \
+        R s = y[t * n + i];                                                                                   \
+        if (t < T - 1) {                                                                                      \
+          const R* W = Wb + (size_t)t * n * n;                                                                \
+          for (int k = 0; k < n; ++k) s -= W[k * n + i] * x[(t + 1) * n + k];                                 \
+        }                                                                                                     \
+        for (int r = i + 1; r < n; ++r) s -= L[r * n + i] * x[t * n + r];                                     \
+        x[t * n + i] = s / L[i * n + i];                                                                      \
       }                                                                                                       \
     }                                                                                                         \
   }                                                                                                           \
@@ -177,7 +247,9 @@
       R *xb = x + (size_t)b * k, *ygb = yg + (size_t)b * T * m, *yf0b = yf0 + (size_t)b * n0;                  \
       R *yfdb = yfd + (size_t)b * N * nx, *zgb = zg + (size_t)b * T * m;                                       \
       R rho = rho_in[b], rf = rho * (R)rho_f_factor, al = (R)alpha;                                           \
-      schur_##SUF(Db, Eb, A0b, Amb, Apb, Gb, T, n, nx, n0, m, rf, rho, (R)sigma, S, P, th, ti, ph, w);        \
+      const int direct = pcg_iters < 0;                                                                       \
+      schur_##SUF(Db, Eb, A0b, Amb, Apb, Gb, T, n, nx, n0, m, rf, rho, (R)sigma, S, P, th, ti, ph, w, direct);\
+      if (direct) chol_##SUF(th, ph, T, n);                                                                   \
       for (int it = 0; it < admm_iters; ++it) {                                                               \
         for (int t = 0; t < T; ++t)                                                                           \
           for (int j = 0; j < n; ++j) {                                                                       \
@@ -198,7 +270,10 @@
             gam[t * n + j] = v;                                                                               \
           }                                                                                                   \
         memcpy(xo, xb, sizeof(R) * k);                                                                        \
-        pcg_##SUF(S, P, gam, xb, T, n, pcg_iters, 0, r, zz, pp, sp);                                          \
+        if (direct)                                                                                           \
+          chol_solve_##SUF(th, ph, gam, xb, r, T, n);                                                         \
+        else                                                                                                  \
+          pcg_##SUF(S, P, gam, xb, T, n, pcg_iters, 0, r, zz, pp, sp);                                        \
         for (int i = 0; i < n0; ++i) cx0[i] = dot_##SUF(A0b + i * n, xb, n);                                  \
         for (int t = 0; t < N; ++t)                                                                           \
           for (int i = 0; i < nx; ++i)                                                                        \

@@ -27,7 +27,9 @@ def max_threads() -> int:
 
 def admm_fixed(qp, rho, admm_iters, pcg_iters, sigma=1e-6, rho_f_factor=1000.0, alpha=1.6, threads=0, x0=None):
     """Fixed-count ADMM from the initial state of admm.py:1051-1088.  qp is an
-    oracle.admm_ref.QP (float32 or float64).  Returns dict of final state arrays."""
+    oracle.admm_ref.QP (float32 or float64).  pcg_iters < 0 solves each ADMM
+    linear system exactly (block Cholesky, the direct backend's semantics).
+    Returns dict of final state arrays."""
     lib = load()
     dt = qp.D.dtype
     suf = "f64" if dt == np.float64 else "f32"

@@ -45,6 +45,14 @@ def test_transfer_poll_limit_hook_round_trips():
     assert lib.tmpc_set_transfer_poll_limit(prev) == 1234
 
 
+def test_iteration_timing_hook_round_trips():
+    lib = _ffi.load()
+    assert lib.tmpc_admm_iteration_timing(1) == 0
+    assert lib.tmpc_admm_iteration_timing(0) == 1
+    buf = (C.c_float * 4)()
+    assert lib.tmpc_admm_iteration_timing_read(buf, 4) == 0  # nothing recorded without a solve
+
+
 def test_interleaved_sizes_without_gpu():
     lib = _ffi.load()
     assert lib.tmpc_interleaved_elems(37, 10) == 64 * 10

@@ -71,18 +71,20 @@ def _oracle_ocp(kind, prog, params, b, use_slack=False):
 
 
 @functools.lru_cache(maxsize=None)
-def _oracle_run(kind, batch, N, sqp, admm, pcg, warm, kw=()):
+def _oracle_run(kind, batch, N, sqp, admm, pcg, warm, kw=(), linsys="pcg"):
     """Oracle solutions of the float64 problem (and, with warm, of a
-    warm-started re-solve from the first solution)."""
+    warm-started re-solve from the first solution).  linsys "dense" solves
+    each ADMM linear system exactly (the direct backend's semantics)."""
     prog, params = _make(kind, batch, N, F64, "cpu", **dict(kw))
     s = TurboMPCSolver(prog, _fixed(sqp, admm, pcg))
     g = s.initial_guess(params)
     cfg = _ocfg(admm, pcg)
-    sols = [sr.solve(_oracle_ocp(kind, prog, params, b), g.states[b], g.controls[b], cfg, sqp) for b in range(batch)]
+    sols = [sr.solve(_oracle_ocp(kind, prog, params, b), g.states[b], g.controls[b], cfg, sqp, linsys=linsys)
+            for b in range(batch)]
     sols2 = None
     if warm:
         sols2 = [sr.solve(_oracle_ocp(kind, prog, params, b), sols[b].states, sols[b].controls, cfg, sqp,
-                          admm_state0=sols[b].state) for b in range(batch)]
+                          admm_state0=sols[b].state, linsys=linsys) for b in range(batch)]
     return prog, params, sols, sols2
 
 
@@ -107,6 +109,40 @@ def test_config3_quadrotor_whole_solve_matches_oracle(dtype):
     sol = s.solve(s.initial_guess(params), params)
     assert (sol.admm_iters[:, :sqp] == admm).all()
     _check_solution(sol, osols, dtype, "config 3")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_config3_quadrotor_direct_backend_matches_oracle(dtype):
+    """The direct backend ("b200_direct", the drop-in for the reference's
+    default admm_fused_cudss): each ADMM linear system solved exactly, here by
+    the batch-interleaved block-Cholesky kernels (n = 16 fp32; fp64 runs the
+    warp-per-problem kernel, n > 12), against the oracle with dense solves."""
+    B, N, sqp, admm = 4, 50, 5, 30
+    _, _, osols, _ = _oracle_run("quadrotor", B, N, sqp, admm, 1, False, linsys="dense")
+    prog, params = _make("quadrotor", B, N, dtype, "cuda")
+    s = TurboMPCSolver(prog, _fixed(sqp, admm, 1), forward_backend="b200_direct")
+    sol = s.solve(s.initial_guess(params), params)
+    assert (sol.admm_iters[:, :sqp] == admm).all()
+    _check_solution(sol, osols, dtype, "config 3 direct")
+
+
+def test_config4_and_5_direct_backend_match_oracle_fp32():
+    """Obstacle rows (m = 12, warm-started re-solve) and the CW + MLP problem
+    (n = 9: the interleaved kernels with padded stage blocks) on the direct
+    backend against the oracle with dense solves."""
+    B, N, sqp, admm = 2, 40, 10, 50
+    _, _, osols, osols2 = _oracle_run("obstacles", B, N, sqp, admm, 1, True, linsys="dense")
+    prog, params = _make("obstacles", B, N, torch.float32, "cuda")
+    s = TurboMPCSolver(prog, _fixed(sqp, admm, 1), forward_backend="b200_direct")
+    sol = s.solve(s.initial_guess(params), params)
+    _check_solution(sol, osols, torch.float32, "config 4 direct")
+    sol2 = s.solve(sol._replace(states=sol.states.detach(), controls=sol.controls.detach()), params)
+    _check_solution(sol2, osols2, torch.float32, "config 4 direct warm start")
+    B, N, sqp, admm = 3, 60, 3, 50
+    _, _, osols, _ = _oracle_run("cw_mlp", B, N, sqp, admm, 1, False, CW_KW, linsys="dense")
+    prog, params = _make("cw_mlp", B, N, torch.float32, "cuda", **dict(CW_KW))
+    s = TurboMPCSolver(prog, _fixed(sqp, admm, 1), forward_backend="b200_direct")
+    _check_solution(s.solve(s.initial_guess(params), params), osols, torch.float32, "config 5 direct")
 
 
 def test_config4_obstacles_with_warm_start_matches_oracle_fp32():

@@ -51,6 +51,8 @@ _SIGS = {
     "tmpc_version": (C.c_int32, []),
     "tmpc_error_string": (C.c_char_p, [C.c_int32]),
     "tmpc_set_transfer_poll_limit": (C.c_uint32, [C.c_uint32]),
+    "tmpc_admm_iteration_timing": (C.c_int32, [C.c_int32]),
+    "tmpc_admm_iteration_timing_read": (C.c_int32, [C.c_void_p, C.c_int32]),
     "tmpc_packed_operator_bytes": (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32]),
     "tmpc_admm_workspace_bytes": (C.c_size_t, [C.POINTER(TmpcDims), C.c_int32, C.POINTER(TmpcAdmmConfig)]),
     "tmpc_admm_solve_fixed_scratch_f64": (C.c_int32, [C.POINTER(TmpcDims), C.POINTER(TmpcQP),

@@ -39,6 +39,9 @@
 // that end at the residual checks (one launch when check_every = 0).  A
 // check that changes some problem's rho re-assembles and re-factors (the
 // factor overwrote the operator) and recomputes gamma for those problems.
+#include <mutex>
+#include <vector>
+
 #include "admm_kernel.cuh"
 #include "riccati_il.cuh"
 
@@ -700,6 +703,34 @@ int il_dispatch(int n, F&& f) {
 
 }  // namespace il
 
+// Diagnostics: CUDA events around the ADMM iteration launches of each call
+// (tmpc_admm_iteration_timing).
+namespace {
+std::mutex g_tm_mu;
+bool g_tm_on = false;
+std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_tm;
+constexpr size_t kTmMax = 1024;
+cudaEvent_t tm_begin(cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  if (!g_tm_on || g_tm.size() >= kTmMax) return nullptr;
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  cudaEventRecord(e, st);
+  return e;
+}
+void tm_end(cudaEvent_t e0, cudaStream_t st) {
+  if (!e0) return;
+  cudaEvent_t e1 = nullptr;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return;
+  }
+  cudaEventRecord(e1, st);
+  std::lock_guard<std::mutex> lk(g_tm_mu);
+  g_tm.emplace_back(e0, e1);
+}
+}  // namespace
+
 // Workspace of the interleaved direct path, 0 when it does not apply.
 template <typename R>
 size_t admm_il_ws_bytes(const TmpcDims& d) {
@@ -781,6 +812,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
       chk((int)cudaPeekAtLastError());
     };
     build(nullptr);
+    cudaEvent_t tm0 = tm_begin(st);
     const int ce = P.check_every;
     if (ce <= 0) {
       iterate(0, P.max_iter);
@@ -800,6 +832,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
         it = c + 1;
       }
     }
+    tm_end(tm0, st);
     // ---- outputs
     chk(deinterleave<R>(Nb, z.x, A.x, static_cast<R*>(P.out.x), st));
     if (P.x_out) chk(deinterleave<R>(Nb, z.x, A.x, P.x_out, st));
@@ -824,3 +857,32 @@ template int launch_admm_direct_il<float>(const AdmmParams<float>&, size_t, cuda
 template int launch_admm_direct_il<double>(const AdmmParams<double>&, size_t, cudaStream_t);
 
 }  // namespace tmpc
+
+extern "C" {
+
+int32_t tmpc_admm_iteration_timing(int32_t enable) {
+  std::lock_guard<std::mutex> lk(tmpc::g_tm_mu);
+  const int32_t prev = tmpc::g_tm_on ? 1 : 0;
+  tmpc::g_tm_on = enable != 0;
+  return prev;
+}
+
+int32_t tmpc_admm_iteration_timing_read(float* ms_out, int32_t max_out) {
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+  {
+    std::lock_guard<std::mutex> lk(tmpc::g_tm_mu);
+    ev.swap(tmpc::g_tm);
+  }
+  int32_t k = 0;
+  for (auto& p : ev) {
+    float ms = -1.f;
+    if (cudaEventSynchronize(p.second) == cudaSuccess && cudaEventElapsedTime(&ms, p.first, p.second) == cudaSuccess &&
+        ms_out && k < max_out)
+      ms_out[k++] = ms;
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  return k;
+}
+
+}  // extern "C"
