@@ -2,8 +2,13 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-A step is one full SQP solve (5 SQP x 30 ADMM x 30 PCG, fixed counts) of the
-whole batch.  For N > 1 (one process per GPU under torchrun) the 65536
+A step is one full SQP solve (5 SQP x 30 ADMM, fixed counts) of the whole
+batch.  Each ADMM iteration's linear system is solved exactly by the block
+Cholesky factor (``--backend direct``, the default: forward backend
+"b200_direct", the drop-in for the reference's default admm_fused_cudss,
+turbompc/solvers/turbompc_solver.py:309) or by 30 PCG iterations
+(``--backend pcg``: "b200", the drop-in for admm_fused_pcg); the default run
+also reports the PCG variant of the same workload inside its line.  For N > 1 (one process per GPU under torchrun) the 65536
 problems are split into contiguous shards (strong scaling, no collective on
 the data path); the step time is the max over ranks.  Rank 0 prints one JSON
 line.  ``--impl reference`` times the CPU restatement of the reference's
@@ -33,6 +38,34 @@ METRIC = "MPC solves/sec (quadrotor N=50, batch 65536)"
 # the kernel reads each problem's QP once and writes its state once, so the
 # traffic grows in proportion to the problems processed).
 NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
+# DRAM bytes (read + write) per problem of one launch of il_admm_kernel (the
+# 30 ADMM iterations of the direct path), from the ncu capture summarised in
+# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 66.55 GB).
+NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 8.124e6
+
+
+def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w):
+    """Bytes one problem must move in one ADMM iteration of the interleaved
+    direct path (il_admm_kernel): the factor read in both sweeps (L_t^-1
+    packed and W_t: E_f = T n(n+1)/2 + N n^2 values, twice), the QP rows of
+    the iteration (A-, A+, G, q, c, l, u) once, and the state it updates
+    (x, y_fdyn, z_g, y_g read and written; gamma and the forward-sweep vector
+    y written once and read once)."""
+    N = T - 1
+    ef = T * n * (n + 1) // 2 + N * n * n
+    rows = 2 * N * nx * n + T * m * n
+    vecs = T * n + N * nx + 2 * T * m
+    state = 2 * (T * n + N * nx + 2 * T * m) + 2 * T * n + 2 * T * n
+    return w * (2 * ef + rows + vecs + state)
+
+
+def direct_launches_per_solve(n0, m, check_every=0):
+    """Kernel launches of one direct-path ADMM call (fixed counts): scalars in,
+    the interleaving of each non-empty QP / state array, assembly, factor,
+    first gamma, the iteration kernel, the conversions back, scalars out."""
+    conv_in = 5 + (2 if n0 else 0) + (3 if m else 0) + 2 + (1 if n0 else 0) + (3 if m else 0)
+    conv_out = 2 + (1 if n0 else 0) + (3 if m else 0)
+    return 1 + conv_in + 3 + 1 + conv_out + 1
 
 
 def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG):
@@ -149,11 +182,101 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def cpu_baseline(target_s=8.0, seed=0, runs=3):
-    """CPU baseline: the C restatement of the reference's ADMM/PCG (oracle/c,
-    the reference's own JAX CPU install is unavailable) on all host cores, on
-    the QPs of the first SQP iteration of this workload (fp32, 30 ADMM x 30
-    PCG), scaled by the 5 SQP iterations of a solve.  Linearisation is not
+def pcg_roofline(T, n, nx, m, n0, shard, kms, hbm):
+    """Roofline object of the register-resident PCG kernel (on-chip bound)."""
+    flops = rows_kernel_flops_per_problem(T, n, nx, m, n0) * shard
+    achieved = flops / (kms / 1e3) / 1e12
+    fpk = fp32_peak_tflops()
+    model_gbs = algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, 4) * shard / (kms / 1e3) / 1e9
+    dram = NCU_DRAM_BYTES_PER_PROBLEM * shard
+    kernel = "admm_rows_kernel" if (T <= 64 and 8 < n <= 16) else "admm_fused_kernel"
+    return {
+        "bound": "fp32", "achieved": achieved, "peak": fpk, "unit": "TFLOP/s", "frac": achieved / fpk,
+        "peak_source": "nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2 x max SM clock); "
+                       "MEASURED_PEAKS.json has no FP32 figure",
+        "traffic": dram, "kernel": kernel, "kernel_ms_per_launch": kms,
+        "flops_per_problem_launch": flops / shard, "smem_pipe_share": NCU_SMEM_PIPE_SHARE,
+        "dram_frac": dram / (kms / 1e3) / 1e9 / hbm, "model_frac": model_gbs / hbm,
+        "note": "the operators stay on chip (registers and shared memory), so the kernel is bound on chip, not by "
+                "HBM: frac = its own FP32 flops (counted from the code at the true block size) per launch time over "
+                "the FP32 peak; smem_pipe_share = shared-memory pipe share from ncu; traffic = measured DRAM bytes "
+                "per launch (ncu, scaled per problem); dram_frac = that traffic over the launch time as a share of "
+                "the measured HBM copy peak; model_frac = the streaming model's bytes (S and Phiinv re-read every "
+                "PCG iteration) per launch time over that peak, > 1 because those bytes are never moved"}
+
+
+def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind):
+    """Roofline object of the interleaved direct path's iteration kernel
+    (il_admm_kernel, HBM bound): algorithmic bytes of its ADMM iterations
+    over its launch time (CUDA events recorded by the library on the launch
+    stream, tmpc_admm_iteration_timing)."""
+    bytes_launch = ADMM * direct_bytes_per_problem_iteration(T, n, nx, m, n0, 4) * shard
+    achieved = bytes_launch / (ims / 1e3) / 1e9
+    return {
+        "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+        "peak_source": f"{pk_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
+        "traffic": NCU_DIRECT_DRAM_BYTES_PER_PROBLEM * shard, "kernel": "il_admm_kernel",
+        "kernel_ms_per_launch": ims, "algorithmic_bytes_per_launch": bytes_launch,
+        "call_ms": kms, "call_frac_of_kernel": ims / kms,
+        "note": "one launch = the 30 ADMM iterations of one SQP iteration for the whole shard; algorithmic bytes = "
+                "per ADMM iteration the block-Cholesky factor read in both sweeps, the QP rows (A-, A+, G, q, c, "
+                "l, u) once and the updated state; traffic = measured DRAM bytes of that kernel (ncu, 8192 "
+                "problems, scaled per problem); call_ms = the whole ADMM call including the layout conversion, "
+                "assembly and factor"}
+
+
+def pcg_variant(ocp, params, sp, batch, steps=2, warmup=1):
+    """The headline workload with 30 PCG iterations per ADMM iteration
+    (forward backend "b200"), device-timed, with the PCG kernel's roofline."""
+    import torch
+
+    from turbompc_b200 import ops
+    from turbompc_b200.solver import TurboMPCSolver
+
+    solver = TurboMPCSolver(ocp, sp, forward_backend="b200")
+    guess = solver.initial_guess(params)
+    for _ in range(warmup):
+        solver.solve(guess, params)
+    orig = ops.admm_solve
+    launch = []
+
+    def timed(*a, **k):
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        out = orig(*a, **k)
+        e1.record()
+        launch.append((e0, e1))
+        return out
+
+    import turbompc_b200.solver as solver_mod
+
+    solver_mod.ops.admm_solve = timed
+    try:
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        s0.record()
+        for _ in range(steps):
+            solver.solve(guess, params)
+        s1.record()
+        torch.cuda.synchronize()
+    finally:
+        solver_mod.ops.admm_solve = orig
+    ms = s0.elapsed_time(s1) / steps
+    kms = sum(a.elapsed_time(b) for a, b in launch) / len(launch)
+    qp = solver._build_qp_data(guess.states, guess.controls, params)
+    hbm, _ = peaks()
+    return {"config": f"quadrotor N={N_HORIZON} batch {batch}, {SQP} SQP x {ADMM} ADMM x {PCG} PCG (forward "
+                      "backend b200, drop-in for admm_fused_pcg)", "metric": "MPC solves/sec",
+            "value": batch / (ms / 1e3), "unit": "solves/s", "ms_per_step": ms, "dtype": "f32", "n_gpus": 1,
+            "roofline": pcg_roofline(qp.T, qp.n, qp.nx, qp.m, qp.n0, batch, kms, hbm)}
+
+
+def cpu_baseline(target_s=8.0, seed=0, runs=3, backend="direct"):
+    """CPU baseline: the C restatement of the reference's ADMM (oracle/c, the
+    reference's own JAX CPU install is unavailable) on all host cores, on the
+    QPs of the first SQP iteration of this workload (fp32, 30 ADMM iterations,
+    each with the direct block-Cholesky solve or with 30 PCG iterations as the
+    GPU arm), scaled by the 5 SQP iterations of a solve.  Linearisation is not
     timed on the CPU side, which flatters the CPU.  The sample is sized so one
     timed run takes about ``target_s`` seconds; the value is the median of
     ``runs`` timed runs on the same sample."""
@@ -176,33 +299,41 @@ def cpu_baseline(target_s=8.0, seed=0, runs=3):
 
     def timed(q):
         t0 = time.perf_counter()
-        c_oracle.admm_fixed(q, 0.1, ADMM, PCG, threads=threads)
+        c_oracle.admm_fixed(q, 0.1, ADMM, -1 if backend == "direct" else PCG, threads=threads)
         return time.perf_counter() - t0
 
     k = threads
     dt = timed(qp_sample(k))
-    k = int(min(8192, max(k, k * target_s / max(dt, 1e-3))))
+    k = int(min(65536, max(k, k * target_s / max(dt, 1e-3))))
     q = qp_sample(k)
     times = [timed(q) for _ in range(runs)]
     dt = statistics.median(times)
     return {"value": k / (dt * SQP), "unit": "solves/s", "cores": threads, "kind": "port",
-            "sample": f"{k} quadrotor QPs x 1 SQP iteration (30 ADMM x 30 PCG, fp32, C restatement in oracle/c, "
+            "sample": f"{k} quadrotor QPs x 1 SQP iteration (30 ADMM, {linsys_label(backend)}, fp32, C restatement "
+                      "in oracle/c, "
                       f"{threads} host threads), scaled x{SQP} SQP iterations; median of {runs} runs "
                       f"({', '.join(f'{t:.1f}' for t in times)} s)"}
 
 
-def workload_config(batch, world, shard):
+def linsys_label(backend):
+    return ("direct block-Cholesky solve per ADMM iteration" if backend == "direct"
+            else f"{PCG} PCG iterations per ADMM iteration")
+
+
+def workload_config(batch, world, shard, backend="direct"):
     """The `config` object of both arms' JSON lines."""
-    return {"workload": f"quadrotor-12 N={N_HORIZON} batch {batch}, {SQP} SQP x {ADMM} ADMM x {PCG} PCG "
-                        "(fixed counts)",
+    return {"workload": f"quadrotor-12 N={N_HORIZON} batch {batch}, {SQP} SQP x {ADMM} ADMM, "
+                        f"{linsys_label(backend)} (fixed counts)",
+            "backend": ("b200_direct (drop-in for admm_fused_cudss, the reference's default)" if backend == "direct"
+                        else "b200 (drop-in for admm_fused_pcg)"),
             "global_batch": batch, "per_gpu_batch": shard, "horizon": N_HORIZON, "parallelism": f"batch-shard x{world}"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_baseline(runs=max(3, args.steps))
-    cfg = workload_config(args.batch, 1, args.batch)
+    cb = cpu_baseline(runs=max(3, args.steps), backend=args.backend)
+    cfg = workload_config(args.batch, 1, args.batch, args.backend)
     cfg["l2"] = "CPU run (no GPU); sample in cpu_baseline.sample"
     line = {"metric": METRIC, "value": cb["value"], "unit": "solves/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": args.batch / cb["value"] * 1e3, "higher_is_better": True,
@@ -504,6 +635,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--backend", default="direct", choices=["direct", "pcg"],
+                    help="linear solve of each ADMM iteration: direct (block Cholesky) or 30 PCG iterations")
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--headline-only", action="store_true",
@@ -572,8 +705,10 @@ def main():
     sp = {"num_sqp_iteration_max": SQP, "tol_convergence": 0.0,
           "admm": {"max_iter": ADMM, "check_termination_every": 0, "adapt_rho_every": 0, "eps_abs": 0.0,
                    "eps_rel": 0.0, "pcg": {"max_iter": PCG, "tol_epsilon": 0.0}}}
-    solver = TurboMPCSolver(ocp, sp, forward_backend="b200")
+    direct = args.backend == "direct"
+    solver = TurboMPCSolver(ocp, sp, forward_backend="b200_direct" if direct else "b200")
     guess = solver.initial_guess(params)
+    lib = _ffi.load(build_if_missing=False)
 
     # ---- device-resident timing (value) with per-launch events for the ADMM kernel
     launch_ms = []
@@ -613,6 +748,8 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    if direct:
+        lib.tmpc_admm_iteration_timing(1)  # events around the iteration kernel of each ADMM call
     with ClockSampler(local) as clk:
         s0, s1 = torch.cuda.Event(True), torch.cuda.Event(True)
         s0.record()
@@ -628,11 +765,19 @@ def main():
     solver_mod.ops.admm_solve = orig
     ms = s0.elapsed_time(s1) / args.steps
     kern_ms = [a.elapsed_time(b) for a, b in launch_ms]
-    kms = sum(kern_ms) / len(kern_ms)
+    kms = sum(kern_ms) / len(kern_ms)  # one whole ADMM call (all its kernels)
+    ims = kms
+    if direct:
+        import ctypes
+
+        lib.tmpc_admm_iteration_timing(0)
+        buf = (ctypes.c_float * 1024)()
+        cnt = lib.tmpc_admm_iteration_timing_read(buf, 1024)
+        ims = sum(buf[:cnt]) / max(cnt, 1)  # the iteration kernel alone
     if dist:
-        t = torch.tensor([ms, kms], device=dev)
+        t = torch.tensor([ms, kms, ims], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, kms = t.tolist()
+        ms, kms, ims = t.tolist()
     value = args.batch / (ms / 1e3)
 
     # ---- end-to-end through the public API with host buffers
@@ -669,13 +814,13 @@ def main():
     if rank == 0:
         qp = solver._build_qp_data(guess.states, guess.controls, params)
         T, n, nx, m, n0 = qp.T, qp.n, qp.nx, qp.m, qp.n0
-        kernel = "admm_rows_kernel" if (T <= 64 and 8 < n <= 16) else "admm_fused_kernel"
-        flops = rows_kernel_flops_per_problem(T, n, nx, m, n0) * shard
-        achieved = flops / (kms / 1e3) / 1e12
-        fpk = fp32_peak_tflops()
         hbm, pk_kind = peaks()
-        model_gbs = algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, 4) * shard / (kms / 1e3) / 1e9
-        dram = NCU_DRAM_BYTES_PER_PROBLEM * shard
+        if direct:
+            roof = direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind)
+            per_call = direct_launches_per_solve(n0, m)
+        else:
+            roof = pcg_roofline(T, n, nx, m, n0, shard, kms, hbm)
+            per_call = 1
         # QP data one fused ADMM launch reads (one SQP iteration's D, E, q,
         # A_minus, A_plus, c, G, l, u for this GPU's shard, fp32).
         qp_gb = shard * 4 * (T * n * n * 2 + T * n + 2 * (T - 1) * nx * n + (T - 1) * nx
@@ -683,10 +828,10 @@ def main():
         cb = None
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cb = cpu_baseline()
+                cb = cpu_baseline(backend=args.backend)
             except Exception as exc:  # reported, not fatal
                 cb = {"error": repr(exc)}
-        cfg = workload_config(args.batch, world, shard)
+        cfg = workload_config(args.batch, world, shard, args.backend)
         cfg["l2"] = (f"inputs > L2 (QP data ~{qp_gb:.1f} GB per SQP iteration)" if qp_gb > 0.126
                      else f"QP data {qp_gb:.3f} GB per SQP iteration (fits L2)")
         line = {
@@ -695,28 +840,18 @@ def main():
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
             "e2e": {"value": args.batch / (e2e_ms / 1e3), "unit": "solves/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "roofline": {
-                "bound": "fp32", "achieved": achieved, "peak": fpk, "unit": "TFLOP/s", "frac": achieved / fpk,
-                "peak_source": "nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2 x max SM clock); "
-                               "MEASURED_PEAKS.json has no FP32 figure",
-                "traffic": dram, "kernel": kernel, "kernel_ms_per_launch": kms,
-                "flops_per_problem_launch": flops / shard,
-                "smem_pipe_share": NCU_SMEM_PIPE_SHARE,
-                "dram_frac": dram / (kms / 1e3) / 1e9 / hbm,
-                "model_frac": model_gbs / hbm,
-                "note": "the operators stay on chip (registers and shared memory), so the kernel is bound on "
-                        "chip, not by HBM: frac = its own FP32 flops (counted from the code at the true block "
-                        "size) per launch time over the FP32 peak; smem_pipe_share = shared-memory pipe share "
-                        "from ncu; traffic = measured DRAM bytes per launch (ncu, scaled per problem), dram_frac "
-                        "= that traffic over the launch time as a share of the measured HBM copy peak; "
-                        "model_frac = the streaming model's bytes (S and Phiinv re-read every PCG iteration) "
-                        "per launch time over that peak, > 1 because the model's bytes are never moved"},
-            "gpu_launches": len(launch_ms) + n_lin[0],
+            "roofline": roof,
+            "gpu_launches": len(launch_ms) * per_call + n_lin[0],
             "clocks": clk.summary(),
             "cpu_baseline": cb,
         }
         if world == 1 and not args.headline_only:
             line["configs"] = other_configs()
+            if direct:  # the same workload with 30 PCG iterations per ADMM iteration
+                try:
+                    line["configs"]["pcg_variant"] = pcg_variant(ocp, params, sp, args.batch)
+                except Exception as exc:  # reported, not fatal
+                    line["configs"]["pcg_variant"] = {"error": repr(exc)}
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
