@@ -40,8 +40,8 @@ METRIC = "MPC solves/sec (quadrotor N=50, batch 65536)"
 NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
 # DRAM bytes (read + write) per problem of one launch of il_admm_kernel (the
 # 30 ADMM iterations of the direct path), from the ncu capture summarised in
-# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 66.55 GB).
-NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 8.124e6
+# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 65.88 GB).
+NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 8.042e6
 
 
 def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w):
