@@ -528,14 +528,16 @@ def pcg_sweep(points, reps=5, pcg_iters=PCG, emit=None):
         del Sb, fac
 
 
-def run_config(name, steps=3, warmup=2, emit=True):
+def run_config(name, steps=3, warmup=2, emit=True, backend="direct"):
     """Configs 4 and 5 on one GPU (one JSON line each; the default run above is
     config 3).  obstacles: quadrotor N=40 with 8 spheres per problem, batch
     8192, 10 SQP x 50 ADMM x 30 PCG, each step warm-started from the previous
     solution (states, controls and ADMM state).  cw_mlp: Clohessy-Wiltshire
     with the learned MLP stage cost, N=60, batch 16384, 3 SQP x 50 ADMM x 30
     PCG forward plus the VJP w.r.t. x0, the MLP parameters and A, B (adjoint
-    KKT on the GPU).  Device time with CUDA events."""
+    KKT on the GPU).  backend "direct" (the default, as the headline) replaces
+    the PCG iterations by the exact block-Cholesky solve of every ADMM linear
+    system.  Device time with CUDA events."""
     import torch
 
     from turbompc_b200.problems.learned_cost import make_learned_cost_problem
@@ -547,11 +549,13 @@ def run_config(name, steps=3, warmup=2, emit=True):
                 "admm": {"max_iter": admm, "check_termination_every": 0, "adapt_rho_every": 0, "eps_abs": 0.0,
                          "eps_rel": 0.0, "pcg": {"max_iter": pcg, "tol_epsilon": 0.0}}}
 
+    fb = "b200_direct" if backend == "direct" else "b200"
+    lin = "direct solve" if backend == "direct" else "30 PCG"
     e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
     if name == "obstacles":
         batch = 8192
         prog, params = make_obstacle_problem(batch, N=40, seed=4, dtype=torch.float32, device="cuda")
-        solver = TurboMPCSolver(prog, fixed(10, 50, 30))
+        solver = TurboMPCSolver(prog, fixed(10, 50, 30), forward_backend=fb)
         guess = solver.initial_guess(params)
         for _ in range(warmup):
             guess = solver.solve(guess, params)
@@ -564,11 +568,11 @@ def run_config(name, steps=3, warmup=2, emit=True):
         ms = e0.elapsed_time(e1) / steps
         line = {"config": "obstacles (config 4)", "metric": "MPC solves/sec", "value": batch / (ms / 1e3),
                 "unit": "solves/s", "ms_per_step": ms, "batch": batch, "horizon": 40, "m": 12,
-                "iterations": "10 SQP x 50 ADMM x 30 PCG, warm-started", "dtype": "f32", "n_gpus": 1}
+                "iterations": f"10 SQP x 50 ADMM x {lin}, warm-started", "backend": fb, "dtype": "f32", "n_gpus": 1}
     else:
         batch = 16384
         prog, params = make_learned_cost_problem(batch, N=60, seed=0, dtype=torch.float32, device="cuda")
-        solver = TurboMPCSolver(prog, fixed(3, 50, 30), use_full_hessian=True)
+        solver = TurboMPCSolver(prog, fixed(3, 50, 30), use_full_hessian=True, forward_backend=fb)
         guess = solver.initial_guess(params)
         leaves = {"mlp_W1": params["mlp_W1"], "mlp_b1": params["mlp_b1"], "mlp_w2": params["mlp_w2"],
                   "dynamics_state_dot_params": dict(params["dynamics_state_dot_params"]),
@@ -603,7 +607,7 @@ def run_config(name, steps=3, warmup=2, emit=True):
         line = {"config": "cw_mlp (config 5)", "metric": "MPC solves/sec", "value": batch / (ms_f / 1e3),
                 "unit": "solves/s", "forward_ms": ms_f, "forward_plus_vjp_ms": ms_fb,
                 "forward_plus_vjp_solves_per_s": batch / (ms_fb / 1e3), "batch": batch, "horizon": 60,
-                "iterations": "3 SQP x 50 ADMM x 30 PCG; VJP w.r.t. x0, MLP W1 b1 w2, A, B", "dtype": "f32",
+                "iterations": f"3 SQP x 50 ADMM x {lin}; VJP w.r.t. x0, MLP W1 b1 w2, A, B", "backend": fb, "dtype": "f32",
                 "n_gpus": 1}
     if emit:
         print(json.dumps(line), flush=True)
@@ -657,7 +661,7 @@ def main():
                          "(e.g. '24,8,128,4096,f32'); 'default' runs a representative set")
     args = ap.parse_args()
     if args.config:
-        return run_config(args.config)
+        return run_config(args.config, backend=args.backend)
     if args.pcg_sweep:
         spec = args.pcg_sweep
         if spec == "default":

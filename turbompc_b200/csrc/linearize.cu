@@ -40,10 +40,16 @@ template <typename R>
 __device__ __forceinline__ Dual<R> operator+(Dual<R> a, R s) { return {a.v + s, a.d}; }
 template <typename R>
 __device__ __forceinline__ Dual<R> operator-(Dual<R> a, R s) { return {a.v - s, a.d}; }
+// sin and cos of a dual number from one sincos of its value.
+__device__ __forceinline__ void sc(float v, float* s, float* c) { sincosf(v, s, c); }
+__device__ __forceinline__ void sc(double v, double* s, double* c) { sincos(v, s, c); }
 template <typename R>
-__device__ __forceinline__ Dual<R> dsin(Dual<R> a) { return {sin(a.v), cos(a.v) * a.d}; }
-template <typename R>
-__device__ __forceinline__ Dual<R> dcos(Dual<R> a) { return {cos(a.v), -sin(a.v) * a.d}; }
+__device__ __forceinline__ void dsincos(Dual<R> a, Dual<R>& s, Dual<R>& c) {
+  R sv, cv;
+  sc(a.v, &sv, &cv);
+  s = {sv, cv * a.d};
+  c = {cv, -sv * a.d};
+}
 
 // Quadrotor12Dynamics.state_dot (turbompc_b200/dynamics/quadrotor.py), the
 // same expression order.  p = {mass, Jx, Jy, Jz, arm_length, yaw_coefficient}.
@@ -53,7 +59,10 @@ __device__ __forceinline__ void quad_xdot(Dual<R>* out, const Dual<R>* x, const 
   const Dual<R> phi = x[3], th = x[4], psi = x[5];
   const Dual<R> wx = x[9], wy = x[10], wz = x[11];
   const Dual<R> f1 = u[0], f2 = u[1], f3 = u[2], f4 = u[3];
-  const Dual<R> sph = dsin(phi), cph = dcos(phi), sth = dsin(th), cth = dcos(th), sps = dsin(psi), cps = dcos(psi);
+  Dual<R> sph, cph, sth, cth, sps, cps;
+  dsincos(phi, sph, cph);
+  dsincos(th, sth, cth);
+  dsincos(psi, sps, cps);
   const Dual<R> tth = sth / cth;
   out[0] = x[6];
   out[1] = x[7];
