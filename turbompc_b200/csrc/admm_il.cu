@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
 // thread per (problem, stage).  Also ORs the last factor's status bits into
 // the problem's status.  With chg, only problems whose rho just changed.
 // ---------------------------------------------------------------------------
-template <typename R>
+template <int NB, typename R>
 __global__ void __launch_bounds__(kWarp) il_gamma_kernel(IlArgs<R> A, const int* gate, int use_chg) {
   if (gate && *gate == 0) return;
   const int lane = threadIdx.x, t = blockIdx.y;
@@ -281,30 +281,40 @@ __global__ void __launch_bounds__(kWarp) il_gamma_kernel(IlArgs<R> A, const int*
   const int T = A.T, N = T - 1, n = A.n, nx = A.nx, n0 = A.n0, m = A.m;
   const IlSizes z(T, n, nx, n0, m);
   const R rho = A.rho[b], rf = rho * A.rff;
-  auto ctd = [&](int k) {  // rho_f c - y_f, dynamics row k = t nx + i
-    return rf * A.c[ix(b, z.c, k)] - A.yfd[ix(b, z.yfd, k)];
+  // Row by row: each constraint row's values are read once and its target
+  // (rho_f c - y_f, or rho z - y_g) multiplies the whole row into the NB
+  // per-column sums, which see their terms in compute_gamma's order.
+  R eq[NB], iq[NB];
+#pragma unroll
+  for (int j = 0; j < NB; ++j) eq[j] = iq[j] = R(0);
+  auto add_row = [&](R (&s)[NB], const R* row, size_t E, R tgt) {  // row: element offset of the row's first value
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+      if (j < n) s[j] += row[ix(b, E, j)] * tgt;
   };
-  for (int j = 0; j < n; ++j) {
-    R val = A.sigma * A.x[ix(b, z.x, (size_t)t * n + j)] - A.q[ix(b, z.q, (size_t)t * n + j)];
-    R eq = R(0);
-    if (t == 0) {
-      for (int k = 0; k < n0; ++k)
-        eq += A.a0[ix(b, z.a0, (size_t)k * n + j)] * (rf * A.c0[ix(b, z.c0, k)] - A.yf0[ix(b, z.yf0, k)]);
-      if (N > 0)
-        for (int k = 0; k < nx; ++k) eq += A.am[ix(b, z.am, (size_t)k * n + j)] * ctd(k);
-    } else {
-      for (int k = 0; k < nx; ++k)
-        eq += A.ap[ix(b, z.am, ((size_t)(t - 1) * nx + k) * n + j)] * ctd((t - 1) * nx + k);
-      if (t < N)
-        for (int k = 0; k < nx; ++k) eq += A.am[ix(b, z.am, ((size_t)t * nx + k) * n + j)] * ctd(t * nx + k);
+  auto ctd = [&](int k) { return rf * A.c[ix(b, z.c, k)] - A.yfd[ix(b, z.yfd, k)]; };
+  if (t == 0) {
+    for (int k = 0; k < n0; ++k)
+      add_row(eq, A.a0 + (size_t)k * n * kWarp, z.a0, rf * A.c0[ix(b, z.c0, k)] - A.yf0[ix(b, z.yf0, k)]);
+    if (N > 0)
+      for (int k = 0; k < nx; ++k) add_row(eq, A.am + (size_t)k * n * kWarp, z.am, ctd(k));
+  } else {
+    for (int k = 0; k < nx; ++k)
+      add_row(eq, A.ap + (size_t)((t - 1) * nx + k) * n * kWarp, z.am, ctd((t - 1) * nx + k));
+    if (t < N)
+      for (int k = 0; k < nx; ++k) add_row(eq, A.am + (size_t)(t * nx + k) * n * kWarp, z.am, ctd(t * nx + k));
+  }
+  for (int k = 0; k < m; ++k)
+    add_row(iq, A.g + (size_t)(t * m + k) * n * kWarp, z.g,
+            rho * A.zg[ix(b, z.zm, (size_t)t * m + k)] - A.yg[ix(b, z.zm, (size_t)t * m + k)]);
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    if (j < n) {
+      R val = A.sigma * A.x[ix(b, z.x, (size_t)t * n + j)] - A.q[ix(b, z.q, (size_t)t * n + j)];
+      val += eq[j];
+      val += iq[j];
+      A.gam[ix(b, z.x, (size_t)t * n + j)] = val;
     }
-    val += eq;
-    R iq = R(0);
-    for (int k = 0; k < m; ++k)
-      iq += A.g[ix(b, z.g, ((size_t)t * m + k) * n + j)] *
-            (rho * A.zg[ix(b, z.zm, (size_t)t * m + k)] - A.yg[ix(b, z.zm, (size_t)t * m + k)]);
-    val += iq;
-    A.gam[ix(b, z.x, (size_t)t * n + j)] = val;
   }
 }
 
@@ -799,7 +809,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
       il_assemble_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, P.qp, gate);
       chk((int)cudaPeekAtLastError());
       chk(launch_factor<NB, R>(Nb, T, n, A.ops, A.ops, A.fstat, gate, st));
-      il_gamma_kernel<R><<<ggrid, kWarp, 0, st>>>(A, gate, gate ? 1 : 0);
+      il_gamma_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, gate, gate ? 1 : 0);
       chk((int)cudaPeekAtLastError());
       if (gate) {
         il_clear_chg_kernel<<<(G32 + 255) / 256, 256, 0, st>>>(A.chg, G32, A.gate);
