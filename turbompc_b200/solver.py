@@ -413,7 +413,6 @@ class TurboMPCSolver:
                     "btki,bti->btk", qp_next.ineq.G, xb)
             kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
             # Masked update (problems already converged keep their iterate).
-            a3 = active[:, None, None]
             sel = lambda new, old: torch.where(active.view(-1, *([1] * (new.dim() - 1))), new, old)
             states, controls, slacks = sel(s_new, states), sel(c_new, controls), sel(sl_new, slacks)
             st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
@@ -424,13 +423,12 @@ class TurboMPCSolver:
             conv = sel(cv, conv)
             it_count = it_count + active.to(torch.int64)
             if k + 1 < max_iter:
-                # Fields shared with the previous QP (reused blocks) need no select.
-                qp = qp_next if bool(active.all()) else QPData(*[type(f)(*[
-                    sel(a_, b_) if isinstance(a_, torch.Tensor) and a_.dim() > 0 and a_ is not b_ else a_
-                    for a_, b_ in zip(vars(f).values(), vars(g_).values())]) for f, g_ in zip(
-                        (qp_next.cost, qp_next.eq, qp_next.ineq), (qp.cost, qp.eq, qp.ineq))])
+                # Every problem moves on to the QP at its new iterate: a problem
+                # that has converged still runs (its results are discarded by
+                # the selects above), so its QP needs no select and the loop
+                # never waits on the device to decide.
+                qp = qp_next
             active = active & (conv > tol)
-            del a3
         return TurboMPCSolution(states=states, controls=controls, slack=st.xi_g, status=self.STATUS_SUCCESS,
                                 num_iter=it_count, convergence_error=conv, admm_iters=admm_iters, admm_state=st,
                                 solver_stats=SolverStats(admm_iters, eqv, inv, cerr, kstatus), kkt_state=kkt)
