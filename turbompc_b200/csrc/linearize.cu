@@ -54,8 +54,21 @@ __device__ __forceinline__ void dsincos(Dual<R> a, Dual<R>& s, Dual<R>& c) {
 // Quadrotor12Dynamics.state_dot (turbompc_b200/dynamics/quadrotor.py), the
 // same expression order.  p = {mass, Jx, Jy, Jz, arm_length, yaw_coefficient}.
 template <typename R>
-__device__ __forceinline__ void quad_xdot(Dual<R>* out, const Dual<R>* x, const Dual<R>* u, const R* p) {
-  const R m = p[0], Jx = p[1], Jy = p[2], Jz = p[3], L = p[4], k = p[5];
+__device__ __forceinline__ Dual<R> dscale(Dual<R> a, R s) { return {a.v * s, a.d * s}; }
+// a / b with rb = 1 / b.v computed once by the caller.
+template <typename R>
+__device__ __forceinline__ Dual<R> ddiv(Dual<R> a, Dual<R> b, R rb) {
+  const R q = a.v * rb;
+  return {q, (a.d - q * b.d) * rb};
+}
+
+// Quadrotor12Dynamics.state_dot (turbompc_b200/dynamics/quadrotor.py), the
+// same expression order; divisions by cos(theta) and by the constants are
+// multiplications by reciprocals formed once.  p = {mass, Jx, Jy, Jz,
+// arm_length, yaw_coefficient}; rp = {1/mass, 1/Jx, 1/Jy, 1/Jz}.
+template <typename R>
+__device__ __forceinline__ void quad_xdot(Dual<R>* out, const Dual<R>* x, const Dual<R>* u, const R* p, const R* rp) {
+  const R Jx = p[1], Jy = p[2], Jz = p[3], L = p[4], k = p[5];
   const Dual<R> phi = x[3], th = x[4], psi = x[5];
   const Dual<R> wx = x[9], wy = x[10], wz = x[11];
   const Dual<R> f1 = u[0], f2 = u[1], f3 = u[2], f4 = u[3];
@@ -63,23 +76,24 @@ __device__ __forceinline__ void quad_xdot(Dual<R>* out, const Dual<R>* x, const 
   dsincos(phi, sph, cph);
   dsincos(th, sth, cth);
   dsincos(psi, sps, cps);
-  const Dual<R> tth = sth / cth;
+  const R rc = R(1) / cth.v;
+  const Dual<R> tth = ddiv(sth, cth, rc);
   out[0] = x[6];
   out[1] = x[7];
   out[2] = x[8];
   out[3] = (wx + sph * tth * wy) + cph * tth * wz;
   out[4] = cph * wy - sph * wz;
-  out[5] = (sph * wy + cph * wz) / cth;
-  const Dual<R> F = (((f1 + f2) + f3) + f4) / Dual<R>{m, R(0)};
+  out[5] = ddiv(sph * wy + cph * wz, cth, rc);
+  const Dual<R> F = dscale(((f1 + f2) + f3) + f4, rp[0]);
   out[6] = (cps * sth * cph + sps * sph) * F;
   out[7] = (sps * sth * cph - cps * sph) * F;
   out[8] = cth * cph * F - R(9.81);
   const Dual<R> tx = L * (f2 - f4);
   const Dual<R> ty = L * (f3 - f1);
   const Dual<R> tz = k * (((f1 - f2) + f3) - f4);
-  out[9] = (tx - (Jz - Jy) * wy * wz) / Dual<R>{Jx, R(0)};
-  out[10] = (ty - (Jx - Jz) * wz * wx) / Dual<R>{Jy, R(0)};
-  out[11] = (tz - (Jy - Jx) * wx * wy) / Dual<R>{Jz, R(0)};
+  out[9] = dscale(tx - (Jz - Jy) * wy * wz, rp[1]);
+  out[10] = dscale(ty - (Jx - Jz) * wz * wx, rp[2]);
+  out[11] = dscale(tz - (Jy - Jx) * wx * wy, rp[3]);
 }
 
 // ClohessyWiltshireDynamics.state_dot (turbompc_b200/dynamics/spacecraft.py); p = {mean_motion}.
@@ -95,8 +109,8 @@ __device__ __forceinline__ void cw_xdot(Dual<R>* out, const Dual<R>* x, const Du
 }
 
 template <typename R, int MODEL>
-__device__ __forceinline__ void xdot(Dual<R>* out, const Dual<R>* x, const Dual<R>* u, const R* p) {
-  if constexpr (MODEL == TMPC_MODEL_QUADROTOR12) quad_xdot(out, x, u, p);
+__device__ __forceinline__ void xdot(Dual<R>* out, const Dual<R>* x, const Dual<R>* u, const R* p, const R* rp) {
+  if constexpr (MODEL == TMPC_MODEL_QUADROTOR12) quad_xdot(out, x, u, p, rp);
   else cw_xdot(out, x, u, p);
 }
 
@@ -113,10 +127,11 @@ struct ModelDims<TMPC_MODEL_CLOHESSY_WILTSHIRE> {
 
 // One step of the scheme (turbompc_b200/dynamics/integrators.py order).
 template <typename R, int MODEL>
-__device__ __forceinline__ void step(Dual<R>* xn, const Dual<R>* x, const Dual<R>* u, const R* p, int scheme, R dt) {
+__device__ __forceinline__ void step(Dual<R>* xn, const Dual<R>* x, const Dual<R>* u, const R* p, const R* rp,
+                                     int scheme, R dt) {
   constexpr int NX = ModelDims<MODEL>::nx;
   Dual<R> k1[NX], tmp[NX];
-  xdot<R, MODEL>(k1, x, u, p);
+  xdot<R, MODEL>(k1, x, u, p, rp);
   if (scheme == TMPC_SCHEME_EULER) {
 #pragma unroll
     for (int i = 0; i < NX; ++i) xn[i] = x[i] + dt * k1[i];
@@ -127,25 +142,25 @@ __device__ __forceinline__ void step(Dual<R>* xn, const Dual<R>* x, const Dual<R
   for (int i = 0; i < NX; ++i) tmp[i] = x[i] + h * k1[i];
   if (scheme == TMPC_SCHEME_MIDPOINT) {
     Dual<R> k2[NX];
-    xdot<R, MODEL>(k2, tmp, u, p);
+    xdot<R, MODEL>(k2, tmp, u, p, rp);
 #pragma unroll
     for (int i = 0; i < NX; ++i) xn[i] = x[i] + dt * k2[i];
     return;
   }
   Dual<R> acc[NX], k[NX];
-  xdot<R, MODEL>(k, tmp, u, p);  // k2
+  xdot<R, MODEL>(k, tmp, u, p, rp);  // k2
 #pragma unroll
   for (int i = 0; i < NX; ++i) {
     acc[i] = k1[i] + R(2) * k[i];
     tmp[i] = x[i] + h * k[i];
   }
-  xdot<R, MODEL>(k, tmp, u, p);  // k3
+  xdot<R, MODEL>(k, tmp, u, p, rp);  // k3
 #pragma unroll
   for (int i = 0; i < NX; ++i) {
     acc[i] = acc[i] + R(2) * k[i];
     tmp[i] = x[i] + dt * k[i];
   }
-  xdot<R, MODEL>(k, tmp, u, p);  // k4
+  xdot<R, MODEL>(k, tmp, u, p, rp);  // k4
   const R sixth = R(1.0 / 6.0);
 #pragma unroll
   for (int i = 0; i < NX; ++i) xn[i] = x[i] + dt * (sixth * (acc[i] + k[i]));
@@ -172,6 +187,9 @@ __global__ void __launch_bounds__(256) linearize_kernel(int Nb, int T, const R* 
   R p[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) p[i] = pp.v[i];
+  R rp[4];  // reciprocals of the quadrotor's mass and inertias (unused by the other models)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) rp[i] = (MODEL == TMPC_MODEL_QUADROTOR12 && i < NP) ? R(1) / p[i] : R(0);
   Dual<R> x[NX], u[NU], xn[NX];
   const R* xs = states + ((size_t)b * T + t) * NX;
   const R* us = controls + ((size_t)b * T + t) * NU;
@@ -179,7 +197,7 @@ __global__ void __launch_bounds__(256) linearize_kernel(int Nb, int T, const R* 
   for (int i = 0; i < NX; ++i) x[i] = {valid ? xs[i] : R(0), (i == j) ? R(1) : R(0)};
 #pragma unroll
   for (int i = 0; i < NU; ++i) u[i] = {valid ? us[i] : R(0), (NX + i == j) ? R(1) : R(0)};
-  step<R, MODEL>(xn, x, u, p, scheme, dt);
+  step<R, MODEL>(xn, x, u, p, rp, scheme, dt);
   // Column j of A_minus_t, and the lane's share of A_minus_t z.
   R zj = R(0);  // z_j by a select chain (no runtime register-array index)
 #pragma unroll
