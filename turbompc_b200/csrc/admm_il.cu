@@ -75,7 +75,7 @@ struct IlSizes {
 template <typename R>
 struct IlWs {
   size_t ops, q, a0, am, ap, g, c0, c, l, u, x, yf0, yfd, zg, yg, xig, gam, ys, rho, sw;  // R offsets
-  size_t act, iters, status, fstat, chg, gate;                                           // int offsets
+  size_t act, iters, status, fstat, chg, apid, gate;                                     // int offsets
   size_t rbytes, bytes;
   IlWs(int Nb, int T, int n, int nx, int n0, int m) {
     const IlSizes z(T, n, nx, n0, m);
@@ -97,6 +97,7 @@ struct IlWs {
     status = io; io += G32;
     fstat = io; io += G32;
     chg = io; io += G32;
+    apid = io; io += groups(Nb);
     gate = io; io += 4;
     bytes = rbytes + io * sizeof(int);
   }
@@ -106,7 +107,7 @@ struct IlWs {
 template <typename R>
 struct IlArgs {
   R *ops, *q, *a0, *am, *ap, *g, *c0, *c, *l, *u, *x, *yf0, *yfd, *zg, *yg, *xig, *gam, *ys, *rho, *sw;
-  int *act, *iters, *status, *fstat, *chg, *gate;
+  int *act, *iters, *status, *fstat, *chg, *apid, *gate;
   int Nb, T, n, nx, n0, m, use_slack;
   R sigma, alpha, rff;
 };
@@ -122,6 +123,7 @@ IlArgs<R> il_args(void* ws, const AdmmParams<R>& P) {
   a.yfd = r + L.yfd; a.zg = r + L.zg; a.yg = r + L.yg; a.xig = r + L.xig; a.gam = r + L.gam; a.ys = r + L.ys;
   a.rho = r + L.rho; a.sw = r + L.sw;
   a.act = i + L.act; a.iters = i + L.iters; a.status = i + L.status; a.fstat = i + L.fstat; a.chg = i + L.chg;
+  a.apid = i + L.apid;
   a.gate = i + L.gate;
   a.Nb = P.Nb; a.T = P.T; a.n = P.n; a.nx = P.nx; a.n0 = P.n0; a.m = P.m; a.use_slack = P.use_slack;
   a.sigma = P.sigma; a.alpha = P.alpha; a.rff = P.rho_f_factor;
@@ -150,6 +152,33 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
   A.fstat[b] = 0;
   A.chg[b] = 0;
   if (b == 0) A.gate[0] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Structure of A+: the explicit integrators give A+_t = [-I 0] for every
+// stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One warp
+// per group checks its 32 problems' interleaved A+ exactly; where every one
+// matches, the iteration kernel forms A+ x and A+^T y from the identity
+// (bit-identical: the products with the exact -1 and 0 entries are exact)
+// and does not stream A+ each iteration.
+// ---------------------------------------------------------------------------
+template <typename R>
+__global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
+  const int lane = threadIdx.x, grp = blockIdx.x;
+  const int b = grp * kWarp + lane;
+  const IlSizes z(A.T, A.n, A.nx, A.n0, A.m);
+  const int n = A.n, nx = A.nx;
+  bool ok = true;
+  if (b < A.Nb) {
+    const R* p = A.ap + (size_t)grp * z.am * kWarp + lane;
+    for (size_t e = 0; e < z.am && ok; ++e) {
+      const int rem = (int)(e % ((size_t)nx * n));
+      const int k = rem / n, j = rem - k * n;
+      ok = p[e * kWarp] == (j == k ? R(-1) : R(0));
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (lane == 0) A.apid[grp] = ok ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -372,6 +401,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   const int trin = (int)tri(n), nn = n * n, woff = T * trin;
   const R rho = A.rho[b], rf = rho * A.rff, al = A.alpha, sw = A.sw[b], sigma = A.sigma;
   const bool slack = A.use_slack != 0;
+  const bool apI = A.apid[grp] != 0;  // A+_t = [-I 0] for the whole group
   // group bases of the interleaved arrays (element e of this group: base[e * 32 + lane])
   auto gb = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp; };
   const R* F = gb(A.ops, z.ops);
@@ -423,7 +453,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   auto fetch_bwd_b = [&](int t) {
     if (t < N) {
       copy(BB + oAm * L32, AM + (size_t)t * nx * n * L32, nx * n);
-      copy(BB + oAp * L32, AP + (size_t)t * nx * n * L32, nx * n);
+      if (!apI) copy(BB + oAp * L32, AP + (size_t)t * nx * n * L32, nx * n);
       copy(BB + oc * L32, CC + (size_t)t * nx * L32, nx);
       copy(BB + oyf * L32, YFD + (size_t)t * nx * L32, nx);
     }
@@ -520,7 +550,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
         if (q < nx) {
           if (t < N) {
             const R cx = il_dot<NB>(BBl + (oAm + q * n) * L32, L32, xtl, n) +
-                         il_dot<NB>(BBl + (oAp + q * n) * L32, L32, xnl, n);
+                         (apI ? -xnl[q * L32] : il_dot<NB>(BBl + (oAp + q * n) * L32, L32, xnl, n));
             const R cr = BBl[(oc + q) * L32];
             const R y = BBl[(oyf + q) * L32] + rf * al * (cx - cr);
             if (act) YFDl[(t * nx + q) * L32] = y;
@@ -568,7 +598,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
       __syncthreads();  // ctv, gtv, ct0v complete
       if (own) {  // gamma for the next iteration (column i)
         if (t < N) {  // the A+ terms of the dynamics rows of stage t complete gamma_{t+1}
-          const R ap = il_dot<NB>(BBl + (oAp + i) * L32, n * L32, ctvl, nx);
+          const R ap = apI ? (i < nx ? -ctvl[i * L32] : R(0)) : il_dot<NB>(BBl + (oAp + i) * L32, n * L32, ctvl, nx);
           if (act) GAMl[((t + 1) * n + i) * L32] = (gval + (ap + geq)) + giq;
         }
         const R val = sigma * xr - BBl[(oq + i) * L32];
@@ -793,6 +823,9 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   inl(P.in.z_g, A.zg, z.zm);
   inl(P.in.y_g, A.yg, z.zm);
   inl(P.in.xi_g, A.xig, z.zm);
+  if (rc) return rc;
+  il_ap_identity_kernel<R><<<(unsigned)groups(Nb), kWarp, 0, st>>>(A);
+  chk((int)cudaPeekAtLastError());
   if (rc) return rc;
   return il_dispatch<R>(n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
