@@ -40,21 +40,23 @@ METRIC = "MPC solves/sec (quadrotor N=50, batch 65536)"
 NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
 # DRAM bytes (read + write) per problem of one launch of il_admm_kernel (the
 # 30 ADMM iterations of the direct path), from the ncu capture summarised in
-# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 55.64 GB; A+ = [-I 0] detected, not streamed).
-NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 6.792e6
+# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 52.04 GB; A+ = [-I 0] and the unit rows of G detected, not streamed).
+NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 6.353e6
 
 
-def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False):
+def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_select=False):
     """Bytes one problem must move in one ADMM iteration of the interleaved
     direct path (il_admm_kernel): the factor read in both sweeps (L_t^-1
     packed and W_t: E_f = T n(n+1)/2 + N n^2 values, twice), the QP rows of
     the iteration (A-, A+, G, q, c, l, u) once, and the state it updates
     (x, y_fdyn, z_g, y_g read and written; gamma and the forward-sweep vector
     y written once and read once).  With ap_identity (A+_t = [-I 0], which the
-    kernel detects and then does not stream) A+ is not counted."""
+    kernel detects and then does not stream) A+ is not counted, with g_select
+    (every inequality row a unit vector on the same columns in every stage,
+    likewise detected) G is not counted."""
     N = T - 1
     ef = T * n * (n + 1) // 2 + N * n * n
-    rows = (1 if ap_identity else 2) * N * nx * n + T * m * n
+    rows = (1 if ap_identity else 2) * N * nx * n + (0 if g_select else T * m * n)
     vecs = T * n + N * nx + 2 * T * m
     state = 2 * (T * n + N * nx + 2 * T * m) + 2 * T * n + 2 * T * n
     return w * (2 * ef + rows + vecs + state)
@@ -206,19 +208,19 @@ def pcg_roofline(T, n, nx, m, n0, shard, kms, hbm):
                 "PCG iteration) per launch time over that peak, > 1 because those bytes are never moved"}
 
 
-def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, ap_identity=False):
+def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, ap_identity=False, g_select=False):
     """Roofline object of the interleaved direct path's iteration kernel
     (il_admm_kernel, HBM bound): algorithmic bytes of its ADMM iterations
     over its launch time (CUDA events recorded by the library on the launch
     stream, tmpc_admm_iteration_timing)."""
-    bytes_launch = ADMM * direct_bytes_per_problem_iteration(T, n, nx, m, n0, 4, ap_identity) * shard
+    bytes_launch = ADMM * direct_bytes_per_problem_iteration(T, n, nx, m, n0, 4, ap_identity, g_select) * shard
     achieved = bytes_launch / (ims / 1e3) / 1e9
     return {
         "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
         "peak_source": f"{pk_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
         "traffic": NCU_DIRECT_DRAM_BYTES_PER_PROBLEM * shard, "kernel": "il_admm_kernel",
         "kernel_ms_per_launch": ims, "algorithmic_bytes_per_launch": bytes_launch,
-        "call_ms": kms, "call_frac_of_kernel": ims / kms, "a_plus_streamed": not ap_identity,
+        "call_ms": kms, "call_frac_of_kernel": ims / kms, "a_plus_streamed": not ap_identity, "g_streamed": not g_select,
         "note": "one launch = the 30 ADMM iterations of one SQP iteration for the whole shard; algorithmic bytes = "
                 "per ADMM iteration the block-Cholesky factor read in both sweeps, the QP rows (A-, A+, G, q, c, "
                 "l, u) once and the updated state; traffic = measured DRAM bytes of that kernel (ncu, 8192 "
@@ -824,7 +826,11 @@ def main():
             ap = qp.eq.A_plus
             pat = torch.zeros(ap.shape[-2:], dtype=ap.dtype, device=ap.device)
             pat[:, :nx] = -torch.eye(nx, dtype=ap.dtype, device=ap.device)
-            roof = direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, bool((ap == pat).all()))
+            G = qp.ineq.G
+            g0 = G[:1, :1]
+            gsel = bool((G == g0).all()) and bool(((g0 == 1).sum(-1) == 1).all()) and bool(
+                ((g0 == 0) | (g0 == 1)).all())
+            roof = direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, bool((ap == pat).all()), gsel)
             per_call = direct_launches_per_solve(n0, m)
         else:
             roof = pcg_roofline(T, n, nx, m, n0, shard, kms, hbm)

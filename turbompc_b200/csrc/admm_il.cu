@@ -75,7 +75,7 @@ struct IlSizes {
 template <typename R>
 struct IlWs {
   size_t ops, q, a0, am, ap, g, c0, c, l, u, x, yf0, yfd, zg, yg, xig, gam, ys, rho, sw;  // R offsets
-  size_t act, iters, status, fstat, chg, apid, gate;                                     // int offsets
+  size_t act, iters, status, fstat, chg, apid, gsel, gcol, gate;                         // int offsets
   size_t rbytes, bytes;
   IlWs(int Nb, int T, int n, int nx, int n0, int m) {
     const IlSizes z(T, n, nx, n0, m);
@@ -98,6 +98,8 @@ struct IlWs {
     fstat = io; io += G32;
     chg = io; io += G32;
     apid = io; io += groups(Nb);
+    gsel = io; io += groups(Nb);
+    gcol = io; io += groups(Nb) * (size_t)(m > 0 ? m : 1);
     gate = io; io += 4;
     bytes = rbytes + io * sizeof(int);
   }
@@ -107,7 +109,7 @@ struct IlWs {
 template <typename R>
 struct IlArgs {
   R *ops, *q, *a0, *am, *ap, *g, *c0, *c, *l, *u, *x, *yf0, *yfd, *zg, *yg, *xig, *gam, *ys, *rho, *sw;
-  int *act, *iters, *status, *fstat, *chg, *apid, *gate;
+  int *act, *iters, *status, *fstat, *chg, *apid, *gsel, *gcol, *gate;
   int Nb, T, n, nx, n0, m, use_slack;
   R sigma, alpha, rff;
 };
@@ -124,6 +126,8 @@ IlArgs<R> il_args(void* ws, const AdmmParams<R>& P) {
   a.rho = r + L.rho; a.sw = r + L.sw;
   a.act = i + L.act; a.iters = i + L.iters; a.status = i + L.status; a.fstat = i + L.fstat; a.chg = i + L.chg;
   a.apid = i + L.apid;
+  a.gsel = i + L.gsel;
+  a.gcol = i + L.gcol;
   a.gate = i + L.gate;
   a.Nb = P.Nb; a.T = P.T; a.n = P.n; a.nx = P.nx; a.n0 = P.n0; a.m = P.m; a.use_slack = P.use_slack;
   a.sigma = P.sigma; a.alpha = P.alpha; a.rff = P.rho_f_factor;
@@ -179,6 +183,40 @@ __global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
   }
   ok = __all_sync(0xffffffffu, ok);
   if (lane == 0) A.apid[grp] = ok ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// Structure of G: box constraints on single variables (the quadrotor's thrust
+// bounds) make every inequality row a unit vector, G_t[k] = e_{c_k}, with the
+// same columns c_k in every stage.  One warp per group takes the columns from
+// its first problem's first stage and checks every row of its 32 problems
+// exactly; where all match, the iteration kernel forms G x and G^T y from the
+// columns (the same sums: the other terms are exact zeros) and does not stream
+// G each iteration.
+// ---------------------------------------------------------------------------
+template <typename R>
+__global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
+  const int lane = threadIdx.x, grp = blockIdx.x;
+  const int b = grp * kWarp + lane;
+  const int T = A.T, n = A.n, m = A.m;
+  const IlSizes z(T, n, A.nx, A.n0, m);
+  const R* g = A.g + (size_t)grp * z.g * kWarp;  // group base: element e of lane l at g[e * 32 + l]
+  bool ok = true;
+  for (int k = 0; k < m; ++k) {
+    // column of the single 1 in row k of problem 0 (lane 0), stage 0; -1 if none
+    int c = -1;
+    for (int j = 0; j < n; ++j)
+      if (g[(size_t)(k * n + j) * kWarp] == R(1)) c = j;
+    if (lane == 0) A.gcol[(size_t)grp * m + k] = c;
+    if (c < 0) ok = false;
+    if (b < A.Nb && ok) {
+      for (int t = 0; t < T && ok; ++t)
+        for (int j = 0; j < n; ++j)
+          if (g[((size_t)(t * m + k) * n + j) * kWarp + lane] != (j == c ? R(1) : R(0))) ok = false;
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (lane == 0) A.gsel[grp] = (ok && m > 0) ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -402,6 +440,8 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   const R rho = A.rho[b], rf = rho * A.rff, al = A.alpha, sw = A.sw[b], sigma = A.sigma;
   const bool slack = A.use_slack != 0;
   const bool apI = A.apid[grp] != 0;  // A+_t = [-I 0] for the whole group
+  const bool gS = A.gsel[grp] != 0;   // G_t[k] = e_{gc[k]} for the whole group
+  const int* gc = A.gcol + (size_t)grp * (m > 0 ? m : 1);
   // group bases of the interleaved arrays (element e of this group: base[e * 32 + lane])
   auto gb = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp; };
   const R* F = gb(A.ops, z.ops);
@@ -458,7 +498,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
       copy(BB + oyf * L32, YFD + (size_t)t * nx * L32, nx);
     }
     if (m > 0) {
-      copy(BB + oG * L32, Gm + (size_t)t * m * n * L32, m * n);
+      if (!gS) copy(BB + oG * L32, Gm + (size_t)t * m * n * L32, m * n);
       copy(BB + ozg * L32, ZG + (size_t)t * m * L32, m);
       copy(BB + oyg * L32, YG + (size_t)t * m * L32, m);
       copy(BB + ol * L32, LL + (size_t)t * m * L32, m);
@@ -558,7 +598,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
           }
         } else {
           const int k = q - nx;
-          const R gx = il_dot<NB>(BBl + (oG + k * n) * L32, L32, xtl, n);
+          const R gx = gS ? xtl[gc[k] * L32] : il_dot<NB>(BBl + (oG + k * n) * L32, L32, xtl, n);
           const R zold = BBl[(ozg + k) * L32], ygo = BBl[(oyg + k) * L32];
           const R zt = al * gx + (R(1) - al) * zold + ygo / rho;
           R cl = zt;
@@ -614,7 +654,12 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
           }
         }
         R iq = R(0);
-        for (int k = 0; k < m; ++k) iq += BBl[(oG + k * n + i) * L32] * gtvl[k * L32];
+        if (gS) {
+          for (int k = 0; k < m; ++k)
+            if (gc[k] == i) iq += gtvl[k * L32];
+        } else {
+          for (int k = 0; k < m; ++k) iq += BBl[(oG + k * n + i) * L32] * gtvl[k * L32];
+        }
         if (t == 0) {
           if (act) GAMl[i * L32] = (val + eq) + iq;
         } else {
@@ -826,6 +871,10 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   if (rc) return rc;
   il_ap_identity_kernel<R><<<(unsigned)groups(Nb), kWarp, 0, st>>>(A);
   chk((int)cudaPeekAtLastError());
+  if (m > 0) {
+    il_g_select_kernel<R><<<(unsigned)groups(Nb), kWarp, 0, st>>>(A);
+    chk((int)cudaPeekAtLastError());
+  }
   if (rc) return rc;
   return il_dispatch<R>(n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
