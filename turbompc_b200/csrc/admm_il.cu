@@ -155,6 +155,10 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
   A.status[b] = 0;
   A.fstat[b] = 0;
   A.chg[b] = 0;
+  if ((b & (kWarp - 1)) == 0) {  // per-group structure flags, cleared by the checks on a mismatch
+    A.apid[b / kWarp] = 1;
+    A.gsel[b / kWarp] = 1;
+  }
   if (b == 0) A.gate[0] = 0;
 }
 
@@ -168,21 +172,19 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
 // ---------------------------------------------------------------------------
 template <typename R>
 __global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
-  const int lane = threadIdx.x, grp = blockIdx.x;
+  // one warp per (group, stage): lane l checks A+_t of problem 32 grp + l;
+  // apid[grp] was set to 1 by il_scalars_in_kernel and is cleared on a mismatch
+  const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
   const int b = grp * kWarp + lane;
   const IlSizes z(A.T, A.n, A.nx, A.n0, A.m);
   const int n = A.n, nx = A.nx;
   bool ok = true;
   if (b < A.Nb) {
-    const R* p = A.ap + (size_t)grp * z.am * kWarp + lane;
-    for (size_t e = 0; e < z.am && ok; ++e) {
-      const int rem = (int)(e % ((size_t)nx * n));
-      const int k = rem / n, j = rem - k * n;
-      ok = p[e * kWarp] == (j == k ? R(-1) : R(0));
-    }
+    const R* p = A.ap + ((size_t)grp * z.am + (size_t)t * nx * n) * kWarp + lane;
+    for (int k = 0; k < nx; ++k)
+      for (int j = 0; j < n; ++j) ok = ok && (p[(size_t)(k * n + j) * kWarp] == (j == k ? R(-1) : R(0)));
   }
-  ok = __all_sync(0xffffffffu, ok);
-  if (lane == 0) A.apid[grp] = ok ? 1 : 0;
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) A.apid[grp] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -196,27 +198,26 @@ __global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
 // ---------------------------------------------------------------------------
 template <typename R>
 __global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
-  const int lane = threadIdx.x, grp = blockIdx.x;
+  // one warp per (group, stage); gsel[grp] was set to 1 by il_scalars_in_kernel
+  // and is cleared on a mismatch
+  const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
   const int b = grp * kWarp + lane;
-  const int T = A.T, n = A.n, m = A.m;
-  const IlSizes z(T, n, A.nx, A.n0, m);
+  const int n = A.n, m = A.m;
+  const IlSizes z(A.T, n, A.nx, A.n0, m);
   const R* g = A.g + (size_t)grp * z.g * kWarp;  // group base: element e of lane l at g[e * 32 + l]
   bool ok = true;
   for (int k = 0; k < m; ++k) {
-    // column of the single 1 in row k of problem 0 (lane 0), stage 0; -1 if none
+    // column of the single 1 in row k of the group's first problem, first stage; -1 if none
     int c = -1;
     for (int j = 0; j < n; ++j)
       if (g[(size_t)(k * n + j) * kWarp] == R(1)) c = j;
-    if (lane == 0) A.gcol[(size_t)grp * m + k] = c;
+    if (t == 0 && lane == 0) A.gcol[(size_t)grp * m + k] = c;
     if (c < 0) ok = false;
-    if (b < A.Nb && ok) {
-      for (int t = 0; t < T && ok; ++t)
-        for (int j = 0; j < n; ++j)
-          if (g[((size_t)(t * m + k) * n + j) * kWarp + lane] != (j == c ? R(1) : R(0))) ok = false;
-    }
+    if (b < A.Nb && ok)
+      for (int j = 0; j < n; ++j)
+        ok = ok && (g[((size_t)(t * m + k) * n + j) * kWarp + lane] == (j == c ? R(1) : R(0)));
   }
-  ok = __all_sync(0xffffffffu, ok);
-  if (lane == 0) A.gsel[grp] = (ok && m > 0) ? 1 : 0;
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) A.gsel[grp] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -869,11 +870,13 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   inl(P.in.y_g, A.yg, z.zm);
   inl(P.in.xi_g, A.xig, z.zm);
   if (rc) return rc;
-  il_ap_identity_kernel<R><<<(unsigned)groups(Nb), kWarp, 0, st>>>(A);
+  il_ap_identity_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)N), kWarp, 0, st>>>(A);
   chk((int)cudaPeekAtLastError());
   if (m > 0) {
-    il_g_select_kernel<R><<<(unsigned)groups(Nb), kWarp, 0, st>>>(A);
+    il_g_select_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)T), kWarp, 0, st>>>(A);
     chk((int)cudaPeekAtLastError());
+  } else {
+    cudaMemsetAsync(A.gsel, 0, groups(Nb) * sizeof(int), st);
   }
   if (rc) return rc;
   return il_dispatch<R>(n, [&](auto tag) {
