@@ -65,11 +65,13 @@ def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_
 
 def direct_launches_per_solve(n0, m, check_every=0):
     """Kernel launches of one direct-path ADMM call (fixed counts): scalars in,
-    the interleaving of each non-empty QP / state array, assembly, factor,
-    first gamma, the iteration kernel, the conversions back, scalars out."""
+    the interleaving of each non-empty QP / state array, the structure checks
+    of A+ and G, assembly, factor, first gamma, the iteration kernel, the
+    conversions back, scalars out."""
     conv_in = 5 + (2 if n0 else 0) + (3 if m else 0) + 2 + (1 if n0 else 0) + (3 if m else 0)
     conv_out = 2 + (1 if n0 else 0) + (3 if m else 0)
-    return 1 + conv_in + 3 + 1 + conv_out + 1
+    checks = 1 + (1 if m else 0)
+    return 1 + conv_in + checks + 3 + 1 + conv_out + 1
 
 
 def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG):
