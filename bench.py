@@ -68,7 +68,7 @@ def direct_launches_per_solve(n0, m, check_every=0):
     the interleaving of each non-empty QP / state array, the structure checks
     of A+ and G, assembly, factor, first gamma, the iteration kernel, the
     conversions back, scalars out."""
-    conv_in = 5 + (2 if n0 else 0) + (3 if m else 0) + 2 + (1 if n0 else 0) + (3 if m else 0)
+    conv_in = 6 + (3 if n0 else 0) + (6 if m else 0)  # q A- A+ c x y_fdyn; A0 c0 y_f0; G l u z_g y_g xi_g
     conv_out = 2 + (1 if n0 else 0) + (3 if m else 0)
     checks = 1 + (1 if m else 0)
     return 1 + conv_in + checks + 3 + 1 + conv_out + 1
