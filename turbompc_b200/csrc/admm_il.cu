@@ -232,6 +232,28 @@ __global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
 // D and E come from the caller's problem-major arrays (Theta's element (r, c),
 // r >= c, takes D[c][r], as the other assembly paths do).
 // ---------------------------------------------------------------------------
+// A row of n <= NB values of a problem-major array into registers (zero
+// beyond n): 128-bit loads when vec (16-byte aligned row, n a multiple of the
+// vector width), else scalar loads.
+template <int NB, typename R>
+__device__ __forceinline__ void il_load_row(R (&dst)[NB], const R* src, int n, bool vec) {
+  constexpr int V = 16 / sizeof(R);
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < NB; j += V) {
+      if (j < n) {
+        ld128(&dst[j], src + j);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) dst[j + v] = R(0);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NB; ++j) dst[j] = j < n ? src[j] : R(0);
+  }
+}
+
 template <int NB, typename R>
 __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP qp, const int* gate) {
   if (gate && *gate == 0) return;
@@ -267,17 +289,26 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
 #pragma unroll
   for (int e = 0; e < TR; ++e) acc[e] = R(0);
   for (int k = 0; k < m; ++k) rank1(Gl + (size_t)(t * m + k) * n * kWarp);
+  // Theta's column c takes row c of D_t (D[c][r], r >= c): rows read whole, with
+  // 128-bit loads where the rows are 16-byte aligned (a lane's row is one
+  // contiguous run in the caller's problem-major array)
+  const bool vec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
 #pragma unroll
-  for (int r = 0; r < NB; ++r)
+  for (int c = 0; c < NB; ++c) {
+    if (c < n) {
+      R dr[NB];
+      il_load_row<NB>(dr, D + c * n, n, vec);
 #pragma unroll
-    for (int c = 0; c <= r; ++c) {
-      if (r < n) {
-        R v = D[c * n + r];
-        if (r == c) v += A.sigma;
-        v += rho * acc[LI(r, c)];
-        acc[LI(r, c)] = v;
+      for (int r = c; r < NB; ++r) {
+        if (r < n) {
+          R v = dr[r];
+          if (r == c) v += A.sigma;
+          v += rho * acc[LI(r, c)];
+          acc[LI(r, c)] = v;
+        }
       }
     }
+  }
   // park (D + sigma I) + rho G^T G in the output, then + rho_f A^T A
 #pragma unroll
   for (int r = 0; r < NB; ++r)
@@ -322,12 +353,17 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
 #pragma unroll
         for (int j = 0; j < NB; ++j) acc[i * NB + j] = fma(x[i], y[j], acc[i * NB + j]);
     }
+    const bool evec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(E) & 15) == 0;
 #pragma unroll
-    for (int i = 0; i < HB; ++i)
+    for (int i = 0; i < HB; ++i) {
+      if (h + i < n) {
+        R er[NB];
+        il_load_row<NB>(er, E + (h + i) * n, n, evec);
 #pragma unroll
-      for (int j = 0; j < NB; ++j)
-        if (h + i < n && j < n)
-          O[(size_t)(T * trin + (t * n + h + i) * n + j) * kWarp] = E[(h + i) * n + j] + rf * acc[i * NB + j];
+        for (int j = 0; j < NB; ++j)
+          if (j < n) O[(size_t)(T * trin + (t * n + h + i) * n + j) * kWarp] = er[j] + rf * acc[i * NB + j];
+      }
+    }
   }
 }
 
