@@ -181,8 +181,13 @@ __global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
   bool ok = true;
   if (b < A.Nb) {
     const R* p = A.ap + ((size_t)grp * z.am + (size_t)t * nx * n) * kWarp + lane;
-    for (int k = 0; k < nx; ++k)
-      for (int j = 0; j < n; ++j) ok = ok && (p[(size_t)(k * n + j) * kWarp] == (j == k ? R(-1) : R(0)));
+    int bad = 0;  // no short-circuit: the loads stay independent
+#pragma unroll 8
+    for (int e = 0; e < nx * n; ++e) {
+      const int k = e / n, j = e - k * n;
+      bad |= p[(size_t)e * kWarp] != (j == k ? R(-1) : R(0));
+    }
+    ok = bad == 0;
   }
   if (!__all_sync(0xffffffffu, ok) && lane == 0) A.apid[grp] = 0;
 }
@@ -213,9 +218,12 @@ __global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
       if (g[(size_t)(k * n + j) * kWarp] == R(1)) c = j;
     if (t == 0 && lane == 0) A.gcol[(size_t)grp * m + k] = c;
     if (c < 0) ok = false;
-    if (b < A.Nb && ok)
-      for (int j = 0; j < n; ++j)
-        ok = ok && (g[((size_t)(t * m + k) * n + j) * kWarp + lane] == (j == c ? R(1) : R(0)));
+    if (b < A.Nb && ok) {
+      int bad = 0;
+#pragma unroll 8
+      for (int j = 0; j < n; ++j) bad |= g[((size_t)(t * m + k) * n + j) * kWarp + lane] != (j == c ? R(1) : R(0));
+      ok = bad == 0;
+    }
   }
   if (!__all_sync(0xffffffffu, ok) && lane == 0) A.gsel[grp] = 0;
 }

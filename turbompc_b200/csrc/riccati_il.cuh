@@ -347,42 +347,60 @@ struct SchurMap {
   }
 };
 
+// Each block converts kConvTiles consecutive 32-element tiles of one group
+// (all loads of the block issued before its stores).
+constexpr int kConvTiles = 4;
+
 template <typename R, class Map>
 __global__ void __launch_bounds__(256) interleave_kernel(const R* __restrict__ in, R* out, int Nb, size_t E_in,
                                                          size_t E, Map map) {
-  __shared__ R tile[32][33];
+  __shared__ R tile[kConvTiles][32][33];
   const size_t grp = blockIdx.y;
-  const size_t e0 = (size_t)blockIdx.x * 32;
+  const size_t e0 = (size_t)blockIdx.x * 32 * kConvTiles;
   const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int r = ty; r < 32; r += 8) {
-    const size_t b = grp * 32 + r, e = e0 + tx;
-    tile[r][tx] = (b < (size_t)Nb && e < E) ? in[b * E_in + map(e)] : R(0);
-  }
+#pragma unroll
+  for (int k = 0; k < kConvTiles; ++k)
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {
+      const size_t b = grp * 32 + r, e = e0 + (size_t)k * 32 + tx;
+      tile[k][r][tx] = (b < (size_t)Nb && e < E) ? in[b * E_in + map(e)] : R(0);
+    }
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const size_t e = e0 + r;
-    if (e < E) out[(grp * E + e) * 32 + tx] = tile[tx][r];
-  }
+#pragma unroll
+  for (int k = 0; k < kConvTiles; ++k)
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {
+      const size_t e = e0 + (size_t)k * 32 + r;
+      if (e < E) out[(grp * E + e) * 32 + tx] = tile[k][tx][r];
+    }
 }
 
 template <typename R>
 __global__ void __launch_bounds__(256) deinterleave_kernel(const R* __restrict__ in, R* out, int Nb, size_t E) {
-  __shared__ R tile[32][33];
+  __shared__ R tile[kConvTiles][32][33];
   const size_t grp = blockIdx.y;
-  const size_t e0 = (size_t)blockIdx.x * 32;
+  const size_t e0 = (size_t)blockIdx.x * 32 * kConvTiles;
   const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int r = ty; r < 32; r += 8) {
-    const size_t e = e0 + r;
-    tile[r][tx] = e < E ? in[(grp * E + e) * 32 + tx] : R(0);
-  }
+#pragma unroll
+  for (int k = 0; k < kConvTiles; ++k)
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {
+      const size_t e = e0 + (size_t)k * 32 + r;
+      tile[k][r][tx] = e < E ? in[(grp * E + e) * 32 + tx] : R(0);
+    }
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const size_t b = grp * 32 + r, e = e0 + tx;
-    if (b < (size_t)Nb && e < E) out[b * E + e] = tile[tx][r];
-  }
+#pragma unroll
+  for (int k = 0; k < kConvTiles; ++k)
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {
+      const size_t b = grp * 32 + r, e = e0 + (size_t)k * 32 + tx;
+      if (b < (size_t)Nb && e < E) out[b * E + e] = tile[k][tx][r];
+    }
 }
 
-inline bool grid_ok(int Nb, size_t E) { return groups(Nb) <= 65535 && (E + 31) / 32 <= 0x7fffffffu; }
+inline bool grid_ok(int Nb, size_t E) {
+  return groups(Nb) <= 65535 && (E + 32 * kConvTiles - 1) / (32 * kConvTiles) <= 0x7fffffffu;
+}
 
 template <typename R, class Map>
 int interleave(int Nb, size_t E_in, size_t E, const R* in, R* out, Map map, cudaStream_t st) {
@@ -390,7 +408,7 @@ int interleave(int Nb, size_t E_in, size_t E, const R* in, R* out, Map map, cuda
   if (Nb == 0 || E == 0) return TMPC_OK;
   if (!in || !out) return TMPC_ERR_NULL_ARG;
   if (!grid_ok(Nb, E)) return TMPC_ERR_BAD_DIMS;
-  dim3 grid((unsigned)((E + 31) / 32), (unsigned)groups(Nb)), block(32, 8);
+  dim3 grid((unsigned)((E + 32 * kConvTiles - 1) / (32 * kConvTiles)), (unsigned)groups(Nb)), block(32, 8);
   interleave_kernel<R, Map><<<grid, block, 0, st>>>(in, out, Nb, E_in, E, map);
   return (int)cudaPeekAtLastError();
 }
@@ -401,7 +419,7 @@ int deinterleave(int Nb, size_t E, const R* in, R* out, cudaStream_t st) {
   if (Nb == 0 || E == 0) return TMPC_OK;
   if (!in || !out) return TMPC_ERR_NULL_ARG;
   if (!grid_ok(Nb, E)) return TMPC_ERR_BAD_DIMS;
-  dim3 grid((unsigned)((E + 31) / 32), (unsigned)groups(Nb)), block(32, 8);
+  dim3 grid((unsigned)((E + 32 * kConvTiles - 1) / (32 * kConvTiles)), (unsigned)groups(Nb)), block(32, 8);
   deinterleave_kernel<R><<<grid, block, 0, st>>>(in, out, Nb, E);
   return (int)cudaPeekAtLastError();
 }
