@@ -40,10 +40,32 @@ __global__ void __launch_bounds__(kKktThreads) kkt_residual_kernel(TmpcQP qpa, c
     const R* xt = x + (size_t)t * n;
     R s = qp.q[e];
     const R* Dt = qp.D + (size_t)t * n * n + (size_t)j * n;
-    for (int k = 0; k < n; ++k) s = fma(Dt[k], xt[k], s);
+    // rows of D_t and E_{t-1} are contiguous per thread: 128-bit loads where aligned
+    constexpr int V = 16 / sizeof(R);
+    const bool vec = n % V == 0 && (reinterpret_cast<uintptr_t>(qp.D) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(qp.E) & 15) == 0;
+    if (vec) {
+      for (int k = 0; k < n; k += V) {
+        R w[V];
+        ld128(w, Dt + k);
+#pragma unroll
+        for (int v = 0; v < V; ++v) s = fma(w[v], xt[k + v], s);
+      }
+    } else {
+      for (int k = 0; k < n; ++k) s = fma(Dt[k], xt[k], s);
+    }
     if (t > 0) {
       const R* Et = qp.E + (size_t)(t - 1) * n * n + (size_t)j * n;  // E_{t-1}[j][:]
-      for (int k = 0; k < n; ++k) s = fma(Et[k], xt[k - n], s);
+      if (vec) {
+        for (int k = 0; k < n; k += V) {
+          R w[V];
+          ld128(w, Et + k);
+#pragma unroll
+          for (int v = 0; v < V; ++v) s = fma(w[v], xt[k + v - n], s);
+        }
+      } else {
+        for (int k = 0; k < n; ++k) s = fma(Et[k], xt[k - n], s);
+      }
     }
     if (t < N) {
       const R* Et = qp.E + (size_t)t * n * n;  // E_t[:][j]
