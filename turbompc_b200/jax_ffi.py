@@ -9,7 +9,9 @@ package is built and tested, so this module is untested here).
 After ``register()``, the reference's adapter
 (turbompc/solvers/admm/admm_ffi_backend.py:271-430, which calls
 ``jax.ffi.ffi_call("admm_fused_cuda" / "admm_fused_cuda_f64", ...)``) runs the
-b200 fused ADMM kernel with its operands, attributes and results unchanged.
+b200 fused ADMM kernel with its operands, attributes and results unchanged, and
+the cuDSS adapter (admm/admm_cudss_ffi_backend.py, targets "admm_cudss_cuda" /
+"admm_cudss_cuda_f64") runs the b200 direct (block-Cholesky) solve.
 """
 from __future__ import annotations
 
@@ -18,7 +20,8 @@ import os
 
 from . import build as _build
 
-TARGETS = {"admm_fused_cuda": "AdmmB200Cuda", "admm_fused_cuda_f64": "AdmmB200CudaF64"}
+TARGETS = {"admm_fused_cuda": "AdmmB200Cuda", "admm_fused_cuda_f64": "AdmmB200CudaF64",
+           "admm_cudss_cuda": "AdmmB200DirectCuda", "admm_cudss_cuda_f64": "AdmmB200DirectCudaF64"}
 
 
 def register(lib_path: str = _build.FFI_LIB) -> None:
