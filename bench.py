@@ -45,7 +45,7 @@ NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
 NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 6.353e6
 
 
-def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_select=False):
+def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_select=False, w_rows=None):
     """Bytes one problem must move in one ADMM iteration of the interleaved
     direct path (il_admm_kernel): the factor read in both sweeps (L_t^-1
     packed and W_t: E_f = T n(n+1)/2 + N n^2 values, twice), the QP rows of
@@ -54,9 +54,13 @@ def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_
     y written once and read once).  With ap_identity (A+_t = [-I 0], which the
     kernel detects and then does not stream) A+ is not counted, with g_select
     (every inequality row a unit vector on the same columns in every stage,
-    likewise detected) G is not counted."""
+    likewise detected) G is not counted.  w_rows: the rows of each W_t that
+    are not exact zeros (nx when the rows of Phi_t for stage t+1's controls
+    vanish, which the library detects after each factor; n otherwise): only
+    those rows are read."""
     N = T - 1
-    ef = T * n * (n + 1) // 2 + N * n * n
+    wr = n if w_rows is None else w_rows
+    ef = T * n * (n + 1) // 2 + N * wr * n
     rows = (1 if ap_identity else 2) * N * nx * n + (0 if g_select else T * m * n)
     vecs = T * n + N * nx + 2 * T * m
     state = 2 * (T * n + N * nx + 2 * T * m) + 2 * T * n + 2 * T * n
@@ -66,12 +70,12 @@ def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_
 def direct_launches_per_solve(n0, m, check_every=0):
     """Kernel launches of one direct-path ADMM call (fixed counts): scalars in,
     the interleaving of each non-empty QP / state array, the structure checks
-    of A+ and G, assembly, factor, first gamma, the iteration kernel, the
-    conversions back, scalars out."""
+    of A+ and G, assembly, factor, the zero-row check of W, first gamma, the
+    iteration kernel, the conversions back, scalars out."""
     conv_in = 6 + (3 if n0 else 0) + (6 if m else 0)  # q A- A+ c x y_fdyn; A0 c0 y_f0; G l u z_g y_g xi_g
     conv_out = 2 + (1 if n0 else 0) + (3 if m else 0)
     checks = 1 + (1 if m else 0)
-    return 1 + conv_in + checks + 3 + 1 + conv_out + 1
+    return 1 + conv_in + checks + 4 + 1 + conv_out + 1
 
 
 def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG):
@@ -211,12 +215,14 @@ def pcg_roofline(T, n, nx, m, n0, shard, kms, hbm):
                 "PCG iteration) per launch time over that peak, > 1 because those bytes are never moved"}
 
 
-def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, ap_identity=False, g_select=False):
+def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, ap_identity=False, g_select=False,
+                    w_rows=None):
     """Roofline object of the interleaved direct path's iteration kernel
     (il_admm_kernel, HBM bound): algorithmic bytes of its ADMM iterations
     over its launch time (CUDA events recorded by the library on the launch
     stream, tmpc_admm_iteration_timing)."""
-    bytes_launch = ADMM * direct_bytes_per_problem_iteration(T, n, nx, m, n0, 4, ap_identity, g_select) * shard
+    bytes_launch = ADMM * direct_bytes_per_problem_iteration(T, n, nx, m, n0, 4, ap_identity, g_select,
+                                                             w_rows) * shard
     achieved = bytes_launch / (ims / 1e3) / 1e9
     return {
         "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -224,6 +230,7 @@ def direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, ap_identity=
         "traffic": NCU_DIRECT_DRAM_BYTES_PER_PROBLEM * shard, "kernel": "il_admm_kernel",
         "kernel_ms_per_launch": ims, "algorithmic_bytes_per_launch": bytes_launch,
         "call_ms": kms, "call_frac_of_kernel": ims / kms, "a_plus_streamed": not ap_identity, "g_streamed": not g_select,
+        "w_rows_read": n if w_rows is None else w_rows,
         "note": "one launch = the 30 ADMM iterations of one SQP iteration for the whole shard; algorithmic bytes = "
                 "per ADMM iteration the block-Cholesky factor read in both sweeps, the QP rows (A-, A+, G, q, c, "
                 "l, u) once and the updated state; traffic = measured DRAM bytes of that kernel (ncu, 8192 "
@@ -833,7 +840,11 @@ def main():
             g0 = G[:1, :1]
             gsel = bool((G == g0).all()) and bool(((g0 == 1).sum(-1) == 1).all()) and bool(
                 ((g0 == 0) | (g0 == 1)).all())
-            roof = direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, bool((ap == pat).all()), gsel)
+            # rows nx.. of Phi_t = E_t + rho_f A+_t^T A-_t vanish when A+'s control
+            # columns and E's control rows are zero: W_t keeps nx rows
+            wz = bool((ap[..., nx:] == 0).all()) and bool((qp.cost.E[..., nx:, :] == 0).all())
+            roof = direct_roofline(T, n, nx, m, n0, shard, ims, kms, hbm, pk_kind, bool((ap == pat).all()), gsel,
+                                   nx if wz else n)
             per_call = direct_launches_per_solve(n0, m)
         else:
             roof = pcg_roofline(T, n, nx, m, n0, shard, kms, hbm)

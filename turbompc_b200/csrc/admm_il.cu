@@ -50,6 +50,7 @@ namespace il {
 
 constexpr int kIlWarps = 16;  // one warp per stage row (NB <= 16)
 constexpr int kIlThreads = 32 * kIlWarps;
+constexpr int kIlCmpWarps = 8;  // compact variant: two stage rows per warp, two blocks per SM
 
 // Element counts per problem of the interleaved workspace arrays.
 struct IlSizes {
@@ -75,7 +76,7 @@ struct IlSizes {
 template <typename R>
 struct IlWs {
   size_t ops, q, a0, am, ap, g, c0, c, l, u, x, yf0, yfd, zg, yg, xig, gam, ys, rho, sw;  // R offsets
-  size_t act, iters, status, fstat, chg, apid, gsel, gcol, gate;                         // int offsets
+  size_t act, iters, status, fstat, chg, apid, gsel, gcol, wrow, gate;                   // int offsets
   size_t rbytes, bytes;
   IlWs(int Nb, int T, int n, int nx, int n0, int m) {
     const IlSizes z(T, n, nx, n0, m);
@@ -100,6 +101,7 @@ struct IlWs {
     apid = io; io += groups(Nb);
     gsel = io; io += groups(Nb);
     gcol = io; io += groups(Nb) * (size_t)(m > 0 ? m : 1);
+    wrow = io; io += groups(Nb);
     gate = io; io += 4;
     bytes = rbytes + io * sizeof(int);
   }
@@ -109,7 +111,7 @@ struct IlWs {
 template <typename R>
 struct IlArgs {
   R *ops, *q, *a0, *am, *ap, *g, *c0, *c, *l, *u, *x, *yf0, *yfd, *zg, *yg, *xig, *gam, *ys, *rho, *sw;
-  int *act, *iters, *status, *fstat, *chg, *apid, *gsel, *gcol, *gate;
+  int *act, *iters, *status, *fstat, *chg, *apid, *gsel, *gcol, *wrow, *gate;
   int Nb, T, n, nx, n0, m, use_slack;
   R sigma, alpha, rff;
 };
@@ -128,6 +130,7 @@ IlArgs<R> il_args(void* ws, const AdmmParams<R>& P) {
   a.apid = i + L.apid;
   a.gsel = i + L.gsel;
   a.gcol = i + L.gcol;
+  a.wrow = i + L.wrow;
   a.gate = i + L.gate;
   a.Nb = P.Nb; a.T = P.T; a.n = P.n; a.nx = P.nx; a.n0 = P.n0; a.m = P.m; a.use_slack = P.use_slack;
   a.sigma = P.sigma; a.alpha = P.alpha; a.rff = P.rho_f_factor;
@@ -226,6 +229,38 @@ __global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
     }
   }
   if (!__all_sync(0xffffffffu, ok) && lane == 0) A.gsel[grp] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Rows of the factor's off-diagonal blocks W_t = Phi_t L_t^-T that are exact
+// zeros.  Phi_t = E_t + rho_f A+_t^T A-_t couples stage t + 1's variables
+// (rows) to stage t's (columns); with A+_t = [-I 0] and no control-rate term
+// in E_t (the quadrotor's case) its rows nx..n-1 are zero, and so are those
+// rows of W_t.  One block per group reads rows nx..n-1 of every W_t of its
+// 32 problems (after each factor) and records in wrow[grp] how many leading
+// rows the iteration kernel has to read: nx where all the others are exact
+// zeros, n otherwise.  Skipping exact-zero products leaves every sum as it
+// was, so the iterates do not change.
+// ---------------------------------------------------------------------------
+constexpr int kWrowThreads = 128;
+template <typename R>
+__global__ void __launch_bounds__(kWrowThreads) il_w_rows_kernel(IlArgs<R> A, const int* gate) {
+  if (gate && *gate == 0) return;
+  const int lane = threadIdx.x & (kWarp - 1), w = threadIdx.x / kWarp, grp = blockIdx.x;
+  const int b = grp * kWarp + lane;
+  const int T = A.T, N = T - 1, n = A.n, nx = A.nx;
+  const size_t trin = tri(n), nn = (size_t)n * n;
+  const R* F = A.ops + (size_t)grp * op_elems(T, n) * kWarp + lane;
+  int bad = nx >= n ? 1 : 0;  // nothing to skip
+  if (b < A.Nb && !bad) {
+    for (int t = w; t < N; t += kWrowThreads / kWarp) {
+      const R* W = F + ((size_t)T * trin + (size_t)t * nn + (size_t)nx * n) * kWarp;
+#pragma unroll 8
+      for (int e = 0; e < (n - nx) * n; ++e) bad |= W[(size_t)e * kWarp] != R(0);
+    }
+  }
+  const int any = __syncthreads_or(bad);
+  if (threadIdx.x == 0) A.wrow[grp] = any ? n : nx;
 }
 
 // ---------------------------------------------------------------------------
@@ -440,19 +475,29 @@ __global__ void il_clear_chg_kernel(int* chg, int G32, int* gate) {
 // ---------------------------------------------------------------------------
 // The ADMM iterations [it0, it1) of one group of 32 problems.
 // ---------------------------------------------------------------------------
-// Stage buffer sizes (elements per problem).
-__host__ __device__ inline int il_fwd_elems(int n) { return (int)(tri(n) + (size_t)n * n + n); }
+// Stage buffer sizes (elements per problem).  The full layout keeps room for
+// every block; the compact one (CMP: A+_t = [-I 0], unit inequality rows and
+// W_t rows nx..n-1 exact zeros, all detected per group) drops A+, G and the
+// zero rows of W.
+__host__ __device__ inline int il_fwd_elems(int n, int wrows) { return (int)(tri(n) + (size_t)wrows * n + n); }
 __host__ __device__ inline int il_qp_elems(int n, int nx, int m) { return 2 * nx * n + m * n + 2 * n + 2 * nx + 4 * m; }
-__host__ __device__ inline int il_buf_b_elems(int n, int nx, int m) {
-  const int a = il_fwd_elems(n), q = il_qp_elems(n, nx, m);
+__host__ __device__ inline int il_qp_elems_cmp(int n, int nx, int m) { return nx * n + 2 * n + 2 * nx + 4 * m; }
+__host__ __device__ inline int il_buf_a_elems(int n, int nx, bool cmp) { return il_fwd_elems(n, cmp ? nx : n); }
+__host__ __device__ inline int il_buf_b_elems(int n, int nx, int m, bool cmp) {
+  const int a = il_buf_a_elems(n, nx, cmp), q = cmp ? il_qp_elems_cmp(n, nx, m) : il_qp_elems(n, nx, m);
   return a > q ? a : q;
 }
 // Dynamic shared memory: buffer A, buffer B, then the vectors
 // ush[NB], xs0[NB], xs1[NB], ctv[nx], gtv[m], ct0v[n0] (each x 32 lanes).
 template <int NB, typename R>
-size_t il_admm_smem(int n, int nx, int n0, int m) {
-  const size_t e = (size_t)il_fwd_elems(n) + il_buf_b_elems(n, nx, m) + 3 * NB + nx + m + n0;
+size_t il_admm_smem(int n, int nx, int n0, int m, bool cmp) {
+  const size_t e = (size_t)il_buf_a_elems(n, nx, cmp) + il_buf_b_elems(n, nx, m, cmp) + 3 * NB + nx + m + n0;
   return e * kWarp * sizeof(R);
+}
+// The compact layout applies to a group whose structure flags all hold.
+__device__ __forceinline__ bool il_group_compact(const int* apid, const int* gsel, const int* wrow, int grp, int nx,
+                                                 int m) {
+  return apid[grp] != 0 && (m == 0 || gsel[grp] != 0) && wrow[grp] == nx;
 }
 
 // sum_{k < cnt} a[k sa] v[k 32] with four partial sums, unrolled to NB terms
@@ -467,10 +512,16 @@ __device__ __forceinline__ R il_dot(const R* a, int sa, const R* v, int cnt) {
 }
 
 // EX: n == NB, so every stage-block loop has compile-time bounds and strides.
-template <int NB, typename R, bool EX>
-__global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> A, int it0, int it1) {
-  constexpr int NW = kIlWarps;
-  static_assert(NB <= NW, "one warp per stage row");
+// NW warps per block; warp w owns the stage rows / columns w, w + NW, ...
+// CMP: the compact variant (runs only the groups whose structure flags all
+// hold, with the compact buffers: 8 warps and two blocks per SM); the full
+// variant skips those groups when skip_cmp is set (the compact launch ran
+// them).  Both do the same arithmetic in the same order.
+template <int NB, typename R, bool EX, int NW, bool CMP>
+__global__ void __launch_bounds__(32 * NW, CMP ? 2 : 1) il_admm_kernel(const IlArgs<R> A, int it0, int it1,
+                                                                      int skip_cmp) {
+  constexpr int RPW = (NB + NW - 1) / NW;  // stage rows per warp
+  constexpr int NT = 32 * NW;
   constexpr int V = 16 / sizeof(R);
   constexpr int L32 = kWarp;
   extern __shared__ __align__(16) unsigned char il_smem[];
@@ -478,14 +529,20 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   const int grp = blockIdx.x;
   const int b = grp * kWarp + lane;
   const int T = A.T, N = T - 1, n = EX ? NB : A.n, nx = A.nx, n0 = A.n0, m = A.m;
+  {
+    const bool cg = il_group_compact(A.apid, A.gsel, A.wrow, grp, nx, m);
+    if (CMP ? !cg : (skip_cmp && cg)) return;  // the other variant runs this group
+  }
   const bool act = b < A.Nb && A.act[b] != 0;
   if (!__syncthreads_or(act)) return;  // every problem of the group has converged
   const IlSizes z(T, n, nx, n0, m);
   const int trin = (int)tri(n), nn = n * n, woff = T * trin;
   const R rho = A.rho[b], rf = rho * A.rff, al = A.alpha, sw = A.sw[b], sigma = A.sigma;
   const bool slack = A.use_slack != 0;
-  const bool apI = A.apid[grp] != 0;  // A+_t = [-I 0] for the whole group
-  const bool gS = A.gsel[grp] != 0;   // G_t[k] = e_{gc[k]} for the whole group
+  const bool apI = CMP || A.apid[grp] != 0;        // A+_t = [-I 0] for the whole group
+  const bool gS = CMP || A.gsel[grp] != 0;         // G_t[k] = e_{gc[k]} for the whole group
+  const int wr = CMP ? nx : A.wrow[grp];           // rows of W_t that are not exact zeros: nx or n
+  const int wcap = CMP ? nx : n;                   // W rows the stage buffer holds
   const int* gc = A.gcol + (size_t)grp * (m > 0 ? m : 1);
   // group bases of the interleaved arrays (element e of this group: base[e * 32 + lane])
   auto gb = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp; };
@@ -508,7 +565,7 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   R* const C0l = n0 > 0 ? gb(A.c0, z.c0) + lane : nullptr;
   R* const YF0l = n0 > 0 ? gb(A.yf0, z.yf0) + lane : nullptr;
   R* sm = reinterpret_cast<R*>(il_smem);
-  const int SA = il_fwd_elems(n), SB = il_buf_b_elems(n, nx, m);
+  const int SA = il_buf_a_elems(n, nx, CMP), SB = il_buf_b_elems(n, nx, m, CMP);
   R* BA = sm;
   R* BB = sm + SA * L32;
   R* ush = BB + SB * L32;
@@ -520,20 +577,22 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   // copy `elems` interleaved elements (contiguous from src) to dst, 16 bytes per cp.async
   auto copy = [&](R* dst, const R* src, int elems) {
     const int chunks = elems * (L32 / V);
-    for (int c = threadIdx.x; c < chunks; c += kIlThreads) cp_async16(dst + c * V, src + c * V);
+    for (int c = threadIdx.x; c < chunks; c += NT) cp_async16(dst + c * V, src + c * V);
   };
-  // buffer B (backward) offsets
-  const int oAm = 0, oAp = nx * n, oG = 2 * nx * n, oq = oG + m * n, oc = oq + n, ox = oc + nx, oyf = ox + n,
-            ozg = oyf + nx, oyg = ozg + m, ol = oyg + m, ou = ol + m;
+  // stage buffer A / forward buffers: L_t^-1 (packed), W rows, then the vector
+  const int ovec = trin + wcap * n;
+  // buffer B (backward) offsets; the compact layout has no A+ and no G
+  const int oAm = 0, oAp = CMP ? 0 : nx * n, oG = CMP ? nx * n : 2 * nx * n, oq = oG + (CMP ? 0 : m * n),
+            oc = oq + n, ox = oc + nx, oyf = ox + n, ozg = oyf + nx, oyg = ozg + m, ol = oyg + m, ou = ol + m;
   auto fetch_fwd = [&](R* dst, int t) {
     copy(dst, F + (size_t)t * trin * L32, trin);
-    if (t > 0) copy(dst + trin * L32, F + ((size_t)woff + (size_t)(t - 1) * nn) * L32, nn);
-    copy(dst + (trin + nn) * L32, GAM + (size_t)t * n * L32, n);
+    if (t > 0) copy(dst + trin * L32, F + ((size_t)woff + (size_t)(t - 1) * nn) * L32, wr * n);
+    copy(dst + ovec * L32, GAM + (size_t)t * n * L32, n);
   };
   auto fetch_bwd_a = [&](int t) {
     copy(BA, F + (size_t)t * trin * L32, trin);
-    if (t < N) copy(BA + trin * L32, F + ((size_t)woff + (size_t)t * nn) * L32, nn);
-    copy(BA + (trin + nn) * L32, YS + (size_t)t * n * L32, n);
+    if (t < N) copy(BA + trin * L32, F + ((size_t)woff + (size_t)t * nn) * L32, wr * n);
+    copy(BA + ovec * L32, YS + (size_t)t * n * L32, n);
   };
   auto fetch_bwd_b = [&](int t) {
     if (t < N) {
@@ -566,8 +625,6 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
   R* const YFDl = YFD + lane;
   R* const ZGl = m > 0 ? ZG + lane : nullptr;
   R* const YGl = m > 0 ? YG + lane : nullptr;
-  const int i = w;  // the stage row / column this warp owns (NB <= NW)
-  const bool own = i < n;
 
   for (int it = it0; it < it1; ++it) {
     // ---------------- forward sweep: y_t = L_t^-1 (gamma_t - W_{t-1} y_{t-1})
@@ -579,19 +636,32 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
       R* bufl = ((t & 1) ? BB : BA) + lane;
       cp_async_wait<1>();
       __syncthreads();
-      if (own) {
-        R u = bufl[(trin + nn + i) * L32];
-        if (t > 0) u -= il_dot<NB>(bufl + (trin + i * n) * L32, L32, xs0l, n);
-        ushl[i * L32] = u;
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        if (i < n) {
+          R u = bufl[(ovec + i) * L32];
+          if (t > 0 && i < wr) u -= il_dot<NB>(bufl + (trin + i * n) * L32, L32, xs0l, n);
+          ushl[i * L32] = u;
+        }
       }
       __syncthreads();
-      R y = R(0);
-      if (own) {
-        y = il_dot<NB>(bufl + (i * (i + 1) / 2) * L32, L32, ushl, i + 1);
-        if (act) YSl[(t * n + i) * L32] = y;
+      R y[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        y[r] = R(0);
+        if (i < n) {
+          y[r] = il_dot<NB>(bufl + (i * (i + 1) / 2) * L32, L32, ushl, i + 1);
+          if (act) YSl[(t * n + i) * L32] = y[r];
+        }
       }
       __syncthreads();  // every read of this stage's buffer, ush and xs0 is done
-      if (own) xs0l[i * L32] = y;
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        if (i < n) xs0l[i * L32] = y[r];
+      }
       if (t + 2 < T) fetch_fwd(bufl - lane, t + 2);
       cp_async_commit();
     }
@@ -601,7 +671,9 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
     // ---------------- backward sweep with the ADMM-level updates
     // x~_{t+1} in xs[(t + 1) & 1], x~_t into xs[t & 1]; the pieces of gamma_t
     // formed at step t wait in registers for the A+ terms of step t - 1.
-    R gval = R(0), geq = R(0), giq = R(0);
+    R gval[RPW], geq[RPW], giq[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) gval[r] = geq[r] = giq[r] = R(0);
     fetch_bwd_a(N);
     cp_async_commit();
     fetch_bwd_b(N);
@@ -611,20 +683,29 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
       R* xnl = (t & 1) ? xs0l : xs1l;  // x~_{t+1}
       cp_async_wait<1>();
       __syncthreads();
-      if (own) {
-        R u = BAl[(trin + nn + i) * L32];
-        if (t < N) u -= il_dot<NB>(BAl + (trin + i) * L32, n * L32, xnl, n);  // column i of W_t
-        ushl[i * L32] = u;
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        if (i < n) {
+          R u = BAl[(ovec + i) * L32];
+          if (t < N) u -= il_dot<NB>(BAl + (trin + i) * L32, n * L32, xnl, wr);  // column i of W_t (rows < wr)
+          ushl[i * L32] = u;
+        }
       }
       __syncthreads();
-      R xv = R(0);
-      if (own) {  // row i of L_t^-T: sum_{r >= i} Linv[r][i] u_r
-        R s[4] = {R(0), R(0), R(0), R(0)};
+      R xv[RPW];
 #pragma unroll
-        for (int r = 0; r < NB; ++r)
-          if (r >= i && r < n) s[r & 3] = fma(BAl[(r * (r + 1) / 2 + i) * L32], ushl[r * L32], s[r & 3]);
-        xv = (s[0] + s[1]) + (s[2] + s[3]);
-        xtl[i * L32] = xv;
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        xv[r] = R(0);
+        if (i < n) {  // row i of L_t^-T: sum_{r >= i} Linv[r][i] u_r
+          R s[4] = {R(0), R(0), R(0), R(0)};
+#pragma unroll
+          for (int k = 0; k < NB; ++k)
+            if (k >= i && k < n) s[k & 3] = fma(BAl[(k * (k + 1) / 2 + i) * L32], ushl[k * L32], s[k & 3]);
+          xv[r] = (s[0] + s[1]) + (s[2] + s[3]);
+          xtl[i * L32] = xv[r];
+        }
       }
       cp_async_wait<0>();
       __syncthreads();  // x~_t complete, buffer B of stage t landed, buffer A consumed
@@ -675,42 +756,52 @@ __global__ void __launch_bounds__(kIlThreads, 1) il_admm_kernel(const IlArgs<R> 
           ct0vl[k * L32] = rf * c0 - y;
         }
       }
-      R xr = R(0);
-      if (own) {  // relaxation of x_t
-        xr = al * xv + (R(1) - al) * BBl[(ox + i) * L32];
-        if (act) X[(t * n + i) * L32] = xr;
+      R xr[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        xr[r] = R(0);
+        if (i < n) {  // relaxation of x_t
+          xr[r] = al * xv[r] + (R(1) - al) * BBl[(ox + i) * L32];
+          if (act) X[(t * n + i) * L32] = xr[r];
+        }
       }
       __syncthreads();  // ctv, gtv, ct0v complete
-      if (own) {  // gamma for the next iteration (column i)
-        if (t < N) {  // the A+ terms of the dynamics rows of stage t complete gamma_{t+1}
-          const R ap = apI ? (i < nx ? -ctvl[i * L32] : R(0)) : il_dot<NB>(BBl + (oAp + i) * L32, n * L32, ctvl, nx);
-          if (act) GAMl[((t + 1) * n + i) * L32] = (gval + (ap + geq)) + giq;
-        }
-        const R val = sigma * xr - BBl[(oq + i) * L32];
-        R eq = R(0);
-        if (t == 0) {
-          for (int k = 0; k < n0; ++k) eq += A0l[(k * n + i) * L32] * ct0vl[k * L32];
-        }
-        if (t < N) {
-          if (t == 0) {
-            for (int k = 0; k < nx; ++k) eq += BBl[(oAm + k * n + i) * L32] * ctvl[k * L32];
-          } else {
-            eq = il_dot<NB>(BBl + (oAm + i) * L32, n * L32, ctvl, nx);
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int i = w + r * NW;
+        if (i < n) {  // gamma for the next iteration (column i)
+          if (t < N) {  // the A+ terms of the dynamics rows of stage t complete gamma_{t+1}
+            const R ap =
+                apI ? (i < nx ? -ctvl[i * L32] : R(0)) : il_dot<NB>(BBl + (oAp + i) * L32, n * L32, ctvl, nx);
+            if (act) GAMl[((t + 1) * n + i) * L32] = (gval[r] + (ap + geq[r])) + giq[r];
           }
-        }
-        R iq = R(0);
-        if (gS) {
-          for (int k = 0; k < m; ++k)
-            if (gc[k] == i) iq += gtvl[k * L32];
-        } else {
-          for (int k = 0; k < m; ++k) iq += BBl[(oG + k * n + i) * L32] * gtvl[k * L32];
-        }
-        if (t == 0) {
-          if (act) GAMl[i * L32] = (val + eq) + iq;
-        } else {
-          gval = val;
-          geq = eq;
-          giq = iq;
+          const R val = sigma * xr[r] - BBl[(oq + i) * L32];
+          R eq = R(0);
+          if (t == 0) {
+            for (int k = 0; k < n0; ++k) eq += A0l[(k * n + i) * L32] * ct0vl[k * L32];
+          }
+          if (t < N) {
+            if (t == 0) {
+              for (int k = 0; k < nx; ++k) eq += BBl[(oAm + k * n + i) * L32] * ctvl[k * L32];
+            } else {
+              eq = il_dot<NB>(BBl + (oAm + i) * L32, n * L32, ctvl, nx);
+            }
+          }
+          R iq = R(0);
+          if (gS) {
+            for (int k = 0; k < m; ++k)
+              if (gc[k] == i) iq += gtvl[k * L32];
+          } else {
+            for (int k = 0; k < m; ++k) iq += BBl[(oG + k * n + i) * L32] * gtvl[k * L32];
+          }
+          if (t == 0) {
+            if (act) GAMl[i * L32] = (val + eq) + iq;
+          } else {
+            gval[r] = val;
+            geq[r] = eq;
+            giq[r] = iq;
+          }
         }
       }
       __syncthreads();  // buffer B, ctv, gtv consumed
@@ -816,7 +907,7 @@ __global__ void il_scalars_out_kernel(IlArgs<R> A, R* rho_out, uint32_t* iters_o
 template <int NB, typename R>
 bool il_fits(const TmpcDims& d) {
   if (d.n > max_nb<R>() || d.Nb <= 0 || !grid_ok(d.Nb, op_elems(d.T, d.n))) return false;
-  if ((long)il_admm_smem<NB, R>(d.n, d.nx, d.n0, d.m) > max_dyn_smem()) return false;
+  if ((long)il_admm_smem<NB, R>(d.n, d.nx, d.n0, d.m, false) > max_dyn_smem()) return false;
   if ((long)il_check_smem<NB, R>(d.T, d.nx, d.n0, d.m) > max_dyn_smem()) return false;
   return (long)staged_smem_elems<R>(d.n, false) * (long)sizeof(R) <= max_dyn_smem();
 }
@@ -925,10 +1016,18 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   if (rc) return rc;
   return il_dispatch<R>(n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;
-    const size_t smem = il_admm_smem<NB, R>(n, nx, n0, m);
+    const size_t smem = il_admm_smem<NB, R>(n, nx, n0, m, false);
     const size_t csmem = il_check_smem<NB, R>(T, nx, n0, m);
-    auto kadmm = n == NB ? il_admm_kernel<NB, R, true> : il_admm_kernel<NB, R, false>;
+    auto kadmm = n == NB ? il_admm_kernel<NB, R, true, kIlWarps, false> : il_admm_kernel<NB, R, false, kIlWarps, false>;
     chk((int)cudaFuncSetAttribute(kadmm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // fp32: the groups with the compact structure run in the compact variant
+    // (two blocks per SM) when two of its blocks fit one SM's shared memory
+    const size_t csm = il_admm_smem<NB, R>(n, nx, n0, m, true);
+    void (*kcmp)(const IlArgs<R>, int, int, int) = nullptr;
+    if constexpr (sizeof(R) == 4)
+      kcmp = n == NB ? il_admm_kernel<NB, R, true, kIlCmpWarps, true> : il_admm_kernel<NB, R, false, kIlCmpWarps, true>;
+    const bool use_cmp = kcmp != nullptr && nx < n && (long)(2 * (csm + 1024)) <= max_sm_smem();
+    if (use_cmp) chk((int)cudaFuncSetAttribute(kcmp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm));
     chk((int)cudaFuncSetAttribute(il_check_kernel<NB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem));
     if (rc) return rc;
     const dim3 ggrid((unsigned)groups(Nb), (unsigned)T);
@@ -938,6 +1037,8 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
       il_assemble_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, P.qp, gate);
       chk((int)cudaPeekAtLastError());
       chk(launch_factor<NB, R>(Nb, T, n, A.ops, A.ops, A.fstat, gate, st));
+      il_w_rows_kernel<R><<<(unsigned)groups(Nb), kWrowThreads, 0, st>>>(A, gate);
+      chk((int)cudaPeekAtLastError());
       il_gamma_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, gate, gate ? 1 : 0);
       chk((int)cudaPeekAtLastError());
       if (gate) {
@@ -947,7 +1048,11 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
     };
     auto iterate = [&](int a, int e) {
       if (e <= a) return;
-      kadmm<<<(unsigned)groups(Nb), kIlThreads, smem, st>>>(A, a, e);
+      if (use_cmp) {
+        kcmp<<<(unsigned)groups(Nb), 32 * kIlCmpWarps, csm, st>>>(A, a, e, 0);
+        chk((int)cudaPeekAtLastError());
+      }
+      kadmm<<<(unsigned)groups(Nb), kIlThreads, smem, st>>>(A, a, e, use_cmp ? 1 : 0);
       chk((int)cudaPeekAtLastError());
     };
     build(nullptr);

@@ -20,6 +20,13 @@ int max_dyn_smem() {
   return v;
 }
 
+int max_sm_smem() {
+  int dev = 0, v = 100 * 1024;
+  if (cudaGetDevice(&dev) != cudaSuccess) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess) v = 100 * 1024;
+  return v;
+}
+
 }  // namespace tmpc
 
 extern "C" {

@@ -206,6 +206,7 @@ __device__ __forceinline__ QPView<R> qp_view(const TmpcQP& qp, int b, int T, int
 
 int check_dims(const TmpcDims* d);  // capi.cu
 int max_dyn_smem();                 // capi.cu: opt-in shared memory per block of the current device
+int max_sm_smem();                  // capi.cu: shared memory per SM of the current device
 
 // Calls f(std::integral_constant<int, NB>) for the compiled block size of n.
 template <typename F>
