@@ -168,27 +168,27 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
 // ---------------------------------------------------------------------------
 // Structure of A+: the explicit integrators give A+_t = [-I 0] for every
 // stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One warp
-// per group checks its 32 problems' interleaved A+ exactly; where every one
-// matches, the iteration kernel forms A+ x and A+^T y from the identity
-// (bit-identical: the products with the exact -1 and 0 entries are exact)
-// and does not stream A+ each iteration.
+// per group checks its 32 problems' A+ exactly, in the caller's problem-major
+// array, before any layout conversion; where every one matches, A+ is not
+// converted to the interleaved layout and the assembly, the first gamma and
+// the iteration kernel form its products from the identity (bit-identical:
+// the products with the exact -1 and 0 entries are exact).
 // ---------------------------------------------------------------------------
 template <typename R>
-__global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
+__global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A, const R* __restrict__ ap_pm) {
   // one warp per (group, stage): lane l checks A+_t of problem 32 grp + l;
   // apid[grp] was set to 1 by il_scalars_in_kernel and is cleared on a mismatch
   const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
   const int b = grp * kWarp + lane;
-  const IlSizes z(A.T, A.n, A.nx, A.n0, A.m);
-  const int n = A.n, nx = A.nx;
+  const int n = A.n, nx = A.nx, N = A.T - 1;
   bool ok = true;
   if (b < A.Nb) {
-    const R* p = A.ap + ((size_t)grp * z.am + (size_t)t * nx * n) * kWarp + lane;
+    const R* p = ap_pm + ((size_t)b * N + t) * nx * n;  // a contiguous run of nx n values per lane
     int bad = 0;  // no short-circuit: the loads stay independent
 #pragma unroll 8
     for (int e = 0; e < nx * n; ++e) {
       const int k = e / n, j = e - k * n;
-      bad |= p[(size_t)e * kWarp] != (j == k ? R(-1) : R(0));
+      bad |= p[e] != (j == k ? R(-1) : R(0));
     }
     ok = bad == 0;
   }
@@ -200,31 +200,32 @@ __global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A) {
 // bounds) make every inequality row a unit vector, G_t[k] = e_{c_k}, with the
 // same columns c_k in every stage.  One warp per group takes the columns from
 // its first problem's first stage and checks every row of its 32 problems
-// exactly; where all match, the iteration kernel forms G x and G^T y from the
-// columns (the same sums: the other terms are exact zeros) and does not stream
-// G each iteration.
+// exactly, in the caller's problem-major array; where all match, G is not
+// converted to the interleaved layout and the assembly, the first gamma and
+// the iteration kernel form G x and G^T y from the columns (the same sums:
+// the other terms are exact zeros).
 // ---------------------------------------------------------------------------
 template <typename R>
-__global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A) {
+__global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A, const R* __restrict__ g_pm) {
   // one warp per (group, stage); gsel[grp] was set to 1 by il_scalars_in_kernel
   // and is cleared on a mismatch
   const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
   const int b = grp * kWarp + lane;
-  const int n = A.n, m = A.m;
-  const IlSizes z(A.T, n, A.nx, A.n0, m);
-  const R* g = A.g + (size_t)grp * z.g * kWarp;  // group base: element e of lane l at g[e * 32 + l]
+  const int n = A.n, m = A.m, T = A.T;
+  const R* g0 = g_pm + (size_t)grp * kWarp * T * m * n;  // first problem of the group, stage 0
+  const R* gl = g_pm + ((size_t)b * T + t) * m * n;      // this lane's problem, stage t
   bool ok = true;
   for (int k = 0; k < m; ++k) {
     // column of the single 1 in row k of the group's first problem, first stage; -1 if none
     int c = -1;
     for (int j = 0; j < n; ++j)
-      if (g[(size_t)(k * n + j) * kWarp] == R(1)) c = j;
+      if (g0[k * n + j] == R(1)) c = j;
     if (t == 0 && lane == 0) A.gcol[(size_t)grp * m + k] = c;
     if (c < 0) ok = false;
     if (b < A.Nb && ok) {
       int bad = 0;
 #pragma unroll 8
-      for (int j = 0; j < n; ++j) bad |= g[((size_t)(t * m + k) * n + j) * kWarp + lane] != (j == c ? R(1) : R(0));
+      for (int j = 0; j < n; ++j) bad |= gl[k * n + j] != (j == c ? R(1) : R(0));
       ok = bad == 0;
     }
   }
@@ -310,6 +311,11 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
   const IlSizes z(T, n, nx, n0, m);
   const int trin = (int)tri(n);
   const R rho = A.rho[b], rf = rho * A.rff;
+  // A+_t = [-I 0] / unit inequality rows (detected per group): the rank-1
+  // terms of those rows are formed from the structure (the same values: every
+  // other product is an exact zero) and the rows are not read
+  const bool apI = A.apid[grp] != 0, gS = m > 0 && A.gsel[grp] != 0;
+  const int* gc = A.gcol + (size_t)grp * (m > 0 ? m : 1);
   auto lv = [&](R* p, size_t E) { return p + (size_t)grp * E * kWarp + lane; };
   R* O = lv(A.ops, z.ops);
   const R* Gl = m > 0 ? lv(A.g, z.g) : nullptr;
@@ -331,7 +337,16 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
   // ---- Theta_t: (D + sigma I) + rho_ineq G^T G
 #pragma unroll
   for (int e = 0; e < TR; ++e) acc[e] = R(0);
-  for (int k = 0; k < m; ++k) rank1(Gl + (size_t)(t * m + k) * n * kWarp);
+  if (gS) {
+    for (int k = 0; k < m; ++k) {
+      const int c = gc[k];
+#pragma unroll
+      for (int r = 0; r < NB; ++r)
+        if (r == c) acc[LI(r, r)] = fma(R(1), R(1), acc[LI(r, r)]);
+    }
+  } else {
+    for (int k = 0; k < m; ++k) rank1(Gl + (size_t)(t * m + k) * n * kWarp);
+  }
   // Theta's column c takes row c of D_t (D[c][r], r >= c): rows read whole, with
   // 128-bit loads where the rows are 16-byte aligned (a lane's row is one
   // contiguous run in the caller's problem-major array)
@@ -365,7 +380,13 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
     if (N > 0)
       for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)k * n * kWarp);
   } else {
-    for (int k = 0; k < nx; ++k) rank1(APl + (size_t)((t - 1) * nx + k) * n * kWarp);
+    if (apI) {
+#pragma unroll
+      for (int r = 0; r < NB; ++r)
+        if (r < nx) acc[LI(r, r)] = fma(R(-1), R(-1), acc[LI(r, r)]);
+    } else {
+      for (int k = 0; k < nx; ++k) rank1(APl + (size_t)((t - 1) * nx + k) * n * kWarp);
+    }
     if (t < N)
       for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)(t * nx + k) * n * kWarp);
   }
@@ -383,7 +404,16 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
   for (int h = 0; h < n; h += HB) {
 #pragma unroll
     for (int e = 0; e < HB * NB; ++e) acc[e] = R(0);
-    for (int k = 0; k < nx; ++k) {
+    if (apI) {  // A+^T A- has the rows -A-_t[k] (k < nx) and zero rows below
+#pragma unroll
+      for (int i = 0; i < HB; ++i)
+        if (h + i < nx) {
+          const R* am = AMl + (size_t)(t * nx + h + i) * n * kWarp;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) acc[i * NB + j] = fma(R(-1), j < n ? am[j * kWarp] : R(0), R(0));
+        }
+    }
+    for (int k = 0; k < (apI ? 0 : nx); ++k) {
       const R* ap = APl + (size_t)(t * nx + k) * n * kWarp;
       const R* am = AMl + (size_t)(t * nx + k) * n * kWarp;
       R x[HB], y[NB];
@@ -428,6 +458,9 @@ __global__ void __launch_bounds__(kWarp) il_gamma_kernel(IlArgs<R> A, const int*
   const int T = A.T, N = T - 1, n = A.n, nx = A.nx, n0 = A.n0, m = A.m;
   const IlSizes z(T, n, nx, n0, m);
   const R rho = A.rho[b], rf = rho * A.rff;
+  const int grp = blockIdx.x;
+  const bool apI = A.apid[grp] != 0, gS = m > 0 && A.gsel[grp] != 0;  // structure: rows not read
+  const int* gc = A.gcol + (size_t)grp * (m > 0 ? m : 1);
   // Row by row: each constraint row's values are read once and its target
   // (rho_f c - y_f, or rho z - y_g) multiplies the whole row into the NB
   // per-column sums, which see their terms in compute_gamma's order.
@@ -446,14 +479,28 @@ __global__ void __launch_bounds__(kWarp) il_gamma_kernel(IlArgs<R> A, const int*
     if (N > 0)
       for (int k = 0; k < nx; ++k) add_row(eq, A.am + (size_t)k * n * kWarp, z.am, ctd(k));
   } else {
-    for (int k = 0; k < nx; ++k)
-      add_row(eq, A.ap + (size_t)((t - 1) * nx + k) * n * kWarp, z.am, ctd((t - 1) * nx + k));
+    if (apI) {  // row k of A+ is -e_k: only column k takes its target
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+        if (j < nx) eq[j] += R(-1) * ctd((t - 1) * nx + j);
+    } else {
+      for (int k = 0; k < nx; ++k)
+        add_row(eq, A.ap + (size_t)((t - 1) * nx + k) * n * kWarp, z.am, ctd((t - 1) * nx + k));
+    }
     if (t < N)
       for (int k = 0; k < nx; ++k) add_row(eq, A.am + (size_t)(t * nx + k) * n * kWarp, z.am, ctd(t * nx + k));
   }
-  for (int k = 0; k < m; ++k)
-    add_row(iq, A.g + (size_t)(t * m + k) * n * kWarp, z.g,
-            rho * A.zg[ix(b, z.zm, (size_t)t * m + k)] - A.yg[ix(b, z.zm, (size_t)t * m + k)]);
+  for (int k = 0; k < m; ++k) {
+    const R tgt = rho * A.zg[ix(b, z.zm, (size_t)t * m + k)] - A.yg[ix(b, z.zm, (size_t)t * m + k)];
+    if (gS) {  // row k of G is e_{gc[k]}
+      const int c = gc[k];
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+        if (j == c) iq[j] += R(1) * tgt;
+    } else {
+      add_row(iq, A.g + (size_t)(t * m + k) * n * kWarp, z.g, tgt);
+    }
+  }
 #pragma unroll
   for (int j = 0; j < NB; ++j) {
     if (j < n) {
@@ -989,11 +1036,31 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   il_scalars_in_kernel<R><<<(G32 + 255) / 256, 256, 0, st>>>(A, static_cast<const R*>(P.in.rho_bar),
                                                              P.slack_weight, P.max_iter);
   chk((int)cudaPeekAtLastError());
+  // structure of A+ and G on the caller's arrays: groups where it holds
+  // convert neither (their rows are formed from the structure)
+  if (N > 0) {
+    il_ap_identity_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)N), kWarp, 0, st>>>(
+        A, static_cast<const R*>(P.qp.A_plus));
+    chk((int)cudaPeekAtLastError());
+  } else {
+    cudaMemsetAsync(A.apid, 0, groups(Nb) * sizeof(int), st);
+  }
+  if (m > 0) {
+    il_g_select_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)T), kWarp, 0, st>>>(A, static_cast<const R*>(P.qp.G));
+    chk((int)cudaPeekAtLastError());
+  } else {
+    cudaMemsetAsync(A.gsel, 0, groups(Nb) * sizeof(int), st);
+  }
+  if (rc) return rc;
+  auto inl_skip = [&](const void* src, R* dst, size_t E, const int* skip) {
+    if (E == 0 || src == nullptr) return;
+    chk(interleave<R>(Nb, E, E, static_cast<const R*>(src), dst, IdentityMap{}, st, skip));
+  };
   inl(P.qp.q, A.q, z.q);
   inl(P.qp.A0, A.a0, z.a0);
   inl(P.qp.A_minus, A.am, z.am);
-  inl(P.qp.A_plus, A.ap, z.am);
-  inl(P.qp.G, A.g, z.g);
+  inl_skip(P.qp.A_plus, A.ap, z.am, A.apid);
+  inl_skip(P.qp.G, A.g, z.g, A.gsel);
   inl(P.qp.c0, A.c0, z.c0);
   inl(P.qp.c, A.c, z.c);
   inl(P.qp.l, A.l, z.lu);
@@ -1004,15 +1071,6 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   inl(P.in.z_g, A.zg, z.zm);
   inl(P.in.y_g, A.yg, z.zm);
   inl(P.in.xi_g, A.xig, z.zm);
-  if (rc) return rc;
-  il_ap_identity_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)N), kWarp, 0, st>>>(A);
-  chk((int)cudaPeekAtLastError());
-  if (m > 0) {
-    il_g_select_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)T), kWarp, 0, st>>>(A);
-    chk((int)cudaPeekAtLastError());
-  } else {
-    cudaMemsetAsync(A.gsel, 0, groups(Nb) * sizeof(int), st);
-  }
   if (rc) return rc;
   return il_dispatch<R>(n, [&](auto tag) {
     constexpr int NB = decltype(tag)::value;

@@ -319,7 +319,8 @@ __global__ void __launch_bounds__(kWarp) factor_staged_kernel(const R* ops, R* f
 // ---------------------------------------------------------------------------
 // Layout conversion: [Nb][E] problem-major <-> interleaved, through a 32 x 32
 // shared-memory tile (coalesced on both sides).  With a gather map, element e
-// of the interleaved array takes the problem-major element src(e).
+// of the interleaved array takes the problem-major element src(e).  With
+// skip, groups whose skip flag is set are left unconverted.
 // ---------------------------------------------------------------------------
 struct IdentityMap {
   __device__ size_t operator()(size_t e) const { return e; }
@@ -353,9 +354,10 @@ constexpr int kConvTiles = 4;
 
 template <typename R, class Map>
 __global__ void __launch_bounds__(256) interleave_kernel(const R* __restrict__ in, R* out, int Nb, size_t E_in,
-                                                         size_t E, Map map) {
+                                                         size_t E, Map map, const int* skip) {
   __shared__ R tile[kConvTiles][32][33];
   const size_t grp = blockIdx.y;
+  if (skip && skip[grp]) return;
   const size_t e0 = (size_t)blockIdx.x * 32 * kConvTiles;
   const int tx = threadIdx.x, ty = threadIdx.y;
 #pragma unroll
@@ -403,13 +405,14 @@ inline bool grid_ok(int Nb, size_t E) {
 }
 
 template <typename R, class Map>
-int interleave(int Nb, size_t E_in, size_t E, const R* in, R* out, Map map, cudaStream_t st) {
+int interleave(int Nb, size_t E_in, size_t E, const R* in, R* out, Map map, cudaStream_t st,
+               const int* skip = nullptr) {
   if (Nb < 0) return TMPC_ERR_BAD_DIMS;
   if (Nb == 0 || E == 0) return TMPC_OK;
   if (!in || !out) return TMPC_ERR_NULL_ARG;
   if (!grid_ok(Nb, E)) return TMPC_ERR_BAD_DIMS;
   dim3 grid((unsigned)((E + 32 * kConvTiles - 1) / (32 * kConvTiles)), (unsigned)groups(Nb)), block(32, 8);
-  interleave_kernel<R, Map><<<grid, block, 0, st>>>(in, out, Nb, E_in, E, map);
+  interleave_kernel<R, Map><<<grid, block, 0, st>>>(in, out, Nb, E_in, E, map, skip);
   return (int)cudaPeekAtLastError();
 }
 
