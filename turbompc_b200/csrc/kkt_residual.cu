@@ -34,54 +34,64 @@ __global__ void __launch_bounds__(kKktThreads) kkt_residual_kernel(TmpcQP qpa, c
   const R* ygb = m > 0 ? yg + (size_t)b * T * m : nullptr;
   const R* sl = (use_slack && m > 0) ? slack + (size_t)b * T * m : nullptr;
   R stat = R(0), eq = R(0), ineq = R(0);
-  // stationarity, entry (t, j)
+  // stationarity, entry (t, j): each term's products in their own partial
+  // sum (independent FMA chains whose loads can be in flight together),
+  // added in the order of the formula
+  constexpr int V = 16 / sizeof(R);
+  const bool vec = n % V == 0 && (reinterpret_cast<uintptr_t>(qp.D) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(qp.E) & 15) == 0;
   for (int e = threadIdx.x; e < T * n; e += blockDim.x) {
     const int t = e / n, j = e - t * n;
     const R* xt = x + (size_t)t * n;
-    R s = qp.q[e];
+    R sd = R(0), se0 = R(0), se1 = R(0), s0 = R(0), sm = R(0), sp = R(0), sg = R(0);
     const R* Dt = qp.D + (size_t)t * n * n + (size_t)j * n;
+    const R* Em = t > 0 ? qp.E + (size_t)(t - 1) * n * n + (size_t)j * n : nullptr;  // E_{t-1}[j][:]
     // rows of D_t and E_{t-1} are contiguous per thread: 128-bit loads where aligned
-    constexpr int V = 16 / sizeof(R);
-    const bool vec = n % V == 0 && (reinterpret_cast<uintptr_t>(qp.D) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(qp.E) & 15) == 0;
     if (vec) {
+#pragma unroll 2
       for (int k = 0; k < n; k += V) {
         R w[V];
         ld128(w, Dt + k);
 #pragma unroll
-        for (int v = 0; v < V; ++v) s = fma(w[v], xt[k + v], s);
+        for (int v = 0; v < V; ++v) sd = fma(w[v], xt[k + v], sd);
       }
-    } else {
-      for (int k = 0; k < n; ++k) s = fma(Dt[k], xt[k], s);
-    }
-    if (t > 0) {
-      const R* Et = qp.E + (size_t)(t - 1) * n * n + (size_t)j * n;  // E_{t-1}[j][:]
-      if (vec) {
+      if (Em) {
+#pragma unroll 2
         for (int k = 0; k < n; k += V) {
           R w[V];
-          ld128(w, Et + k);
+          ld128(w, Em + k);
 #pragma unroll
-          for (int v = 0; v < V; ++v) s = fma(w[v], xt[k + v - n], s);
+          for (int v = 0; v < V; ++v) se0 = fma(w[v], xt[k + v - n], se0);
         }
-      } else {
-        for (int k = 0; k < n; ++k) s = fma(Et[k], xt[k - n], s);
+      }
+    } else {
+#pragma unroll 4
+      for (int k = 0; k < n; ++k) sd = fma(Dt[k], xt[k], sd);
+      if (Em) {
+#pragma unroll 4
+        for (int k = 0; k < n; ++k) se0 = fma(Em[k], xt[k - n], se0);
       }
     }
     if (t < N) {
       const R* Et = qp.E + (size_t)t * n * n;  // E_t[:][j]
-      for (int k = 0; k < n; ++k) s = fma(Et[(size_t)k * n + j], xt[n + k], s);
+#pragma unroll 4
+      for (int k = 0; k < n; ++k) se1 = fma(Et[(size_t)k * n + j], xt[n + k], se1);
     }
     if (t == 0)
-      for (int k = 0; k < n0; ++k) s = fma(qp.A0[(size_t)k * n + j], y0[k], s);
+      for (int k = 0; k < n0; ++k) s0 = fma(qp.A0[(size_t)k * n + j], y0[k], s0);
     if (t < N) {
       const R* am = qp.Am + (size_t)t * nx * n;
-      for (int k = 0; k < nx; ++k) s = fma(am[(size_t)k * n + j], yd[(size_t)t * nx + k], s);
+#pragma unroll 4
+      for (int k = 0; k < nx; ++k) sm = fma(am[(size_t)k * n + j], yd[(size_t)t * nx + k], sm);
     }
     if (t > 0) {
       const R* ap = qp.Ap + (size_t)(t - 1) * nx * n;
-      for (int k = 0; k < nx; ++k) s = fma(ap[(size_t)k * n + j], yd[(size_t)(t - 1) * nx + k], s);
+#pragma unroll 4
+      for (int k = 0; k < nx; ++k) sp = fma(ap[(size_t)k * n + j], yd[(size_t)(t - 1) * nx + k], sp);
     }
-    for (int k = 0; k < m; ++k) s = fma(qp.G[((size_t)t * m + k) * n + j], ygb[(size_t)t * m + k], s);
+#pragma unroll 4
+    for (int k = 0; k < m; ++k) sg = fma(qp.G[((size_t)t * m + k) * n + j], ygb[(size_t)t * m + k], sg);
+    const R s = (((((qp.q[e] + sd) + se0) + se1) + s0) + (sm + sp)) + sg;
     stat = fmax(stat, fabs(s));
   }
   // equality rows
@@ -94,9 +104,12 @@ __global__ void __launch_bounds__(kKktThreads) kkt_residual_kernel(TmpcQP qpa, c
       const int r = e - n0, t = r / nx, i = r - t * nx;
       const R* am = qp.Am + ((size_t)t * nx + i) * n;
       const R* ap = qp.Ap + ((size_t)t * nx + i) * n;
-      s = -qp.c[r];
-      for (int k = 0; k < n; ++k) s = fma(am[k], x[(size_t)t * n + k], s);
-      for (int k = 0; k < n; ++k) s = fma(ap[k], x[(size_t)(t + 1) * n + k], s);
+      R sa = R(0), sb = R(0);
+#pragma unroll 4
+      for (int k = 0; k < n; ++k) sa = fma(am[k], x[(size_t)t * n + k], sa);
+#pragma unroll 4
+      for (int k = 0; k < n; ++k) sb = fma(ap[k], x[(size_t)(t + 1) * n + k], sb);
+      s = (sa + sb) - qp.c[r];
     }
     eq = fmax(eq, fabs(s));
   }
@@ -105,6 +118,7 @@ __global__ void __launch_bounds__(kKktThreads) kkt_residual_kernel(TmpcQP qpa, c
     const int t = e / m;
     const R* gr = qp.G + (size_t)e * n;
     R s = R(0);
+#pragma unroll 4
     for (int k = 0; k < n; ++k) s = fma(gr[k], x[(size_t)t * n + k], s);
     const R gb = sl ? s + sl[e] : s;
     g_out[(size_t)b * T * m + e] = gb;
