@@ -352,6 +352,17 @@ int32_t tmpc_obstacle_rows_f32(const TmpcDims* dims, int32_t dim, int32_t n_obst
 int32_t tmpc_obstacle_rows_f64(const TmpcDims* dims, int32_t dim, int32_t n_obstacles, const double* states,
                                const double* centers, const double* radii, double row_scale, double* G, double* l,
                                double* u, tmpc_stream_t stream);
+/* Inequality rows at an iterate: g[b][t][k] = G_t[k] . z_t (+ slack[b][t][k]
+ * when slack is non-null), clamped to [l, u] when l and u are given (both or
+ * neither).  G [Nb][T][m][n], z [Nb][T][n], slack / l / u / g_out [Nb][T][m];
+ * dims->nx and dims->n0 are not used.
+ * Replaces the G z products of ADMM's initial state (z_g = clamp(G x, l, u),
+ * turbompc/solvers/admm/admm.py:1051-1088) and of the SQP loop's active-set
+ * identification (turbompc/solvers/turbompc_solver.py:1387-1439). */
+int32_t tmpc_ineq_rows_f32(const TmpcDims* dims, const float* G, const float* z, const float* slack, const float* l,
+                           const float* u, float* g_out, tmpc_stream_t stream);
+int32_t tmpc_ineq_rows_f64(const TmpcDims* dims, const double* G, const double* z, const double* slack,
+                           const double* l, const double* u, double* g_out, tmpc_stream_t stream);
 /* A learned stage cost s * w2 . tanh(W1 z + b1) (z = [x, u], every stage)
  * quadratised exactly and added in place to the cost blocks (the
  * stage-separable case of get_cost_linearized_blocks,

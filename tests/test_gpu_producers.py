@@ -65,3 +65,21 @@ def test_repeated_learned_cost_solves_are_identical():
     for _ in range(3):
         again = s.solve(g, p)
         assert torch.equal(again.controls, first.controls) and torch.equal(again.states, first.states)
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_ineq_rows_kernel_matches_torch(dtype):
+    """tmpc_ineq_rows_*: G z, G z + slack and clamp(G z, l, u) against the
+    PyTorch products (the solver's active-set g and ADMM's initial z_g)."""
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    Nb, T, m, n = 45, 11, 5, 13
+    G = torch.randn(Nb, T, m, n, generator=gen, device="cuda", dtype=dtype)
+    z = torch.randn(Nb, T, n, generator=gen, device="cuda", dtype=dtype)
+    s = torch.randn(Nb, T, m, generator=gen, device="cuda", dtype=dtype)
+    lo = -torch.rand(Nb, T, m, generator=gen, device="cuda", dtype=dtype)
+    hi = torch.rand(Nb, T, m, generator=gen, device="cuda", dtype=dtype)
+    ref = torch.einsum("btki,bti->btk", G.double(), z.double())
+    assert rel_err(ops.ineq_rows(G, z).cpu().numpy(), ref.cpu().numpy()) < TOL[dtype]
+    assert rel_err(ops.ineq_rows(G, z, s).cpu().numpy(), (ref + s.double()).cpu().numpy()) < TOL[dtype]
+    cl = torch.minimum(torch.maximum(ref, lo.double()), hi.double())
+    assert rel_err(ops.ineq_rows(G, z, lo=lo, hi=hi).cpu().numpy(), cl.cpu().numpy()) < TOL[dtype]

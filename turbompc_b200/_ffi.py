@@ -68,6 +68,7 @@ _SIGS["tmpc_adjoint_kkt_workspace_bytes"] = (C.c_size_t, [C.POINTER(TmpcDims), C
 for _s in ("f32", "f64"):
     _SIGS[f"tmpc_obstacle_rows_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, C.c_int32, _P, _P, _P,
                                                      C.c_double, _P, _P, _P, _P])
+    _SIGS[f"tmpc_ineq_rows_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), _P, _P, _P, _P, _P, _P, _P])
     _SIGS[f"tmpc_mlp_cost_blocks_{_s}"] = (C.c_int32, [C.POINTER(TmpcDims), C.c_int32, _P, _P, _P, _P, _P,
                                                        C.c_double, _P, _P, _P])
     _SIGS[f"tmpc_interleave_{_s}"] = (C.c_int32, [C.c_int32, C.c_int64, _P, _P, _P])

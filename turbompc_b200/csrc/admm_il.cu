@@ -167,69 +167,76 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
 
 // ---------------------------------------------------------------------------
 // Structure of A+: the explicit integrators give A+_t = [-I 0] for every
-// stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One warp
-// per group checks its 32 problems' A+ exactly, in the caller's problem-major
-// array, before any layout conversion; where every one matches, A+ is not
+// stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One
+// coalesced pass over the caller's problem-major array checks every problem's
+// A+ exactly, before any layout conversion; where all 32 problems of a group
+// match, the group's A+ is not
 // converted to the interleaved layout and the assembly, the first gamma and
 // the iteration kernel form its products from the identity (bit-identical:
 // the products with the exact -1 and 0 entries are exact).
 // ---------------------------------------------------------------------------
+constexpr int kFlatThreads = 256;
+inline unsigned flat_blocks(size_t elems) {
+  const size_t b = (elems + kFlatThreads - 1) / kFlatThreads;
+  return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
 template <typename R>
-__global__ void __launch_bounds__(kWarp) il_ap_identity_kernel(IlArgs<R> A, const R* __restrict__ ap_pm) {
-  // one warp per (group, stage): lane l checks A+_t of problem 32 grp + l;
-  // apid[grp] was set to 1 by il_scalars_in_kernel and is cleared on a mismatch
-  const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
-  const int b = grp * kWarp + lane;
-  const int n = A.n, nx = A.nx, N = A.T - 1;
-  bool ok = true;
-  if (b < A.Nb) {
-    const R* p = ap_pm + ((size_t)b * N + t) * nx * n;  // a contiguous run of nx n values per lane
-    int bad = 0;  // no short-circuit: the loads stay independent
-#pragma unroll 8
-    for (int e = 0; e < nx * n; ++e) {
-      const int k = e / n, j = e - k * n;
-      bad |= p[e] != (j == k ? R(-1) : R(0));
-    }
-    ok = bad == 0;
+__global__ void __launch_bounds__(kFlatThreads) il_ap_identity_kernel(IlArgs<R> A, const R* __restrict__ ap_pm) {
+  // one pass over the whole problem-major array (coalesced, grid-stride):
+  // apid[grp] was set to 1 by il_scalars_in_kernel and is cleared (plain
+  // stores of 0) where any entry of the group's problems differs
+  const int n = A.n, nx = A.nx;
+  const size_t per_stage = (size_t)nx * n, per_prob = (size_t)(A.T - 1) * per_stage;
+  const size_t total = per_prob * (size_t)A.Nb;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t b = e / per_prob, s = (e - b * per_prob) % per_stage;
+    const int k = (int)(s / n), j = (int)(s - (size_t)k * n);
+    if (ap_pm[e] != (j == k ? R(-1) : R(0))) A.apid[b / kWarp] = 0;
   }
-  if (!__all_sync(0xffffffffu, ok) && lane == 0) A.apid[grp] = 0;
 }
 
 // ---------------------------------------------------------------------------
 // Structure of G: box constraints on single variables (the quadrotor's thrust
 // bounds) make every inequality row a unit vector, G_t[k] = e_{c_k}, with the
-// same columns c_k in every stage.  One warp per group takes the columns from
-// its first problem's first stage and checks every row of its 32 problems
-// exactly, in the caller's problem-major array; where all match, G is not
+// same columns c_k in every stage.  One thread per (group, row) takes the
+// columns from the group's first problem's first stage, then one coalesced
+// pass over the caller's problem-major array checks every row exactly; where
+// all 32 problems of a group match, the group's G is not
 // converted to the interleaved layout and the assembly, the first gamma and
 // the iteration kernel form G x and G^T y from the columns (the same sums:
 // the other terms are exact zeros).
 // ---------------------------------------------------------------------------
 template <typename R>
-__global__ void __launch_bounds__(kWarp) il_g_select_kernel(IlArgs<R> A, const R* __restrict__ g_pm) {
-  // one warp per (group, stage); gsel[grp] was set to 1 by il_scalars_in_kernel
-  // and is cleared on a mismatch
-  const int lane = threadIdx.x, grp = blockIdx.x, t = blockIdx.y;
-  const int b = grp * kWarp + lane;
-  const int n = A.n, m = A.m, T = A.T;
-  const R* g0 = g_pm + (size_t)grp * kWarp * T * m * n;  // first problem of the group, stage 0
-  const R* gl = g_pm + ((size_t)b * T + t) * m * n;      // this lane's problem, stage t
-  bool ok = true;
-  for (int k = 0; k < m; ++k) {
-    // column of the single 1 in row k of the group's first problem, first stage; -1 if none
-    int c = -1;
-    for (int j = 0; j < n; ++j)
-      if (g0[k * n + j] == R(1)) c = j;
-    if (t == 0 && lane == 0) A.gcol[(size_t)grp * m + k] = c;
-    if (c < 0) ok = false;
-    if (b < A.Nb && ok) {
-      int bad = 0;
-#pragma unroll 8
-      for (int j = 0; j < n; ++j) bad |= gl[k * n + j] != (j == c ? R(1) : R(0));
-      ok = bad == 0;
-    }
+__global__ void __launch_bounds__(kFlatThreads) il_g_columns_kernel(IlArgs<R> A, const R* __restrict__ g_pm) {
+  // thread per (group, row k): the column of the single 1 in row k of the
+  // group's first problem, first stage (the last 1 of the row; -1 if none)
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = A.m, n = A.n;
+  if (i >= (int)groups(A.Nb) * m) return;
+  const int grp = i / m, k = i - grp * m;
+  const R* row = g_pm + (size_t)grp * kWarp * A.T * m * n + (size_t)k * n;
+  int c = -1;
+  for (int j = 0; j < n; ++j)
+    if (row[j] == R(1)) c = j;
+  A.gcol[i] = c;
+  if (c < 0) A.gsel[grp] = 0;
+}
+
+template <typename R>
+__global__ void __launch_bounds__(kFlatThreads) il_g_select_kernel(IlArgs<R> A, const R* __restrict__ g_pm) {
+  // one pass over the whole problem-major array (coalesced, grid-stride):
+  // every row k of every stage must equal e_{gcol[k]}; gsel[grp] is cleared
+  // (plain stores of 0) where any entry of the group's problems differs
+  const int n = A.n, m = A.m;
+  const size_t per_stage = (size_t)m * n, per_prob = (size_t)A.T * per_stage;
+  const size_t total = per_prob * (size_t)A.Nb;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t b = e / per_prob, s = (e - b * per_prob) % per_stage;
+    const int k = (int)(s / n), j = (int)(s - (size_t)k * n);
+    const size_t grp = b / kWarp;
+    if (g_pm[e] != (j == A.gcol[grp * m + k] ? R(1) : R(0))) A.gsel[grp] = 0;
   }
-  if (!__all_sync(0xffffffffu, ok) && lane == 0) A.gsel[grp] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -1039,14 +1046,16 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   // structure of A+ and G on the caller's arrays: groups where it holds
   // convert neither (their rows are formed from the structure)
   if (N > 0) {
-    il_ap_identity_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)N), kWarp, 0, st>>>(
+    il_ap_identity_kernel<R><<<flat_blocks((size_t)Nb * N * nx * n), kFlatThreads, 0, st>>>(
         A, static_cast<const R*>(P.qp.A_plus));
     chk((int)cudaPeekAtLastError());
   } else {
     cudaMemsetAsync(A.apid, 0, groups(Nb) * sizeof(int), st);
   }
   if (m > 0) {
-    il_g_select_kernel<R><<<dim3((unsigned)groups(Nb), (unsigned)T), kWarp, 0, st>>>(A, static_cast<const R*>(P.qp.G));
+    il_g_columns_kernel<R><<<(unsigned)((groups(Nb) * m + kFlatThreads - 1) / kFlatThreads), kFlatThreads, 0, st>>>(
+        A, static_cast<const R*>(P.qp.G));
+    il_g_select_kernel<R><<<flat_blocks((size_t)Nb * T * m * n), kFlatThreads, 0, st>>>(A, static_cast<const R*>(P.qp.G));
     chk((int)cudaPeekAtLastError());
   } else {
     cudaMemsetAsync(A.gsel, 0, groups(Nb) * sizeof(int), st);

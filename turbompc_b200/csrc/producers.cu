@@ -17,7 +17,10 @@
 //        grad = s W1^T (w2 * d),   H = s W1^T diag(w2 * (-2 th d)) W1
 //        D_t += H,   q_t += grad - H z
 //    (get_cost_linearized_blocks, optimal_control_problem.py:1068-1174, for a
-//    stage-separable cost: q = gradient - Hessian z).
+//    stage-separable cost: q = gradient - Hessian z);
+//  * the inequality rows at an iterate, g_t = G_t z_t (+ slack), optionally
+//    clamped to [l, u] (the initial z_g of admm.py:1051-1088, and the g of
+//    the SQP's active-set identification, turbompc_solver.py:1387-1439).
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -179,6 +182,37 @@ int mlp_cost_blocks(const TmpcDims* d, int H, const R* states, const R* controls
   return launch(mlp_kernel<16, R>);
 }
 
+// Thread per inequality row (problem, stage, row): the row's n entries
+// against the stage's n values of z (two contiguous runs per thread).
+template <typename R>
+__global__ void __launch_bounds__(256) ineq_rows_kernel(const R* __restrict__ G, const R* __restrict__ z,
+                                                       const R* __restrict__ slack, const R* __restrict__ lo,
+                                                       const R* __restrict__ hi, R* out, size_t rows, int m,
+                                                       int n) {
+  const size_t r = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const R* g = G + r * n;
+  const R* x = z + (r / m) * n;
+  R s = R(0);
+#pragma unroll 4
+  for (int k = 0; k < n; ++k) s = fma(g[k], x[k], s);
+  if (slack) s += slack[r];
+  if (lo) s = fmin(fmax(s, lo[r]), hi[r]);
+  out[r] = s;
+}
+
+template <typename R>
+int ineq_rows(const TmpcDims* d, const R* G, const R* z, const R* slack, const R* lo, const R* hi, R* out,
+              cudaStream_t st) {
+  if (!d) return TMPC_ERR_NULL_ARG;
+  if (d->Nb < 0 || d->T < 1 || d->n < 1 || d->m < 0) return TMPC_ERR_BAD_DIMS;  // nx, n0 unused
+  const size_t rows = (size_t)d->Nb * d->T * d->m;
+  if (rows == 0) return TMPC_OK;
+  if (!G || !z || !out || (lo == nullptr) != (hi == nullptr)) return TMPC_ERR_NULL_ARG;
+  ineq_rows_kernel<R><<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(G, z, slack, lo, hi, out, rows, d->m, d->n);
+  return (int)cudaPeekAtLastError();
+}
+
 }  // namespace prod
 }  // namespace tmpc
 
@@ -207,6 +241,14 @@ int32_t tmpc_mlp_cost_blocks_f64(const TmpcDims* dims, int32_t hidden, const dou
                                  double scale, double* D, double* q, tmpc_stream_t stream) {
   return tmpc::prod::mlp_cost_blocks<double>(dims, hidden, states, controls, W1, b1, w2, scale, D, q,
                                              (cudaStream_t)stream);
+}
+int32_t tmpc_ineq_rows_f32(const TmpcDims* dims, const float* G, const float* z, const float* slack, const float* l,
+                           const float* u, float* g_out, tmpc_stream_t stream) {
+  return tmpc::prod::ineq_rows<float>(dims, G, z, slack, l, u, g_out, (cudaStream_t)stream);
+}
+int32_t tmpc_ineq_rows_f64(const TmpcDims* dims, const double* G, const double* z, const double* slack,
+                           const double* l, const double* u, double* g_out, tmpc_stream_t stream) {
+  return tmpc::prod::ineq_rows<double>(dims, G, z, slack, l, u, g_out, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -247,7 +247,12 @@ def admm_initial_state(qp: QPData, rho_bar, x0: Optional[torch.Tensor] = None) -
     """admm.py:1051-1088: x = 0 (or x0), z_g = clamp(G x, l, u), duals zero."""
     B, T, n, m = qp.Nb, qp.T, qp.n, qp.m
     x = torch.zeros(B, T, n, dtype=qp.dtype, device=qp.device) if x0 is None else x0.clone().contiguous()
-    z = torch.minimum(torch.maximum(torch.einsum("btmn,btn->btm", qp.ineq.G, x), qp.ineq.l), qp.ineq.u)
+    if x0 is None:  # G 0 = 0
+        z = torch.minimum(torch.maximum(torch.zeros_like(qp.ineq.l), qp.ineq.l), qp.ineq.u)
+    elif x.is_cuda:
+        z = ineq_rows(qp.ineq.G, x, lo=qp.ineq.l, hi=qp.ineq.u)
+    else:
+        z = torch.minimum(torch.maximum(torch.einsum("btmn,btn->btm", qp.ineq.G, x), qp.ineq.l), qp.ineq.u)
     return ADMMState(x, torch.zeros_like(z), torch.zeros_like(qp.eq.c0), torch.zeros_like(qp.eq.c),
                      z.contiguous(), torch.zeros_like(z), _rho_vec(rho_bar, qp).clone())
 
@@ -444,6 +449,25 @@ def obstacle_rows(states: torch.Tensor, centers: torch.Tensor, radii: torch.Tens
                                         _ptr(rr, dt, dev), float(row_scale), _ptr(G), _ptr(lo), _ptr(hi),
                                         _stream(dev)))
     return G, lo, hi
+
+
+def ineq_rows(G: torch.Tensor, z: torch.Tensor, slack: Optional[torch.Tensor] = None,
+              lo: Optional[torch.Tensor] = None, hi: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """g = G_t z_t (+ slack), clamped to [lo, hi] when given
+    (tmpc_ineq_rows_*); G (Nb, T, m, n), z (Nb, T, n) -> (Nb, T, m)."""
+    lib = _ffi.load()
+    Nb, T, m, n = G.shape
+    dt, dev = G.dtype, G.device
+    out = torch.empty(Nb, T, m, dtype=dt, device=dev)
+    d = _ffi.TmpcDims(Nb, T, n, 0, 0, m)
+    Gc, zc = G.contiguous(), z.contiguous()
+    sl = slack.contiguous() if slack is not None else None
+    lc = lo.contiguous() if lo is not None else None
+    hc = hi.contiguous() if hi is not None else None
+    name = f"tmpc_ineq_rows_{_suffix(dt)}"
+    _ffi.check(name, getattr(lib, name)(C.byref(d), _ptr(Gc, dt, dev), _ptr(zc, dt, dev), _ptr(sl, dt, dev),
+                                        _ptr(lc, dt, dev), _ptr(hc, dt, dev), _ptr(out), _stream(dev)))
+    return out
 
 
 def mlp_cost_blocks_(D: torch.Tensor, q: torch.Tensor, states: torch.Tensor, controls: torch.Tensor,

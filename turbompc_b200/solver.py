@@ -338,6 +338,15 @@ class TurboMPCSolver:
             conv = torch.maximum(conv, _inf(sw[:, None, None] * slacks + st.y_g))
         return conv, eq, ineq, gb
 
+    @staticmethod
+    def _ineq_rows(qp: QPData, xb, slacks=None):
+        """g = G z (+ slacks) at the QP's iterate: the CUDA kernel for GPU
+        tensors (tmpc_ineq_rows_*)."""
+        if xb.is_cuda:
+            return ops.ineq_rows(qp.ineq.G, xb, slacks)
+        g = torch.einsum("btki,bti->btk", qp.ineq.G, xb)
+        return g if slacks is None else g + slacks
+
     def _build_kkt_state(self, states, controls, st: ADMMState, g, l, u) -> KKTState:
         """turbompc_solver.py:1387-1439."""
         nx = self._program.num_state_variables
@@ -404,13 +413,10 @@ class TurboMPCSolver:
                     qp_next = qp
                     cv = step if k == 0 else conv
                     ev = iv = torch.zeros_like(cv)
-                    g = torch.einsum("btki,bti->btk", qp.ineq.G, xb)
-                    if qp.ineq.use_slack_variables:
-                        g = g + sl_new
+                    g = self._ineq_rows(qp, xb, sl_new if qp.ineq.use_slack_variables else None)
             else:
                 qp_next = self._build_qp_data(s_new, c_new, params, prev=qp) if k + 1 < max_iter else qp
-                cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), torch.einsum(
-                    "btki,bti->btk", qp_next.ineq.G, xb)
+                cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), self._ineq_rows(qp_next, xb)
             kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
             # Masked update (problems already converged keep their iterate).
             sel = lambda new, old: torch.where(active.view(-1, *([1] * (new.dim() - 1))), new, old)
