@@ -40,9 +40,10 @@ METRIC = "MPC solves/sec (quadrotor N=50, batch 65536)"
 NCU_DRAM_BYTES_PER_PROBLEM = 257.2e3
 # DRAM bytes (read + write) per problem of one launch of il_admm_kernel (the
 # 30 ADMM iterations of the direct path), from the ncu capture summarised in
-# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 52.04 GB; A+ = [-I 0]
-# and the unit rows of G detected, so neither is streamed).
-NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 6.353e6
+# profiles/il_admm_quadrotor_b8192_fp32.txt (8192 problems; 48.84 GB; the compact
+# variant: A+ = [-I 0], the unit rows of G and the zero rows of W detected, so
+# none of them is streamed).
+NCU_DIRECT_DRAM_BYTES_PER_PROBLEM = 5.962e6
 
 
 def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_select=False, w_rows=None):
