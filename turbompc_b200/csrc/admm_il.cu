@@ -167,41 +167,55 @@ __global__ void il_scalars_in_kernel(IlArgs<R> A, const R* rho_in, const R* sw_i
 
 // ---------------------------------------------------------------------------
 // Structure of A+: the explicit integrators give A+_t = [-I 0] for every
-// stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One
-// coalesced pass over the caller's problem-major array checks every problem's
-// A+ exactly, before any layout conversion; where all 32 problems of a group
+// stage (turbompc/problems/optimal_control_problem.py:1256-1271).  One pass
+// over the caller's problem-major array (a block per problem, a thread per
+// row) checks every problem's A+ exactly, before any layout conversion; where all 32 problems of a group
 // match, the group's A+ is not
 // converted to the interleaved layout and the assembly, the first gamma and
 // the iteration kernel form its products from the identity (bit-identical:
 // the products with the exact -1 and 0 entries are exact).
 // ---------------------------------------------------------------------------
 constexpr int kFlatThreads = 256;
-inline unsigned flat_blocks(size_t elems) {
-  const size_t b = (elems + kFlatThreads - 1) / kFlatThreads;
-  return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+
+// Whether a row of n values equals `one` at column c and 0 elsewhere (128-bit
+// loads when the row is 16-byte aligned and n a multiple of the vector width).
+template <typename R>
+__device__ __forceinline__ bool row_is_unit(const R* row, int n, int c, R one) {
+  constexpr int V = 16 / sizeof(R);
+  int bad = 0;  // no short-circuit: the loads stay independent
+  if (n % V == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    for (int j = 0; j < n; j += V) {
+      R w[V];
+      ld128(w, row + j);
+#pragma unroll
+      for (int v = 0; v < V; ++v) bad |= w[v] != (j + v == c ? one : R(0));
+    }
+  } else {
+    for (int j = 0; j < n; ++j) bad |= row[j] != (j == c ? one : R(0));
+  }
+  return bad == 0;
 }
 
 template <typename R>
 __global__ void __launch_bounds__(kFlatThreads) il_ap_identity_kernel(IlArgs<R> A, const R* __restrict__ ap_pm) {
-  // one pass over the whole problem-major array (coalesced, grid-stride):
-  // apid[grp] was set to 1 by il_scalars_in_kernel and is cleared (plain
-  // stores of 0) where any entry of the group's problems differs
-  const int n = A.n, nx = A.nx;
-  const size_t per_stage = (size_t)nx * n, per_prob = (size_t)(A.T - 1) * per_stage;
-  const size_t total = per_prob * (size_t)A.Nb;
-  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const size_t b = e / per_prob, s = (e - b * per_prob) % per_stage;
-    const int k = (int)(s / n), j = (int)(s - (size_t)k * n);
-    if (ap_pm[e] != (j == k ? R(-1) : R(0))) A.apid[b / kWarp] = 0;
-  }
+  // one block per problem, one thread per row (t, k) of its A+ (the rows of a
+  // warp are one contiguous run): row k of A+_t must be -e_k.  apid[grp] was
+  // set to 1 by il_scalars_in_kernel and is cleared (plain stores of 0) on a
+  // mismatch
+  const int b = blockIdx.x, n = A.n, nx = A.nx, rows = (A.T - 1) * nx;
+  const R* P = ap_pm + (size_t)b * rows * n;
+  bool ok = true;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) ok &= row_is_unit(P + (size_t)r * n, n, r % nx, R(-1));
+  if (!__syncthreads_and(ok) && threadIdx.x == 0) A.apid[b / kWarp] = 0;
 }
 
 // ---------------------------------------------------------------------------
 // Structure of G: box constraints on single variables (the quadrotor's thrust
 // bounds) make every inequality row a unit vector, G_t[k] = e_{c_k}, with the
 // same columns c_k in every stage.  One thread per (group, row) takes the
-// columns from the group's first problem's first stage, then one coalesced
-// pass over the caller's problem-major array checks every row exactly; where
+// columns from the group's first problem's first stage, then one pass over
+// the caller's problem-major array (a block per problem, a thread per row)
+// checks every row exactly; where
 // all 32 problems of a group match, the group's G is not
 // converted to the interleaved layout and the assembly, the first gamma and
 // the iteration kernel form G x and G^T y from the columns (the same sums:
@@ -225,18 +239,15 @@ __global__ void __launch_bounds__(kFlatThreads) il_g_columns_kernel(IlArgs<R> A,
 
 template <typename R>
 __global__ void __launch_bounds__(kFlatThreads) il_g_select_kernel(IlArgs<R> A, const R* __restrict__ g_pm) {
-  // one pass over the whole problem-major array (coalesced, grid-stride):
-  // every row k of every stage must equal e_{gcol[k]}; gsel[grp] is cleared
-  // (plain stores of 0) where any entry of the group's problems differs
-  const int n = A.n, m = A.m;
-  const size_t per_stage = (size_t)m * n, per_prob = (size_t)A.T * per_stage;
-  const size_t total = per_prob * (size_t)A.Nb;
-  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const size_t b = e / per_prob, s = (e - b * per_prob) % per_stage;
-    const int k = (int)(s / n), j = (int)(s - (size_t)k * n);
-    const size_t grp = b / kWarp;
-    if (g_pm[e] != (j == A.gcol[grp * m + k] ? R(1) : R(0))) A.gsel[grp] = 0;
-  }
+  // one block per problem, one thread per row (t, k) of its G: row k of every
+  // stage must equal e_{gcol[k]}; gsel[grp] is cleared (plain stores of 0)
+  // on a mismatch
+  const int b = blockIdx.x, n = A.n, m = A.m, rows = A.T * m;
+  const int* gc = A.gcol + (size_t)(b / kWarp) * m;
+  const R* P = g_pm + (size_t)b * rows * n;
+  bool ok = true;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) ok &= row_is_unit(P + (size_t)r * n, n, gc[r % m], R(1));
+  if (!__syncthreads_and(ok) && threadIdx.x == 0) A.gsel[b / kWarp] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -1046,7 +1057,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   // structure of A+ and G on the caller's arrays: groups where it holds
   // convert neither (their rows are formed from the structure)
   if (N > 0) {
-    il_ap_identity_kernel<R><<<flat_blocks((size_t)Nb * N * nx * n), kFlatThreads, 0, st>>>(
+    il_ap_identity_kernel<R><<<(unsigned)Nb, kFlatThreads, 0, st>>>(
         A, static_cast<const R*>(P.qp.A_plus));
     chk((int)cudaPeekAtLastError());
   } else {
@@ -1055,7 +1066,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
   if (m > 0) {
     il_g_columns_kernel<R><<<(unsigned)((groups(Nb) * m + kFlatThreads - 1) / kFlatThreads), kFlatThreads, 0, st>>>(
         A, static_cast<const R*>(P.qp.G));
-    il_g_select_kernel<R><<<flat_blocks((size_t)Nb * T * m * n), kFlatThreads, 0, st>>>(A, static_cast<const R*>(P.qp.G));
+    il_g_select_kernel<R><<<(unsigned)Nb, kFlatThreads, 0, st>>>(A, static_cast<const R*>(P.qp.G));
     chk((int)cudaPeekAtLastError());
   } else {
     cudaMemsetAsync(A.gsel, 0, groups(Nb) * sizeof(int), st);
