@@ -378,7 +378,11 @@ class TurboMPCSolver:
             admm_state0 = ops.admm_initial_state(qp, self._params["admm"]["rho"])
         st = admm_state0
         slacks = st.xi_g
-        z_prev = torch.cat([states, controls], -1)
+        # The selected iterate (z = [states, controls], unscaled) of every
+        # problem: its last active SQP iterate.  The KKT state is elementwise in
+        # (iterate, ADMM state, g, l, u), so it is built once after the loop
+        # from the selected inputs (equal to selecting the per-iteration states).
+        z_cur = torch.cat([states, controls], -1)
         conv = torch.full((Nb,), float("inf"), dtype=dt, device=dev)
         it_count = torch.zeros(Nb, dtype=torch.int64, device=dev)
         admm_iters = torch.zeros(Nb, max_iter, dtype=torch.int64, device=dev)
@@ -387,7 +391,7 @@ class TurboMPCSolver:
         cerr = torch.zeros(Nb, max_iter, dtype=dt, device=dev)
         active = torch.ones(Nb, dtype=torch.bool, device=dev)
         nx = self._program.num_state_variables
-        kkt = None
+        g_sel = l_sel = u_sel = None
         sw = qp.ineq.slack_penalization_weight
         kstatus = torch.zeros(Nb, dtype=torch.int32, device=dev)
         rescale = bool(getattr(self._program, "rescale_optimization_variables", False))
@@ -395,19 +399,19 @@ class TurboMPCSolver:
             if k > 0 and tol > 0 and not bool(active.any()):
                 break
             st_new, iters, status = ops.admm_solve(qp, st, cfg, slack_weight=sw, workspace=self._workspace)
-            kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
             xb = st_new.x_blocks  # QP (scaled) coordinates
-            s_new, c_new = xb[..., :nx], xb[..., nx:]
             if rescale:
-                s_new, c_new = self._program.unscale_states_controls(s_new, c_new, params)
+                s_new, c_new = self._program.unscale_states_controls(xb[..., :nx], xb[..., nx:], params)
+                z_new = torch.cat([s_new, c_new], -1)
+            else:
+                z_new = xb
             sl_new = st_new.xi_g
-            z_new = torch.cat([s_new, c_new], -1)
-            step = _inf(z_new - z_prev)
+            step = _inf(z_new - z_cur)
             if sl_new.shape[-1] > 0:
                 step = step + _inf(sl_new - slacks)
             if crit == "first_order":
                 if k + 1 < max_iter:
-                    qp_next = self._build_qp_data(s_new, c_new, params, prev=qp)
+                    qp_next = self._build_qp_data(z_new[..., :nx], z_new[..., nx:], params, prev=qp)
                     cv, ev, iv, g = self._first_order_error(qp_next, xb[..., :nx], xb[..., nx:], sl_new, st_new)
                 else:
                     qp_next = qp
@@ -415,18 +419,27 @@ class TurboMPCSolver:
                     ev = iv = torch.zeros_like(cv)
                     g = self._ineq_rows(qp, xb, sl_new if qp.ineq.use_slack_variables else None)
             else:
-                qp_next = self._build_qp_data(s_new, c_new, params, prev=qp) if k + 1 < max_iter else qp
+                qp_next = self._build_qp_data(z_new[..., :nx], z_new[..., nx:], params, prev=qp) \
+                    if k + 1 < max_iter else qp
                 cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), self._ineq_rows(qp_next, xb)
-            kkt_new = self._build_kkt_state(s_new, c_new, st_new, g, qp_next.ineq.l, qp_next.ineq.u)
-            # Masked update (problems already converged keep their iterate).
-            sel = lambda new, old: torch.where(active.view(-1, *([1] * (new.dim() - 1))), new, old)
-            states, controls, slacks = sel(s_new, states), sel(c_new, controls), sel(sl_new, slacks)
-            st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
-            kkt = kkt_new if kkt is None else KKTState(*(sel(n_, o_) for n_, o_ in zip(kkt_new, kkt)))
-            z_prev = sel(z_new, z_prev)
-            admm_iters[:, k] = torch.where(active, iters, admm_iters[:, k])
+            l_new, u_new = qp_next.ineq.l, qp_next.ineq.u
+            if k == 0:  # every problem is active: nothing to select
+                kstatus = status.clone()
+                z_cur, slacks, st = z_new, sl_new, st_new
+                g_sel, l_sel, u_sel = g, l_new, u_new
+                admm_iters[:, k] = iters
+                conv = cv
+            else:
+                # Masked update (problems already converged keep their iterate).
+                sel = lambda new, old: new if new is old else torch.where(
+                    active.view(-1, *([1] * (new.dim() - 1))), new, old)
+                kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
+                z_cur, slacks = sel(z_new, z_cur), sel(sl_new, slacks)
+                st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
+                g_sel, l_sel, u_sel = sel(g, g_sel), sel(l_new, l_sel), sel(u_new, u_sel)
+                admm_iters[:, k] = torch.where(active, iters, admm_iters[:, k])
+                conv = sel(cv, conv)
             eqv[:, k], inv[:, k], cerr[:, k] = ev, iv, cv
-            conv = sel(cv, conv)
             it_count = it_count + active.to(torch.int64)
             if k + 1 < max_iter:
                 # Every problem moves on to the QP at its new iterate: a problem
@@ -435,6 +448,8 @@ class TurboMPCSolver:
                 # never waits on the device to decide.
                 qp = qp_next
             active = active & (conv > tol)
+        states, controls = z_cur[..., :nx].contiguous(), z_cur[..., nx:].contiguous()
+        kkt = None if g_sel is None else self._build_kkt_state(states, controls, st, g_sel, l_sel, u_sel)
         return TurboMPCSolution(states=states, controls=controls, slack=st.xi_g, status=self.STATUS_SUCCESS,
                                 num_iter=it_count, convergence_error=conv, admm_iters=admm_iters, admm_state=st,
                                 solver_stats=SolverStats(admm_iters, eqv, inv, cerr, kstatus), kkt_state=kkt)
