@@ -284,13 +284,15 @@ __global__ void __launch_bounds__(kWrowThreads) il_w_rows_kernel(IlArgs<R> A, co
 
 // ---------------------------------------------------------------------------
 // Theta_t (lower, packed) and Phi_t at each problem's rho, written into the
-// interleaved operator (the factor's input format): one thread per (problem,
-// stage), the 32 problems of a group in one warp.  The sums of assemble.cuh
+// interleaved operator (the factor's input format): a block of four warps per
+// (group, stage), lane = problem; warp p forms a quarter of Theta_t's lower
+// triangle (a range of its columns, split by entry count: column c takes row c
+// of D_t) and a quarter of Phi_t's rows.  The sums of assemble.cuh
 // (admm.py:93-101), in the same order, formed as rank-1 updates of register
 // accumulators, one row of G / A0 / A- / A+ at a time (each row read once,
 // coalesced from the interleaved copies):
 //   Theta = ((D + sigma I) + rho_ineq sum_k g_k g_k^T) + rho_f sum_k a_k a_k^T
-//   Phi_t = E_t + rho_f sum_k Ap_t[k]^T Am_t[k]   (rows of Phi in two halves)
+//   Phi_t = E_t + rho_f sum_k Ap_t[k]^T Am_t[k]
 // D and E come from the caller's problem-major arrays (Theta's element (r, c),
 // r >= c, takes D[c][r], as the other assembly paths do).
 // ---------------------------------------------------------------------------
@@ -316,15 +318,39 @@ __device__ __forceinline__ void il_load_row(R (&dst)[NB], const R* src, int n, b
   }
 }
 
-template <int NB, typename R>
-__global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP qp, const int* gate) {
-  if (gate && *gate == 0) return;
-  constexpr int TR = NB * (NB + 1) / 2;
-  constexpr int HB = NB / 2;
-  static_assert(HB * NB <= TR, "Phi half-block fits the accumulators");
-  const int lane = threadIdx.x, t = blockIdx.y, grp = blockIdx.x;
+// Columns of the lower triangle of a stage block split into kAsmParts parts
+// of about equal entry counts: part p covers columns [asm_bound(NB, p),
+// asm_bound(NB, p + 1)) (column c holds the NB - c entries (r >= c, c) and
+// takes row c of D, so no part reads another's rows of D).
+constexpr int kAsmParts = 4;
+__host__ __device__ constexpr int asm_cum(int NB, int c) { return c * NB - c * (c - 1) / 2; }  // entries of columns < c
+__host__ __device__ constexpr int asm_bound(int NB, int p) {
+  if (p <= 0) return 0;
+  if (p >= kAsmParts) return NB;
+  const int target = p * NB * (NB + 1) / 2 / kAsmParts;
+  int best = 0, bd = 1 << 30;
+  for (int c = 0; c <= NB; ++c) {
+    const int d = asm_cum(NB, c) - target;
+    const int ad = d < 0 ? -d : d;
+    if (ad < bd) {
+      bd = ad;
+      best = c;
+    }
+  }
+  return best;
+}
+// Index of entry (r, c), r >= c, among the entries of the columns [C0, ...).
+__host__ __device__ constexpr int asm_idx(int NB, int C0, int r, int c) {
+  return asm_cum(NB, c) - asm_cum(NB, C0) + (r - c);
+}
+
+// Part P of the stage's Theta columns and Phi rows (one warp; lane = problem).
+template <int NB, typename R, int P>
+__device__ __forceinline__ void il_assemble_part(const IlArgs<R>& A, const TmpcQP& qp, int grp, int t, int lane) {
+  constexpr int C0 = asm_bound(NB, P), C1 = asm_bound(NB, P + 1);
+  constexpr int CNT = asm_cum(NB, C1) - asm_cum(NB, C0);
+  constexpr int H0 = P * NB / kAsmParts, H1 = (P + 1) * NB / kAsmParts, HR = H1 - H0;  // Phi rows
   const int b = grp * kWarp + lane;
-  if (b >= A.Nb) return;
   const int T = A.T, N = T - 1, n = A.n, nx = A.nx, n0 = A.n0, m = A.m;
   const IlSizes z(T, n, nx, n0, m);
   const int trin = (int)tri(n);
@@ -341,120 +367,129 @@ __global__ void __launch_bounds__(kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP 
   const R* AMl = lv(A.am, z.am);
   const R* APl = lv(A.ap, z.am);
   const R* D = static_cast<const R*>(qp.D) + ((size_t)b * T + t) * n * n;
-  R acc[TR];
-  // rank-1 updates acc += a a^T from a row of n values at p (interleaved, stride 32)
-  auto rank1 = [&](const R* p) {
+  R acc[CNT > 0 ? CNT : 1];
+  // rank-1 updates acc += a a^T (columns C0..C1-1) from a row of n values at p (interleaved, stride 32)
+  auto rank1 = [&](R (&ac)[CNT > 0 ? CNT : 1], const R* p) {
     R a[NB];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) a[j] = j < n ? p[j * kWarp] : R(0);
+    for (int j = 0; j < NB; ++j) a[j] = (j >= C0 && j < n) ? p[j * kWarp] : R(0);
 #pragma unroll
-    for (int r = 0; r < NB; ++r)
+    for (int c = C0; c < C1; ++c)
 #pragma unroll
-      for (int c = 0; c <= r; ++c) acc[LI(r, c)] = fma(a[c], a[r], acc[LI(r, c)]);
+      for (int r = c; r < NB; ++r) ac[asm_idx(NB, C0, r, c)] = fma(a[c], a[r], ac[asm_idx(NB, C0, r, c)]);
   };
-  // ---- Theta_t: (D + sigma I) + rho_ineq G^T G
+  if (CNT > 0) {
+    // ---- Theta_t: (D + sigma I) + rho_ineq G^T G
 #pragma unroll
-  for (int e = 0; e < TR; ++e) acc[e] = R(0);
-  if (gS) {
-    for (int k = 0; k < m; ++k) {
-      const int c = gc[k];
+    for (int e = 0; e < CNT; ++e) acc[e] = R(0);
+    if (gS) {
+      for (int k = 0; k < m; ++k) {
+        const int c = gc[k];
 #pragma unroll
-      for (int r = 0; r < NB; ++r)
-        if (r == c) acc[LI(r, r)] = fma(R(1), R(1), acc[LI(r, r)]);
-    }
-  } else {
-    for (int k = 0; k < m; ++k) rank1(Gl + (size_t)(t * m + k) * n * kWarp);
-  }
-  // Theta's column c takes row c of D_t (D[c][r], r >= c): rows read whole, with
-  // 128-bit loads where the rows are 16-byte aligned (a lane's row is one
-  // contiguous run in the caller's problem-major array)
-  const bool vec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
-#pragma unroll
-  for (int c = 0; c < NB; ++c) {
-    if (c < n) {
-      R dr[NB];
-      il_load_row<NB>(dr, D + c * n, n, vec);
-#pragma unroll
-      for (int r = c; r < NB; ++r) {
-        if (r < n) {
-          R v = dr[r];
-          if (r == c) v += A.sigma;
-          v += rho * acc[LI(r, c)];
-          acc[LI(r, c)] = v;
-        }
+        for (int r = C0; r < C1; ++r)
+          if (r == c) acc[asm_idx(NB, C0, r, r)] = fma(R(1), R(1), acc[asm_idx(NB, C0, r, r)]);
       }
-    }
-  }
-  // park (D + sigma I) + rho G^T G in the output, then + rho_f A^T A
-#pragma unroll
-  for (int r = 0; r < NB; ++r)
-#pragma unroll
-    for (int c = 0; c <= r; ++c)
-      if (r < n) O[(size_t)(t * trin + LI(r, c)) * kWarp] = acc[LI(r, c)];
-#pragma unroll
-  for (int e = 0; e < TR; ++e) acc[e] = R(0);
-  if (t == 0) {
-    for (int k = 0; k < n0; ++k) rank1(A0l + (size_t)k * n * kWarp);
-    if (N > 0)
-      for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)k * n * kWarp);
-  } else {
-    if (apI) {
-#pragma unroll
-      for (int r = 0; r < NB; ++r)
-        if (r < nx) acc[LI(r, r)] = fma(R(-1), R(-1), acc[LI(r, r)]);
     } else {
-      for (int k = 0; k < nx; ++k) rank1(APl + (size_t)((t - 1) * nx + k) * n * kWarp);
+      for (int k = 0; k < m; ++k) rank1(acc, Gl + (size_t)(t * m + k) * n * kWarp);
     }
-    if (t < N)
-      for (int k = 0; k < nx; ++k) rank1(AMl + (size_t)(t * nx + k) * n * kWarp);
-  }
+    // Theta's column c takes row c of D_t (D[c][r], r >= c): rows read whole, with
+    // 128-bit loads where the rows are 16-byte aligned (a lane's row is one
+    // contiguous run in the caller's problem-major array)
+    const bool vec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
 #pragma unroll
-  for (int r = 0; r < NB; ++r)
+    for (int c = C0; c < C1; ++c) {
+      if (c < n) {
+        R dr[NB];
+        il_load_row<NB>(dr, D + c * n, n, vec);
 #pragma unroll
-    for (int c = 0; c <= r; ++c)
-      if (r < n) {
-        R* o = O + (size_t)(t * trin + LI(r, c)) * kWarp;
-        *o = *o + rf * acc[LI(r, c)];
-      }
-  if (t >= N) return;
-  // ---- Phi_t = E_t + rho_f Ap_t^T Am_t, rows [h, h + NB/2)
-  const R* E = static_cast<const R*>(qp.E) + ((size_t)b * N + t) * n * n;
-  for (int h = 0; h < n; h += HB) {
-#pragma unroll
-    for (int e = 0; e < HB * NB; ++e) acc[e] = R(0);
-    if (apI) {  // A+^T A- has the rows -A-_t[k] (k < nx) and zero rows below
-#pragma unroll
-      for (int i = 0; i < HB; ++i)
-        if (h + i < nx) {
-          const R* am = AMl + (size_t)(t * nx + h + i) * n * kWarp;
-#pragma unroll
-          for (int j = 0; j < NB; ++j) acc[i * NB + j] = fma(R(-1), j < n ? am[j * kWarp] : R(0), R(0));
+        for (int r = c; r < NB; ++r) {
+          if (r < n) {
+            R v = dr[r];
+            if (r == c) v += A.sigma;
+            v += rho * acc[asm_idx(NB, C0, r, c)];
+            acc[asm_idx(NB, C0, r, c)] = v;
+          }
         }
+      }
     }
-    for (int k = 0; k < (apI ? 0 : nx); ++k) {
+    // + rho_f A^T A, accumulated apart and added last
+    R ac2[CNT > 0 ? CNT : 1];
+#pragma unroll
+    for (int e = 0; e < CNT; ++e) ac2[e] = R(0);
+    if (t == 0) {
+      for (int k = 0; k < n0; ++k) rank1(ac2, A0l + (size_t)k * n * kWarp);
+      if (N > 0)
+        for (int k = 0; k < nx; ++k) rank1(ac2, AMl + (size_t)k * n * kWarp);
+    } else {
+      if (apI) {
+#pragma unroll
+        for (int r = C0; r < C1; ++r)
+          if (r < nx) ac2[asm_idx(NB, C0, r, r)] = fma(R(-1), R(-1), ac2[asm_idx(NB, C0, r, r)]);
+      } else {
+        for (int k = 0; k < nx; ++k) rank1(ac2, APl + (size_t)((t - 1) * nx + k) * n * kWarp);
+      }
+      if (t < N)
+        for (int k = 0; k < nx; ++k) rank1(ac2, AMl + (size_t)(t * nx + k) * n * kWarp);
+    }
+#pragma unroll
+    for (int c = C0; c < C1; ++c)
+#pragma unroll
+      for (int r = c; r < NB; ++r)
+        if (r < n) O[(size_t)(t * trin + LI(r, c)) * kWarp] = acc[asm_idx(NB, C0, r, c)] + rf * ac2[asm_idx(NB, C0, r, c)];
+  }
+  if (t >= N || HR <= 0) return;
+  // ---- Phi_t = E_t + rho_f Ap_t^T Am_t, rows [H0, H1)
+  const R* E = static_cast<const R*>(qp.E) + ((size_t)b * N + t) * n * n;
+  R ph[HR > 0 ? HR * NB : 1];
+#pragma unroll
+  for (int e = 0; e < HR * NB; ++e) ph[e] = R(0);
+  if (apI) {  // A+^T A- has the rows -A-_t[k] (k < nx) and zero rows below
+#pragma unroll
+    for (int i = 0; i < HR; ++i)
+      if (H0 + i < nx) {
+        const R* am = AMl + (size_t)(t * nx + H0 + i) * n * kWarp;
+#pragma unroll
+        for (int j = 0; j < NB; ++j) ph[i * NB + j] = fma(R(-1), j < n ? am[j * kWarp] : R(0), R(0));
+      }
+  } else {
+    for (int k = 0; k < nx; ++k) {
       const R* ap = APl + (size_t)(t * nx + k) * n * kWarp;
       const R* am = AMl + (size_t)(t * nx + k) * n * kWarp;
-      R x[HB], y[NB];
+      R x[HR > 0 ? HR : 1], y[NB];
 #pragma unroll
-      for (int i = 0; i < HB; ++i) x[i] = h + i < n ? ap[(h + i) * kWarp] : R(0);
+      for (int i = 0; i < HR; ++i) x[i] = H0 + i < n ? ap[(H0 + i) * kWarp] : R(0);
 #pragma unroll
       for (int j = 0; j < NB; ++j) y[j] = j < n ? am[j * kWarp] : R(0);
 #pragma unroll
-      for (int i = 0; i < HB; ++i)
+      for (int i = 0; i < HR; ++i)
 #pragma unroll
-        for (int j = 0; j < NB; ++j) acc[i * NB + j] = fma(x[i], y[j], acc[i * NB + j]);
+        for (int j = 0; j < NB; ++j) ph[i * NB + j] = fma(x[i], y[j], ph[i * NB + j]);
     }
-    const bool evec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(E) & 15) == 0;
+  }
+  const bool evec = (n * sizeof(R)) % 16 == 0 && (reinterpret_cast<uintptr_t>(E) & 15) == 0;
 #pragma unroll
-    for (int i = 0; i < HB; ++i) {
-      if (h + i < n) {
-        R er[NB];
-        il_load_row<NB>(er, E + (h + i) * n, n, evec);
+  for (int i = 0; i < HR; ++i) {
+    if (H0 + i < n) {
+      R er[NB];
+      il_load_row<NB>(er, E + (H0 + i) * n, n, evec);
 #pragma unroll
-        for (int j = 0; j < NB; ++j)
-          if (j < n) O[(size_t)(T * trin + (t * n + h + i) * n + j) * kWarp] = er[j] + rf * acc[i * NB + j];
-      }
+      for (int j = 0; j < NB; ++j)
+        if (j < n) O[(size_t)(T * trin + (t * n + H0 + i) * n + j) * kWarp] = er[j] + rf * ph[i * NB + j];
     }
+  }
+}
+
+template <int NB, typename R>
+__global__ void __launch_bounds__(kAsmParts * kWarp) il_assemble_kernel(IlArgs<R> A, TmpcQP qp, const int* gate) {
+  if (gate && *gate == 0) return;
+  const int lane = threadIdx.x & (kWarp - 1), part = threadIdx.x / kWarp, t = blockIdx.y, grp = blockIdx.x;
+  if (grp * kWarp + lane >= A.Nb) return;
+  static_assert(kAsmParts == 4, "four parts");
+  switch (part) {
+    case 0: il_assemble_part<NB, R, 0>(A, qp, grp, t, lane); break;
+    case 1: il_assemble_part<NB, R, 1>(A, qp, grp, t, lane); break;
+    case 2: il_assemble_part<NB, R, 2>(A, qp, grp, t, lane); break;
+    default: il_assemble_part<NB, R, 3>(A, qp, grp, t, lane); break;
   }
 }
 
@@ -1112,7 +1147,7 @@ int launch_admm_direct_il(const AdmmParams<R>& P, size_t ws_bytes, cudaStream_t 
     // operator, factor (in place) and the first gamma; with `gate`, only
     // when a check opened it, gamma only for the flagged problems
     auto build = [&](const int* gate) {
-      il_assemble_kernel<NB, R><<<ggrid, kWarp, 0, st>>>(A, P.qp, gate);
+      il_assemble_kernel<NB, R><<<ggrid, kAsmParts * kWarp, 0, st>>>(A, P.qp, gate);
       chk((int)cudaPeekAtLastError());
       chk(launch_factor<NB, R>(Nb, T, n, A.ops, A.ops, A.fstat, gate, st));
       il_w_rows_kernel<R><<<(unsigned)groups(Nb), kWrowThreads, 0, st>>>(A, gate);
