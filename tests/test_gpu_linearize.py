@@ -95,21 +95,28 @@ def test_qp_reuse_equals_full_build():
 
 
 @pytest.mark.parametrize("slack", [False, True])
-def test_first_order_error_kernel_matches_torch(slack):
+@pytest.mark.parametrize("nx,nu,dtype", [(6, 3, torch.float64), (12, 4, torch.float64), (12, 4, torch.float32),
+                                         (6, 2, torch.float32), (5, 3, torch.float32)])
+def test_first_order_error_kernel_matches_torch(slack, nx, nu, dtype):
     """tmpc_first_order_error_* against the PyTorch form of the SQP first-order
-    check (fp64, dense QP blocks incl. E coupling, n0 rows, slack variables)."""
+    check (dense QP blocks incl. E coupling, n0 rows, slack variables) in fp64
+    and fp32 at block sizes 8, 9 and 16 (the fp32 results against the fp64
+    PyTorch form)."""
     from tests.helpers import dense_blocks
     from turbompc_b200.problems import synthetic
-    Nb = 5
-    b = dense_blocks(Nb, 6, 3, 9, 4, seed=4)
+    Nb, n = 5, nx + nu
+    b = dense_blocks(Nb, nx, nu, 9, 4, seed=4)
     sw = np.full(Nb, 3.0) if slack else None
-    qd = synthetic.to_qpdata(b, dtype=torch.float64, device="cuda", slack_weight=sw, use_slack=slack)
+    qd = synthetic.to_qpdata(b, dtype=dtype, device="cuda", slack_weight=sw, use_slack=slack)
     g = torch.Generator(device="cuda").manual_seed(5)
-    r = lambda *s: torch.randn(*s, generator=g, device="cuda", dtype=torch.float64)
-    st = ops.ADMMState(r(Nb, 10, 9), r(Nb, 10, 4), r(Nb, 6), r(Nb, 9, 6), r(Nb, 10, 4), r(Nb, 10, 4), r(Nb).abs())
-    states, controls, slacks = r(Nb, 10, 6), r(Nb, 10, 3), r(Nb, 10, 4)
+    r = lambda *s: torch.randn(*s, generator=g, device="cuda", dtype=dtype)
+    st = ops.ADMMState(r(Nb, 10, n), r(Nb, 10, 4), r(Nb, nx), r(Nb, 9, nx), r(Nb, 10, 4), r(Nb, 10, 4), r(Nb).abs())
+    states, controls, slacks = r(Nb, 10, nx), r(Nb, 10, nu), r(Nb, 10, 4)
     s = TurboMPCSolver.__new__(TurboMPCSolver)
     a = s._first_order_error(qd, states, controls, slacks, st)
-    c = s._first_order_error_torch(qd, states, controls, slacks, st)
+    d64 = lambda t: t.double()
+    qd64 = qd.map(d64) if dtype != torch.float64 else qd
+    c = s._first_order_error_torch(qd64, d64(states), d64(controls), d64(slacks), ops.ADMMState(*(d64(t) for t in st)))
+    tol = 1e-12 if dtype == torch.float64 else 1e-5
     for x, y in zip(a, c):
-        assert rel_err(x.cpu().numpy(), y.cpu().numpy()) < 1e-12
+        assert rel_err(x.double().cpu().numpy(), y.cpu().numpy()) < tol
