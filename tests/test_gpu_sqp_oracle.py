@@ -126,6 +126,22 @@ def test_config3_quadrotor_direct_backend_matches_oracle(dtype):
     _check_solution(sol, osols, dtype, "config 3 direct")
 
 
+def test_quadrotor_control_rate_direct_backend_matches_oracle_fp32():
+    """A control-rate penalty puts nonzero control rows into E_t, so the rows
+    nx..n-1 of every W_t are not zero: the interleaved direct path must detect
+    that and run its full kernel variant (W read whole); against the oracle
+    with dense solves."""
+    B, N, sqp, admm = 4, 50, 3, 30
+    kw = (("rate_weight", 0.5),)
+    _, _, osols, _ = _oracle_run("quadrotor", B, N, sqp, admm, 1, False, kw, linsys="dense")
+    prog, params = _make("quadrotor", B, N, torch.float32, "cuda", **dict(kw))
+    s = TurboMPCSolver(prog, _fixed(sqp, admm, 1), forward_backend="b200_direct")
+    g = s.initial_guess(params)
+    qp = s._build_qp_data(g.states, g.controls, params)
+    assert bool((qp.cost.E[..., 12:, :] != 0).any())
+    _check_solution(s.solve(g, params), osols, torch.float32, "quadrotor control rate direct")
+
+
 def test_config4_and_5_direct_backend_match_oracle_fp32():
     """Obstacle rows (m = 12, warm-started re-solve) and the CW + MLP problem
     (n = 9: the interleaved kernels with padded stage blocks) on the direct

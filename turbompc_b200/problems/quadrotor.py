@@ -42,8 +42,12 @@ def quadrotor_params(batch, N=50, dt=0.02, seed=0, dtype=torch.float32, device="
     }
 
 
-def make_quadrotor_problem(batch, N=50, dt=0.02, seed=0, dtype=torch.float32, device="cuda"):
+def make_quadrotor_problem(batch, N=50, dt=0.02, seed=0, dtype=torch.float32, device="cuda", rate_weight=0.0):
+    """Config 3; rate_weight > 0 adds a control-rate penalty (the QP's E blocks
+    then couple consecutive stages' controls)."""
     params = quadrotor_params(batch, N, dt, seed, dtype, device)
+    if rate_weight:
+        params["weights_penalization_control_rate"] = torch.full((4,), float(rate_weight), dtype=dtype, device=device)
     return OptimalControlProblem(Quadrotor12Dynamics(), params), params
 
 
