@@ -187,6 +187,13 @@ class TurboMPCSolver:
         self._workspace = None
         self.solve = self.get_differentiable_solve_function()
 
+    def _side_stream(self, dev):
+        """One side stream per device for the overlapped first-order check."""
+        ss = self.__dict__.setdefault("_side_streams", {})
+        if dev.index not in ss:
+            ss[dev.index] = torch.cuda.Stream(device=dev)
+        return ss[dev.index]
+
     # -------------------------------------------------------------- props
     @property
     def program(self):
@@ -395,10 +402,38 @@ class TurboMPCSolver:
         sw = qp.ineq.slack_penalization_weight
         kstatus = torch.zeros(Nb, dtype=torch.int32, device=dev)
         rescale = bool(getattr(self._program, "rescale_optimization_variables", False))
+        # With tol_convergence <= 0 no problem stops early, so the first-order
+        # check of iteration k (which feeds only the statistics, the selects
+        # and the KKT state) runs on a side stream, overlapping the next ADMM
+        # call; its results are applied right after that call is launched, in
+        # the order the sequential loop applies them.
+        cur = torch.cuda.current_stream(dev) if dev.type == "cuda" else None
+        side = self._side_stream(dev) if (cur is not None and tol <= 0) else None
+        pending = None
+
+        def apply(p):
+            nonlocal g_sel, l_sel, u_sel, conv, active
+            k_, cv_, ev_, iv_, g_, l_, u_, act_, on_side, _keep = p  # _keep: inputs of the side stream
+            if on_side:
+                cur.wait_stream(side)
+                for t_ in (cv_, ev_, iv_, g_):
+                    t_.record_stream(cur)
+            if k_ == 0:
+                g_sel, l_sel, u_sel, conv = g_, l_, u_, cv_
+            else:
+                sel = lambda new, old: new if new is old else torch.where(
+                    act_.view(-1, *([1] * (new.dim() - 1))), new, old)
+                g_sel, l_sel, u_sel, conv = sel(g_, g_sel), sel(l_, l_sel), sel(u_, u_sel), sel(cv_, conv)
+            eqv[:, k_], inv[:, k_], cerr[:, k_] = ev_, iv_, cv_
+            active = act_ & (conv > tol)
+
         for k in range(max_iter):
             if k > 0 and tol > 0 and not bool(active.any()):
                 break
             st_new, iters, status = ops.admm_solve(qp, st, cfg, slack_weight=sw, workspace=self._workspace)
+            if pending is not None:
+                apply(pending)
+                pending = None
             xb = st_new.x_blocks  # QP (scaled) coordinates
             if rescale:
                 s_new, c_new = self._program.unscale_states_controls(xb[..., :nx], xb[..., nx:], params)
@@ -409,10 +444,31 @@ class TurboMPCSolver:
             step = _inf(z_new - z_cur)
             if sl_new.shape[-1] > 0:
                 step = step + _inf(sl_new - slacks)
+            # Masked update (problems already converged keep their iterate).
+            if k == 0:  # every problem is active: nothing to select
+                kstatus = status.clone()
+                z_cur, slacks, st = z_new, sl_new, st_new
+                admm_iters[:, k] = iters
+            else:
+                sel = lambda new, old: new if new is old else torch.where(
+                    active.view(-1, *([1] * (new.dim() - 1))), new, old)
+                kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
+                z_cur, slacks = sel(z_new, z_cur), sel(sl_new, slacks)
+                st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
+                admm_iters[:, k] = torch.where(active, iters, admm_iters[:, k])
+            it_count = it_count + active.to(torch.int64)
+            on_side = False
             if crit == "first_order":
                 if k + 1 < max_iter:
                     qp_next = self._build_qp_data(z_new[..., :nx], z_new[..., nx:], params, prev=qp)
-                    cv, ev, iv, g = self._first_order_error(qp_next, xb[..., :nx], xb[..., nx:], sl_new, st_new)
+                    if side is not None:
+                        side.wait_stream(cur)
+                        with torch.cuda.stream(side):
+                            cv, ev, iv, g = self._first_order_error(qp_next, xb[..., :nx], xb[..., nx:], sl_new,
+                                                                    st_new)
+                        on_side = True
+                    else:
+                        cv, ev, iv, g = self._first_order_error(qp_next, xb[..., :nx], xb[..., nx:], sl_new, st_new)
                 else:
                     qp_next = qp
                     cv = step if k == 0 else conv
@@ -422,32 +478,21 @@ class TurboMPCSolver:
                 qp_next = self._build_qp_data(z_new[..., :nx], z_new[..., nx:], params, prev=qp) \
                     if k + 1 < max_iter else qp
                 cv, ev, iv, g = step, torch.zeros_like(step), torch.zeros_like(step), self._ineq_rows(qp_next, xb)
-            l_new, u_new = qp_next.ineq.l, qp_next.ineq.u
-            if k == 0:  # every problem is active: nothing to select
-                kstatus = status.clone()
-                z_cur, slacks, st = z_new, sl_new, st_new
-                g_sel, l_sel, u_sel = g, l_new, u_new
-                admm_iters[:, k] = iters
-                conv = cv
+            # the side stream's inputs stay referenced until the main stream has
+            # waited for it (their memory is not handed out again before)
+            p = (k, cv, ev, iv, g, qp_next.ineq.l, qp_next.ineq.u, active, on_side, (xb, sl_new, st_new, qp_next))
+            if on_side:
+                pending = p
             else:
-                # Masked update (problems already converged keep their iterate).
-                sel = lambda new, old: new if new is old else torch.where(
-                    active.view(-1, *([1] * (new.dim() - 1))), new, old)
-                kstatus = kstatus | torch.where(active, status, torch.zeros_like(status))
-                z_cur, slacks = sel(z_new, z_cur), sel(sl_new, slacks)
-                st = ADMMState(*(sel(n_, o_) for n_, o_ in zip(st_new, st)))
-                g_sel, l_sel, u_sel = sel(g, g_sel), sel(l_new, l_sel), sel(u_new, u_sel)
-                admm_iters[:, k] = torch.where(active, iters, admm_iters[:, k])
-                conv = sel(cv, conv)
-            eqv[:, k], inv[:, k], cerr[:, k] = ev, iv, cv
-            it_count = it_count + active.to(torch.int64)
+                apply(p)
             if k + 1 < max_iter:
                 # Every problem moves on to the QP at its new iterate: a problem
                 # that has converged still runs (its results are discarded by
-                # the selects above), so its QP needs no select and the loop
-                # never waits on the device to decide.
+                # the selects), so its QP needs no select and the loop never
+                # waits on the device to decide.
                 qp = qp_next
-            active = active & (conv > tol)
+        if pending is not None:
+            apply(pending)
         states, controls = z_cur[..., :nx].contiguous(), z_cur[..., nx:].contiguous()
         kkt = None if g_sel is None else self._build_kkt_state(states, controls, st, g_sel, l_sel, u_sel)
         return TurboMPCSolution(states=states, controls=controls, slack=st.xi_g, status=self.STATUS_SUCCESS,
