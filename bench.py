@@ -68,15 +68,17 @@ def direct_bytes_per_problem_iteration(T, n, nx, m, n0, w, ap_identity=False, g_
     return w * (2 * ef + rows + vecs + state)
 
 
-def direct_launches_per_solve(n0, m, check_every=0):
+def direct_launches_per_solve(n0, m, check_every=0, compact=True):
     """Kernel launches of one direct-path ADMM call (fixed counts): scalars in,
-    the interleaving of each non-empty QP / state array, the structure checks
-    of A+ and G, assembly, factor, the zero-row check of W, first gamma, the
-    iteration kernel, the conversions back, scalars out."""
+    the structure checks of A+ and G (G: its columns, then the rows), the
+    interleaving of each non-empty QP / state array (A+ and G launch and exit
+    for structured groups), assembly, factor, the zero-row check of W, first
+    gamma, the iteration kernel (compact and full variants: two launches in
+    fp32), the conversions back, scalars out."""
     conv_in = 6 + (3 if n0 else 0) + (6 if m else 0)  # q A- A+ c x y_fdyn; A0 c0 y_f0; G l u z_g y_g xi_g
     conv_out = 2 + (1 if n0 else 0) + (3 if m else 0)
-    checks = 1 + (1 if m else 0)
-    return 1 + conv_in + checks + 4 + 1 + conv_out + 1
+    checks = 1 + (2 if m else 0)
+    return 1 + checks + conv_in + 4 + (2 if compact else 1) + conv_out + 1
 
 
 def algorithmic_bytes_per_problem_launch(T, n, nx, m, n0, w, admm=ADMM, pcg=PCG):
@@ -734,6 +736,7 @@ def main():
     orig = ops.admm_solve
     orig_lin = ops.linearize_dynamics
     orig_kkt = ops.first_order_error
+    orig_ineq = ops.ineq_rows
 
     def timed_admm(*a, **k):
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
@@ -751,6 +754,10 @@ def main():
         n_lin[0] += 1
         return orig_kkt(*a, **k)
 
+    def counted_ineq(*a, **k):
+        n_lin[0] += 1
+        return orig_ineq(*a, **k)
+
     def step():
         return solver.solve(guess, params)
 
@@ -760,6 +767,7 @@ def main():
     ops.admm_solve = timed_admm
     ops.linearize_dynamics = counted_lin
     ops.first_order_error = counted_kkt
+    ops.ineq_rows = counted_ineq
     import turbompc_b200.solver as solver_mod
 
     solver_mod.ops.admm_solve = timed_admm
@@ -780,6 +788,7 @@ def main():
     ops.admm_solve = orig
     ops.linearize_dynamics = orig_lin
     ops.first_order_error = orig_kkt
+    ops.ineq_rows = orig_ineq
     solver_mod.ops.admm_solve = orig
     ms = s0.elapsed_time(s1) / args.steps
     kern_ms = [a.elapsed_time(b) for a, b in launch_ms]
